@@ -1,0 +1,91 @@
+// forge_internal.h — shared host-side declarations of the forge_b200 library.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define FORGE_API __attribute__((visibility("default")))
+
+enum { FORGE_PERM_NONE = 0, FORGE_PERM_QKV = 1, FORGE_PERM_GATEUP = 2 };
+
+// Records a one-line error (returned by forge_b200_last_error and printed once
+// to stderr, the reference's "one stderr line, return -1" contract) and
+// returns `code`.
+int forge_fail(int code, const char* fmt, ...);
+// Checks cudaGetLastError after a launch; 0 or -1.
+int forge_check_launch(const char* what);
+// Number of SMs of the current device (cached per device).
+int forge_sm_count();
+
+// ------------------------------------------------------------ GEMV launch
+enum { FORGE_W_BF16 = 0, FORGE_W_Q4 = 1 };
+enum { FORGE_PRO_PLAIN = 0, FORGE_PRO_RMSNORM = 1 };
+enum {
+    FORGE_EPI_STORE = 0,  // y[b][row] = W x
+    FORGE_EPI_RESID = 1,  // y[b][row] += W x   (residual stream, in place)
+    FORGE_EPI_QKV = 2,    // RoPE + KV append + q out
+    FORGE_EPI_SWIGLU = 3, // s[b][f] = silu(gate) * up
+    FORGE_EPI_LOGITS = 4, // logits + running argmax key
+};
+
+struct ForgeGemvArgs {
+    const void* w;         // packed tiles
+    const void* s;         // q4 scale tiles (NULL for bf16)
+    int32_t N, K;          // physical rows / input columns
+    int32_t wkind;         // FORGE_W_*
+    int32_t batch;         // sequences in this call
+    int32_t b0;            // global index of the first sequence (cache/pos indexing)
+    int32_t split;         // 1: hi/lo bf16 activations (exact fp32 inputs), 0: bf16
+    const float* x;        // [batch][x_stride] fp32 input
+    int32_t x_stride;
+    int32_t pro;           // FORGE_PRO_*
+    const float* gain;     // RMSNorm gain [K]
+    float eps;
+    int32_t epi;           // FORGE_EPI_*
+    float* y;              // STORE/RESID/LOGITS output [batch][y_stride]
+    int32_t y_stride;
+    // QKV epilogue
+    float* q_out;          // [batch][H*hd]
+    uint16_t* kc;          // layer base of the K cache: [Btot][Hkv][lmax][hd] bf16
+    uint16_t* vc;
+    const int32_t* pos;    // [Btot] position of the token being decoded
+    int32_t H, Hkv, hd, lmax;
+    const float* rope_cos; // [lmax][hd/2]
+    const float* rope_sin;
+    // SwiGLU epilogue
+    float* s_out;          // [batch][F]
+    int32_t F;
+    // LOGITS epilogue
+    unsigned long long* argmax_key;  // [Btot]
+    int32_t nvalid;        // rows >= nvalid (zero padding) never win the argmax
+    uint32_t* err;         // device error word
+};
+
+// Launches the decode GEMV (one or more launches when the batch exceeds one
+// mma column block). pdl: launch with programmatic stream serialization.
+int forge_gemv_launch(const ForgeGemvArgs& a, cudaStream_t stream, bool pdl);
+int forge_gemv_configure();
+
+// ------------------------------------------------------ flash-decode launch
+struct ForgeAttnArgs {
+    const float* q;        // [B][H*hd] fp32 (RoPE applied)
+    const uint16_t* kc;    // layer base [B][Hkv][lmax][hd] bf16
+    const uint16_t* vc;
+    const int32_t* pos;    // [B]; attends to positions 0..pos[b]
+    int32_t B, H, Hkv, hd, lmax;
+    int32_t nsplit;        // KV splits per (b, kv head)
+    float* partial;        // [B][H][nsplit][hd + 2] scratch
+    uint32_t* counters;    // [B][Hkv] zero-initialised merge counters
+    float* out;            // [B][H*hd] fp32 context
+    uint32_t* err;
+};
+int forge_attn_launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl);
+int forge_attn_configure();
+int forge_attn_pick_splits(int B, int Hkv, int lmax);
+int64_t forge_attn_partial_floats(int B, int H, int hd, int nsplit);
+
+// ------------------------------------------------------------- misc kernels
+int forge_embed_launch(const uint16_t* emb, int d, int vocab, const int32_t* tok, int B, float* x,
+                       uint32_t* err, cudaStream_t stream, bool pdl);
+int forge_argmax_finalize_launch(unsigned long long* keys, int B, int32_t* tok_out,
+                                 int32_t* hist, int32_t* step_counter, int32_t* pos, int hist_cap,
+                                 cudaStream_t stream, bool pdl);

@@ -1,0 +1,649 @@
+// model.cu — the decode engine: one ForgeB200 handle per GPU owns the packed
+// weights, the bf16 KV cache, the step's activation buffers and one CUDA graph
+// per batch size. A decode step is
+//     embed -> L x [QKV(+RMSNorm,RoPE,KV append) -> flash-decode ->
+//                   O(+residual) -> gate/up(+RMSNorm,SwiGLU) -> down(+residual)]
+//     -> LM head(+final RMSNorm, logits, argmax) -> finalize(next token)
+// i.e. decoder_lib.hexa:93-208 + decoder_block_lib.hexa:217-508 +
+// nn_decoder_predict (:485-500) for one new position per sequence, with the
+// KV cache replacing the reference's full recompute. All launches after the
+// first use programmatic dependent launch, so each GEMV's weight stream
+// starts while the previous kernel drains; the whole step is captured once
+// per batch size and replayed.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <vector>
+#include "common.cuh"
+#include "layout.cuh"
+#include "forge_internal.h"
+#include "../../include/forge_b200.h"
+
+namespace {
+struct LayerDev {
+    void *qkv_w = nullptr, *qkv_s = nullptr;
+    void *o_w = nullptr, *o_s = nullptr;
+    void *gu_w = nullptr, *gu_s = nullptr;
+    void *dn_w = nullptr, *dn_s = nullptr;
+    float *g1 = nullptr, *g2 = nullptr;
+};
+
+__global__ void k_embed(const uint16_t* __restrict__ emb, int d, int vocab, const int32_t* __restrict__ tok,
+                        float* __restrict__ x, uint32_t* err) {
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x;
+    int t = tok[b];
+    if (t < 0 || t >= vocab) {
+        if (threadIdx.x == 0) atomicOr(err, FORGE_DEVERR_BAD_INDEX);
+        t = 0;
+    }
+    const uint16_t* row = emb + (size_t)t * d;
+    for (int k = threadIdx.x * 2; k < d; k += blockDim.x * 2) {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(row + k);
+        x[(size_t)b * d + k] = bf16_lo_f32(v);
+        x[(size_t)b * d + k + 1] = bf16_hi_f32(v);
+    }
+}
+
+__global__ void k_finalize(unsigned long long* keys, int B, int32_t* tok, int32_t* hist, int32_t* step,
+                           int32_t* pos, int hist_cap, int hist_stride) {
+    pdl_trigger();
+    pdl_wait();
+    const int b = threadIdx.x;
+    const int s = *step;
+    if (b < B) {
+        const unsigned long long k = keys[b];
+        const int32_t t = k ? (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
+        tok[b] = t;
+        if (s < hist_cap) hist[(size_t)s * hist_stride + b] = t;
+        keys[b] = 0ull;
+        pos[b] += 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *step = s + 1;
+}
+
+__global__ void k_set_i32(int32_t* p, int n, int32_t v) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = v;
+}
+
+int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+}  // namespace
+
+struct ForgeB200 {
+    ForgeModelDesc desc{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int L = 0, d = 0, H = 0, Hkv = 0, hd = 0, F = 0, V = 0, Vpad = 0, qd = 0, kvd = 0, nqkv = 0;
+    int Bmax = 0, lmax = 0;
+    bool q4 = false;
+    std::vector<LayerDev> layers;
+    uint16_t* emb = nullptr;
+    void* head_w = nullptr;
+    float* gF = nullptr;
+    uint16_t *kc = nullptr, *vc = nullptr;
+    size_t kv_layer = 0;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    int32_t *tok = nullptr, *pos = nullptr, *hist = nullptr, *step = nullptr;
+    int hist_cap = 0;
+    float *x = nullptr, *q = nullptr, *ctx = nullptr, *s = nullptr, *logits = nullptr;
+    unsigned long long* amax = nullptr;
+    float* partial = nullptr;
+    uint32_t* counters = nullptr;
+    int nsplit = 1;
+    uint32_t* err = nullptr;
+    uint16_t *stA = nullptr, *stB = nullptr;
+    uint8_t* codes = nullptr;
+    uint16_t* scales = nullptr;
+    int32_t* h_tok = nullptr;  // pinned staging [Bmax]
+    std::map<int, cudaGraphExec_t> graphs;
+    std::vector<void*> allocs;
+    bool weights_ready = false;
+
+    void* alloc(size_t bytes) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) return nullptr;
+        allocs.push_back(p);
+        return p;
+    }
+    bool split_for(int B) const {
+        if (desc.act_mode == 1) return true;
+        if (desc.act_mode == 2) return false;
+        return B <= 4;
+    }
+};
+
+namespace {
+size_t tile_bytes(bool q4, int64_t N, int64_t K) { return q4 ? (size_t)(N * K / 2) : (size_t)(N * K * 2); }
+size_t scale_bytes(bool q4, int64_t N, int64_t K) {
+    return q4 ? (size_t)forge_q4_scale_tile_bytes(N, K, 128) : 0;
+}
+
+// Packs the physical-order bf16 matrix in h->stB ([N][K]) into (w, s).
+int pack_matrix(ForgeB200* h, int64_t N, int64_t K, void* w, void* s, bool q4) {
+    if (q4) {
+        int rc = forge_q4_quantize_bf16(h->stB, N, K, 128, h->codes, h->scales, h->stream);
+        if (!rc) rc = forge_q4_pack_tiles(h->codes, h->scales, N, K, 128, w, s, h->stream);
+        return rc;
+    }
+    return forge_bf16_pack_tiles(h->stB, N, K, w, h->stream);
+}
+
+int alloc_layer(ForgeB200* h, LayerDev& Ld) {
+    const bool q4 = h->q4;
+    Ld.qkv_w = h->alloc(tile_bytes(q4, h->nqkv, h->d));
+    Ld.o_w = h->alloc(tile_bytes(q4, h->d, h->qd));
+    Ld.gu_w = h->alloc(tile_bytes(q4, 2 * h->F, h->d));
+    Ld.dn_w = h->alloc(tile_bytes(q4, h->d, h->F));
+    if (q4) {
+        Ld.qkv_s = h->alloc(scale_bytes(q4, h->nqkv, h->d));
+        Ld.o_s = h->alloc(scale_bytes(q4, h->d, h->qd));
+        Ld.gu_s = h->alloc(scale_bytes(q4, 2 * h->F, h->d));
+        Ld.dn_s = h->alloc(scale_bytes(q4, h->d, h->F));
+    }
+    Ld.g1 = (float*)h->alloc(sizeof(float) * h->d);
+    Ld.g2 = (float*)h->alloc(sizeof(float) * h->d);
+    if (!Ld.qkv_w || !Ld.o_w || !Ld.gu_w || !Ld.dn_w || !Ld.g1 || !Ld.g2 ||
+        (q4 && (!Ld.qkv_s || !Ld.o_s || !Ld.gu_s || !Ld.dn_s)))
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200: out of device memory for layer weights");
+    return 0;
+}
+
+// Source of one logical matrix: either host bf16 or a synthetic stream.
+struct Src {
+    const uint16_t* host;
+    uint64_t seed, offset;
+    float std;
+};
+int fill_rows(ForgeB200* h, uint16_t* dst, int64_t rows, int64_t K, const Src& s) {
+    if (s.host) {
+        cudaError_t e = cudaMemcpyAsync(dst, s.host, (size_t)rows * K * 2, cudaMemcpyHostToDevice, h->stream);
+        return e == cudaSuccess ? 0 : forge_fail(-1, "forge_b200: H2D weights: %s", cudaGetErrorString(e));
+    }
+    return forge_fill_normal_bf16(dst, rows * K, s.seed, s.offset, s.std, h->stream);
+}
+
+int load_layer_impl(ForgeB200* h, int l, const Src src[7], const float* g1, const float* g2, bool gains_one) {
+    LayerDev& Ld = h->layers[l];
+    const int d = h->d, qd = h->qd, kvd = h->kvd, F = h->F;
+    int rc = 0;
+    // QKV: [Wq; Wk; Wv] logical rows -> RoPE-pair permutation -> pack
+    rc |= fill_rows(h, h->stA, qd, d, src[0]);
+    rc |= fill_rows(h, h->stA + (size_t)qd * d, kvd, d, src[1]);
+    rc |= fill_rows(h, h->stA + (size_t)(qd + kvd) * d, kvd, d, src[2]);
+    if (rc) return -1;
+    if (forge_permute_rows_bf16(h->stA, h->stB, h->nqkv, d, FORGE_PERM_QKV, h->hd, h->stream)) return -1;
+    if (pack_matrix(h, h->nqkv, d, Ld.qkv_w, Ld.qkv_s, h->q4)) return -1;
+    // O
+    if (fill_rows(h, h->stB, d, qd, src[3]) || pack_matrix(h, d, qd, Ld.o_w, Ld.o_s, h->q4)) return -1;
+    // gate/up interleave
+    if (fill_rows(h, h->stA, F, d, src[4]) || fill_rows(h, h->stA + (size_t)F * d, F, d, src[5])) return -1;
+    if (forge_permute_rows_bf16(h->stA, h->stB, 2 * F, d, FORGE_PERM_GATEUP, F, h->stream)) return -1;
+    if (pack_matrix(h, 2 * F, d, Ld.gu_w, Ld.gu_s, h->q4)) return -1;
+    // down
+    if (fill_rows(h, h->stB, d, F, src[6]) || pack_matrix(h, d, F, Ld.dn_w, Ld.dn_s, h->q4)) return -1;
+    // gains
+    if (gains_one) {
+        if (forge_fill_f32(Ld.g1, d, 1.0f, h->stream) || forge_fill_f32(Ld.g2, d, 1.0f, h->stream)) return -1;
+    } else {
+        if (cudaMemcpyAsync(Ld.g1, g1, sizeof(float) * d, cudaMemcpyHostToDevice, h->stream) != cudaSuccess ||
+            cudaMemcpyAsync(Ld.g2, g2, sizeof(float) * d, cudaMemcpyHostToDevice, h->stream) != cudaSuccess)
+            return forge_fail(-1, "forge_b200: H2D gains failed");
+    }
+    // staging buffers are reused by the next matrix: keep uploads ordered
+    return cudaStreamSynchronize(h->stream) == cudaSuccess ? 0 : forge_fail(-1, "forge_b200: weight prep failed");
+}
+
+int load_embed_impl(ForgeB200* h, const Src& emb, const Src* head, const float* gF, bool gains_one) {
+    const int64_t V = h->V, Vp = h->Vpad, d = h->d;
+    if (fill_rows(h, h->emb, V, d, emb)) return -1;
+    // head tiles from a zero-padded [Vpad][d] copy
+    if (cudaMemsetAsync(h->stB, 0, (size_t)Vp * d * 2, h->stream) != cudaSuccess) return forge_fail(-1, "memset");
+    if (head) {
+        if (fill_rows(h, h->stB, V, d, *head)) return -1;
+    } else if (cudaMemcpyAsync(h->stB, h->emb, (size_t)V * d * 2, cudaMemcpyDeviceToDevice, h->stream) != cudaSuccess) {
+        return forge_fail(-1, "forge_b200: head copy failed");
+    }
+    if (forge_bf16_pack_tiles(h->stB, Vp, d, h->head_w, h->stream)) return -1;
+    if (gains_one) {
+        if (forge_fill_f32(h->gF, d, 1.0f, h->stream)) return -1;
+    } else if (cudaMemcpyAsync(h->gF, gF, sizeof(float) * d, cudaMemcpyHostToDevice, h->stream) != cudaSuccess) {
+        return forge_fail(-1, "forge_b200: H2D final gain failed");
+    }
+    return cudaStreamSynchronize(h->stream) == cudaSuccess ? 0 : forge_fail(-1, "forge_b200: embedding prep failed");
+}
+
+int enqueue_step(ForgeB200* h, int B) {
+    cudaStream_t st = h->stream;
+    const bool split = h->split_for(B);
+    if (forge_embed_launch(h->emb, h->d, h->V, h->tok, B, h->x, h->err, st, false)) return -1;
+    for (int l = 0; l < h->L; ++l) {
+        const LayerDev& Ld = h->layers[l];
+        uint16_t* kc = h->kc + (size_t)l * h->kv_layer;
+        uint16_t* vc = h->vc + (size_t)l * h->kv_layer;
+        ForgeGemvArgs a{};
+        a.wkind = h->q4 ? FORGE_W_Q4 : FORGE_W_BF16;
+        a.batch = B;
+        a.split = split;
+        a.err = h->err;
+        // QKV + RoPE + KV append
+        ForgeGemvArgs g = a;
+        g.w = Ld.qkv_w; g.s = Ld.qkv_s; g.N = h->nqkv; g.K = h->d;
+        g.x = h->x; g.x_stride = h->d; g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g1; g.eps = h->desc.rms_eps;
+        g.epi = FORGE_EPI_QKV; g.q_out = h->q; g.kc = kc; g.vc = vc; g.pos = h->pos;
+        g.H = h->H; g.Hkv = h->Hkv; g.hd = h->hd; g.lmax = h->lmax;
+        g.rope_cos = h->rope_cos; g.rope_sin = h->rope_sin;
+        if (forge_gemv_launch(g, st, true)) return -1;
+        // attention
+        ForgeAttnArgs at{};
+        at.q = h->q; at.kc = kc; at.vc = vc; at.pos = h->pos; at.B = B; at.H = h->H; at.Hkv = h->Hkv;
+        at.hd = h->hd; at.lmax = h->lmax; at.nsplit = forge_attn_pick_splits(B, h->Hkv, h->lmax);
+        at.partial = h->partial; at.counters = h->counters; at.out = h->ctx; at.err = h->err;
+        if (forge_attn_launch(at, st, true)) return -1;
+        // O projection + residual
+        g = a;
+        g.w = Ld.o_w; g.s = Ld.o_s; g.N = h->d; g.K = h->qd; g.x = h->ctx; g.x_stride = h->qd;
+        g.pro = FORGE_PRO_PLAIN; g.epi = FORGE_EPI_RESID; g.y = h->x; g.y_stride = h->d;
+        if (forge_gemv_launch(g, st, true)) return -1;
+        // gate/up + SwiGLU
+        g = a;
+        g.w = Ld.gu_w; g.s = Ld.gu_s; g.N = 2 * h->F; g.K = h->d; g.x = h->x; g.x_stride = h->d;
+        g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g2; g.eps = h->desc.rms_eps;
+        g.epi = FORGE_EPI_SWIGLU; g.s_out = h->s; g.F = h->F;
+        if (forge_gemv_launch(g, st, true)) return -1;
+        // down + residual
+        g = a;
+        g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = h->s; g.x_stride = h->F;
+        g.pro = FORGE_PRO_PLAIN; g.epi = FORGE_EPI_RESID; g.y = h->x; g.y_stride = h->d;
+        if (forge_gemv_launch(g, st, true)) return -1;
+    }
+    ForgeGemvArgs g{};
+    g.wkind = FORGE_W_BF16; g.batch = B; g.split = split; g.err = h->err;
+    g.w = h->head_w; g.N = h->Vpad; g.K = h->d; g.x = h->x; g.x_stride = h->d;
+    g.pro = FORGE_PRO_RMSNORM; g.gain = h->gF; g.eps = h->desc.rms_eps;
+    g.epi = FORGE_EPI_LOGITS; g.y = h->logits; g.y_stride = h->Vpad; g.argmax_key = h->amax; g.nvalid = h->V;
+    if (forge_gemv_launch(g, st, true)) return -1;
+    return forge_argmax_finalize_launch(h->amax, B, h->tok, h->hist, h->step, h->pos, h->hist_cap, st, true);
+}
+
+cudaGraphExec_t graph_for(ForgeB200* h, int B) {
+    auto it = h->graphs.find(B);
+    if (it != h->graphs.end()) return it->second;
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        forge_fail(-1, "forge_b200: begin capture failed");
+        return nullptr;
+    }
+    int rc = enqueue_step(h, B);
+    cudaError_t e = cudaStreamEndCapture(h->stream, &graph);
+    if (rc || e != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        forge_fail(-1, "forge_b200: step capture failed (%s)", cudaGetErrorString(e));
+        return nullptr;
+    }
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) {
+        forge_fail(-1, "forge_b200: graph instantiate: %s", cudaGetErrorString(e));
+        return nullptr;
+    }
+    h->graphs[B] = exec;
+    return exec;
+}
+
+int check_ready(ForgeB200* h, int B) {
+    if (!h) return forge_fail(FORGE_INVALID_ARGS, "forge_b200: null handle");
+    if (!h->weights_ready) return forge_fail(FORGE_INVALID_ARGS, "forge_b200: weights not loaded");
+    if (B <= 0 || B > h->Bmax) return forge_fail(FORGE_INVALID_ARGS, "forge_b200: batch %d outside 1..%d", B, h->Bmax);
+    return cudaSetDevice(h->device) == cudaSuccess ? 0 : forge_fail(-1, "forge_b200: cudaSetDevice failed");
+}
+
+int read_err(ForgeB200* h) {
+    uint32_t e = 0;
+    if (cudaMemcpy(&e, h->err, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return forge_fail(-1, "forge_b200: device error: %s", cudaGetErrorString(cudaGetLastError()));
+    if (e) {
+        cudaMemset(h->err, 0, 4);
+        return forge_fail(-1, "forge_b200: kernel raised error word 0x%x (1 wait timeout, 2 flag timeout, 4 bad index)", e);
+    }
+    return 0;
+}
+}  // namespace
+
+int forge_embed_launch(const uint16_t* emb, int d, int vocab, const int32_t* tok, int B, float* x,
+                       uint32_t* err, cudaStream_t stream, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(B);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_embed, emb, d, vocab, tok, x, err);
+    return e == cudaSuccess ? 0 : forge_fail(-1, "embed launch: %s", cudaGetErrorString(e));
+}
+
+int forge_argmax_finalize_launch(unsigned long long* keys, int B, int32_t* tok_out, int32_t* hist,
+                                 int32_t* step_counter, int32_t* pos, int hist_cap, cudaStream_t stream,
+                                 bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3((B + 31) / 32 * 32);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    // hist rows are [hist_cap][B_max]; the stride is passed through hist_cap's owner
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_finalize, keys, B, tok_out, hist, step_counter, pos, hist_cap, B);
+    return e == cudaSuccess ? 0 : forge_fail(-1, "finalize launch: %s", cudaGetErrorString(e));
+}
+
+extern "C" {
+FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB200** out) {
+    if (!desc || !out) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: null argument");
+    *out = nullptr;
+    const ForgeModelDesc& m = *desc;
+    if (m.n_layer <= 0 || m.d_model <= 0 || m.n_head <= 0 || m.n_kv_head <= 0 || m.head_dim <= 0 ||
+        m.ffn <= 0 || m.vocab <= 0 || m.max_batch <= 0 || m.max_ctx <= 0)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: non-positive dimension");
+    if (m.n_head % m.n_kv_head) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: n_head %% n_kv_head != 0");
+    if (m.head_dim != 64 && m.head_dim != 128)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: head_dim must be 64 or 128");
+    if (m.d_model % 64 || m.ffn % 16) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: d %% 64, ffn %% 16 required");
+    if (m.weight_kind == FORGE_WEIGHT_Q4_G128 && (m.d_model % 128 || m.ffn % 128 || (m.n_head * m.head_dim) % 128))
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: int4 group-128 needs every K %% 128 == 0");
+    if (m.weight_kind != FORGE_WEIGHT_BF16 && m.weight_kind != FORGE_WEIGHT_Q4_G128)
+        return forge_fail(FORGE_PRECISION_UNSUPPORTED, "forge_b200_create: unknown weight kind %d", m.weight_kind);
+    if (m.tp_size > 1) return forge_fail(FORGE_REGIME_UNSUPPORTED, "forge_b200_create: tensor parallel handles use forge_b200_create_tp");
+    if (m.max_batch > 1024) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: max_batch <= 1024");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: no CUDA device %d", device);
+    if (cudaSetDevice(device) != cudaSuccess) return forge_fail(-1, "forge_b200_create: cudaSetDevice failed");
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, device);
+    if (prop.major != 10) return forge_fail(FORGE_KERNEL_UNSUPPORTED, "forge_b200_create: needs an sm_100 device (got sm_%d%d)", prop.major, prop.minor);
+
+    if (forge_gemv_configure() || forge_attn_configure()) return -1;
+    forge_sm_count();
+    ForgeB200* h = new ForgeB200();
+    h->desc = m;
+    h->device = device;
+    h->L = m.n_layer; h->d = m.d_model; h->H = m.n_head; h->Hkv = m.n_kv_head; h->hd = m.head_dim;
+    h->F = m.ffn; h->V = m.vocab; h->Vpad = (int)round_up(m.vocab, 16);
+    h->qd = h->H * h->hd; h->kvd = h->Hkv * h->hd; h->nqkv = h->qd + 2 * h->kvd;
+    h->Bmax = m.max_batch; h->lmax = m.max_ctx; h->q4 = m.weight_kind == FORGE_WEIGHT_Q4_G128;
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete h;
+        return forge_fail(-1, "forge_b200_create: stream creation failed");
+    }
+    h->layers.resize(h->L);
+    int rc = 0;
+    for (auto& Ld : h->layers) rc |= alloc_layer(h, Ld);
+    const size_t d = h->d;
+    h->emb = (uint16_t*)h->alloc((size_t)h->V * d * 2);
+    h->head_w = h->alloc((size_t)h->Vpad * d * 2);
+    h->gF = (float*)h->alloc(sizeof(float) * d);
+    h->kv_layer = (size_t)h->Bmax * h->Hkv * h->lmax * h->hd;
+    h->kc = (uint16_t*)h->alloc(h->kv_layer * h->L * 2);
+    h->vc = (uint16_t*)h->alloc(h->kv_layer * h->L * 2);
+    h->rope_cos = (float*)h->alloc(sizeof(float) * (size_t)h->lmax * h->hd / 2);
+    h->rope_sin = (float*)h->alloc(sizeof(float) * (size_t)h->lmax * h->hd / 2);
+    h->tok = (int32_t*)h->alloc(4 * h->Bmax);
+    h->pos = (int32_t*)h->alloc(4 * h->Bmax);
+    h->hist_cap = h->lmax + 1;
+    h->hist = (int32_t*)h->alloc((size_t)4 * h->Bmax * h->hist_cap);
+    h->step = (int32_t*)h->alloc(16);
+    h->x = (float*)h->alloc(sizeof(float) * h->Bmax * d);
+    h->q = (float*)h->alloc(sizeof(float) * h->Bmax * h->qd);
+    h->ctx = (float*)h->alloc(sizeof(float) * h->Bmax * h->qd);
+    h->s = (float*)h->alloc(sizeof(float) * (size_t)h->Bmax * h->F);
+    h->logits = (float*)h->alloc(sizeof(float) * (size_t)h->Bmax * h->Vpad);
+    h->amax = (unsigned long long*)h->alloc(8 * h->Bmax);
+    int max_split = 1;
+    for (int B = 1; B <= h->Bmax; ++B) {
+        int ns = forge_attn_pick_splits(B, h->Hkv, h->lmax);
+        if (ns * B > max_split) max_split = ns * B;
+    }
+    h->partial = (float*)h->alloc(sizeof(float) * (size_t)max_split * h->H * (h->hd + 2));
+    h->counters = (uint32_t*)h->alloc(4 * (size_t)h->Bmax * h->Hkv);
+    h->err = (uint32_t*)h->alloc(16);
+    size_t st = std::max({(size_t)h->nqkv * d, (size_t)2 * h->F * d, (size_t)d * h->F, (size_t)d * h->qd,
+                          (size_t)h->Vpad * d});
+    h->stA = (uint16_t*)h->alloc(st * 2);
+    h->stB = (uint16_t*)h->alloc(st * 2);
+    h->codes = (uint8_t*)h->alloc(st / 2);
+    h->scales = (uint16_t*)h->alloc(st / 128 * 2 + 16);
+    if (rc || !h->emb || !h->head_w || !h->kc || !h->vc || !h->stA || !h->stB || !h->codes || !h->partial ||
+        !h->hist || !h->logits || !h->scales) {
+        forge_b200_destroy(h);
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: out of device memory");
+    }
+    if (cudaHostAlloc((void**)&h->h_tok, 4 * h->Bmax, cudaHostAllocDefault) != cudaSuccess) h->h_tok = nullptr;
+    // RoPE tables in double (nn_lib.hexa:509-531), stored fp32 [lmax][hd/2]
+    {
+        const int half = h->hd / 2;
+        std::vector<float> c((size_t)h->lmax * half), s((size_t)h->lmax * half);
+        const double lnb = std::log((double)m.rope_theta);
+        for (int p = 0; p < h->lmax; ++p)
+            for (int i = 0; i < half; ++i) {
+                const double ex = ((double)(2 * i) / (double)h->hd) * lnb;
+                const double invf = 1.0 / std::exp(ex);
+                const double ang = (double)p * invf;
+                c[(size_t)p * half + i] = (float)std::cos(ang);
+                s[(size_t)p * half + i] = (float)std::sin(ang);
+            }
+        cudaMemcpy(h->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(h->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
+    }
+    cudaMemset(h->counters, 0, 4 * (size_t)h->Bmax * h->Hkv);
+    cudaMemset(h->amax, 0, 8 * h->Bmax);
+    cudaMemset(h->err, 0, 16);
+    cudaMemset(h->step, 0, 16);
+    cudaMemset(h->pos, 0, 4 * h->Bmax);
+    cudaMemset(h->tok, 0, 4 * h->Bmax);
+    cudaMemset(h->kc, 0, h->kv_layer * h->L * 2);
+    cudaMemset(h->vc, 0, h->kv_layer * h->L * 2);
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        forge_b200_destroy(h);
+        return forge_fail(-1, "forge_b200_create: device initialisation failed");
+    }
+    *out = h;
+    return 0;
+}
+
+FORGE_API void forge_b200_destroy(ForgeB200* h) {
+    if (!h) return;
+    cudaSetDevice(h->device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    for (auto& kv : h->graphs) cudaGraphExecDestroy(kv.second);
+    for (void* p : h->allocs) cudaFree(p);
+    if (h->h_tok) cudaFreeHost(h->h_tok);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+}
+
+FORGE_API void* forge_b200_stream(ForgeB200* h) { return h ? (void*)h->stream : nullptr; }
+
+FORGE_API int forge_b200_load_layer(ForgeB200* h, int layer, const ForgeLayerWeights* w) {
+    if (!h || !w || layer < 0 || layer >= h->L) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_load_layer: bad args");
+    if (!w->wq || !w->wk || !w->wv || !w->wo || !w->wg || !w->wu || !w->wd || !w->g1 || !w->g2)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_load_layer: null weight pointer");
+    cudaSetDevice(h->device);
+    Src src[7];
+    const uint16_t* ptrs[7] = {w->wq, w->wk, w->wv, w->wo, w->wg, w->wu, w->wd};
+    for (int i = 0; i < 7; ++i) src[i] = Src{ptrs[i], 0, 0, 0.f};
+    return load_layer_impl(h, layer, src, w->g1, w->g2, false) ? FORGE_INVALID_ARGS : 0;
+}
+
+FORGE_API int forge_b200_load_embedding(ForgeB200* h, const uint16_t* emb, const float* gF, const uint16_t* head) {
+    if (!h || !emb || !gF) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_load_embedding: bad args");
+    if (!h->desc.tied_head && !head) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_load_embedding: untied model needs a head");
+    cudaSetDevice(h->device);
+    Src e{emb, 0, 0, 0.f}, hd{head, 0, 0, 0.f};
+    if (load_embed_impl(h, e, h->desc.tied_head ? nullptr : &hd, gF, false)) return FORGE_INVALID_ARGS;
+    h->weights_ready = true;
+    return 0;
+}
+
+FORGE_API int forge_b200_init_synthetic(ForgeB200* h, uint64_t seed, float std) {
+    if (!h) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_init_synthetic: null handle");
+    cudaSetDevice(h->device);
+    for (int l = 0; l < h->L; ++l) {
+        Src src[7];
+        for (int i = 0; i < 7; ++i) src[i] = Src{nullptr, seed, (uint64_t)(2 + 7 * l + i) << 40, std};
+        if (load_layer_impl(h, l, src, nullptr, nullptr, true)) return -1;
+    }
+    Src e{nullptr, seed, 0, std}, hd{nullptr, seed, (uint64_t)1 << 40, std};
+    if (load_embed_impl(h, e, h->desc.tied_head ? nullptr : &hd, nullptr, true)) return -1;
+    h->weights_ready = true;
+    return 0;
+}
+
+FORGE_API int forge_b200_reset(ForgeB200* h) {
+    if (!h) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_reset: null handle");
+    cudaSetDevice(h->device);
+    cudaMemsetAsync(h->pos, 0, 4 * h->Bmax, h->stream);
+    cudaMemsetAsync(h->step, 0, 16, h->stream);
+    cudaMemsetAsync(h->amax, 0, 8 * h->Bmax, h->stream);
+    return cudaStreamSynchronize(h->stream) == cudaSuccess ? 0 : forge_fail(-1, "forge_b200_reset failed");
+}
+
+FORGE_API int forge_b200_fill_kv_synthetic(ForgeB200* h, uint64_t seed, int ctx_len, float std) {
+    if (!h || ctx_len < 0 || ctx_len >= h->lmax) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_fill_kv_synthetic: bad args");
+    cudaSetDevice(h->device);
+    const int64_t n = (int64_t)h->kv_layer * h->L;
+    if (forge_fill_normal_bf16(h->kc, n, seed, (uint64_t)1000 << 40, std, h->stream) ||
+        forge_fill_normal_bf16(h->vc, n, seed, (uint64_t)1001 << 40, std, h->stream))
+        return -1;
+    k_set_i32<<<1, 256, 0, h->stream>>>(h->pos, h->Bmax, ctx_len);
+    return cudaStreamSynchronize(h->stream) == cudaSuccess ? 0 : forge_fail(-1, "forge_b200_fill_kv_synthetic failed");
+}
+
+FORGE_API int forge_b200_set_positions(ForgeB200* h, const int32_t* pos, int batch) {
+    if (!h || !pos || batch <= 0 || batch > h->Bmax) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_set_positions: bad args");
+    for (int b = 0; b < batch; ++b)
+        if (pos[b] < 0 || pos[b] >= h->lmax) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_set_positions: position out of range");
+    cudaSetDevice(h->device);
+    if (cudaMemcpy(h->pos, pos, 4 * batch, cudaMemcpyHostToDevice) != cudaSuccess) return forge_fail(-1, "H2D positions");
+    return 0;
+}
+
+FORGE_API int forge_b200_get_kv(ForgeB200* h, int layer, int seq, uint16_t* k_out, uint16_t* v_out) {
+    if (!h || layer < 0 || layer >= h->L || seq < 0 || seq >= h->Bmax || !k_out || !v_out)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_get_kv: bad args");
+    cudaSetDevice(h->device);
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess) return forge_fail(-1, "forge_b200_get_kv: sync failed");
+    const size_t per_seq = (size_t)h->Hkv * h->lmax * h->hd;
+    const size_t off = (size_t)layer * h->kv_layer + (size_t)seq * per_seq;
+    if (cudaMemcpy(k_out, h->kc + off, per_seq * 2, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(v_out, h->vc + off, per_seq * 2, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_get_kv: D2H failed");
+    return 0;
+}
+
+FORGE_API int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tokens, int32_t* next_tokens, float* logits) {
+    if (int rc = check_ready(h, batch)) return rc;
+    if (!tokens) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_decode_step: null tokens");
+    cudaGraphExec_t g = graph_for(h, batch);
+    if (!g) return -1;
+    int32_t* stage = h->h_tok;
+    if (!stage) return forge_fail(-1, "forge_b200_decode_step: no pinned staging buffer");
+    memcpy(stage, tokens, 4 * batch);
+    cudaMemcpyAsync(h->tok, stage, 4 * batch, cudaMemcpyHostToDevice, h->stream);
+    if (cudaGraphLaunch(g, h->stream) != cudaSuccess) return forge_fail(-1, "forge_b200_decode_step: graph launch failed");
+    if (next_tokens) cudaMemcpyAsync(stage, h->tok, 4 * batch, cudaMemcpyDeviceToHost, h->stream);
+    if (logits)
+        cudaMemcpy2DAsync(logits, sizeof(float) * h->V, h->logits, sizeof(float) * h->Vpad, sizeof(float) * h->V,
+                          batch, cudaMemcpyDeviceToHost, h->stream);
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_decode_step: %s", cudaGetErrorString(cudaGetLastError()));
+    if (next_tokens) memcpy(next_tokens, stage, 4 * batch);
+    return read_err(h);
+}
+
+FORGE_API int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps) {
+    if (int rc = check_ready(h, batch)) return rc;
+    cudaGraphExec_t g = graph_for(h, batch);
+    if (!g) return -1;
+    for (int i = 0; i < n_steps; ++i)
+        if (cudaGraphLaunch(g, h->stream) != cudaSuccess) return forge_fail(-1, "forge_b200_decode_device: graph launch failed");
+    return 0;
+}
+
+FORGE_API int forge_b200_generate(ForgeB200* h, int batch, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out) {
+    if (int rc = check_ready(h, batch)) return rc;
+    if (!prompt || !out || n_prompt <= 0 || n_gen <= 0 || n_prompt + n_gen - 1 > h->lmax)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_generate: bad prompt/generation length");
+    if (forge_b200_reset(h)) return -1;
+    cudaGraphExec_t g = graph_for(h, batch);
+    if (!g) return -1;
+    std::vector<int32_t> col(batch);
+    int32_t* pin = nullptr;
+    if (cudaHostAlloc((void**)&pin, 4 * (size_t)batch * n_prompt, cudaHostAllocDefault) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_generate: pinned alloc failed");
+    for (int p = 0; p < n_prompt; ++p)
+        for (int b = 0; b < batch; ++b) pin[(size_t)p * batch + b] = prompt[(size_t)b * n_prompt + p];
+    int rc = 0;
+    for (int p = 0; p < n_prompt && !rc; ++p) {
+        cudaMemcpyAsync(h->tok, pin + (size_t)p * batch, 4 * batch, cudaMemcpyHostToDevice, h->stream);
+        if (cudaGraphLaunch(g, h->stream) != cudaSuccess) rc = forge_fail(-1, "forge_b200_generate: launch failed");
+    }
+    for (int i = 1; i < n_gen && !rc; ++i)
+        if (cudaGraphLaunch(g, h->stream) != cudaSuccess) rc = forge_fail(-1, "forge_b200_generate: launch failed");
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess)
+        rc = forge_fail(-1, "forge_b200_generate: %s", cudaGetErrorString(cudaGetLastError()));
+    cudaFreeHost(pin);
+    if (rc) return rc;
+    if (int e = read_err(h)) return e;
+    std::vector<int32_t> hist((size_t)n_gen * batch);
+    if (cudaMemcpy2D(hist.data(), 4 * batch, h->hist + (size_t)(n_prompt - 1) * batch, 4 * batch, 4 * batch, n_gen,
+                     cudaMemcpyDeviceToHost) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_generate: D2H history failed");
+    for (int i = 0; i < n_gen; ++i)
+        for (int b = 0; b < batch; ++b) out[(size_t)b * n_gen + i] = hist[(size_t)i * batch + b];
+    return 0;
+}
+
+FORGE_API int forge_b200_sync(ForgeB200* h) {
+    if (!h) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_sync: null handle");
+    cudaSetDevice(h->device);
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_sync: %s", cudaGetErrorString(cudaGetLastError()));
+    return read_err(h);
+}
+
+FORGE_API int64_t forge_b200_step_bytes(ForgeB200* h, int batch, int ctx_len) {
+    if (!h) return -1;
+    const bool q4 = h->q4;
+    auto mat = [&](int64_t N, int64_t K) { return (int64_t)tile_bytes(q4, N, K) + (int64_t)scale_bytes(q4, N, K); };
+    int64_t per_layer = mat(h->nqkv, h->d) + mat(h->d, h->qd) + mat(2 * h->F, h->d) + mat(h->d, h->F) + 8 * h->d;
+    int64_t bytes = per_layer * h->L + (int64_t)h->Vpad * h->d * 2 + 4 * h->d + (int64_t)batch * h->d * 2;
+    // KV: read positions 0..ctx (ctx+1 rows incl. the new one), write one row, K and V, every layer
+    bytes += (int64_t)batch * h->L * 2 * h->Hkv * h->hd * 2 * ((int64_t)ctx_len + 1 + 1);
+    return bytes;
+}
+
+FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
+    if (!h || batch <= 0) return -1;
+    const bool split = h->split_for(batch);
+    auto launches = [&](int K) {
+        const int xs_row = (K + 8) * 2;
+        int max_cols = (227 * 1024 - (6 * (8192 + 256) + 96 + 8 * 16 * 8 * 4)) / xs_row;
+        if (max_cols > 8) max_cols = 8;
+        const int per = max_cols / (split ? 2 : 1);
+        return (batch + per - 1) / per;
+    };
+    int per_layer = launches(h->d) * 2 + launches(h->qd) + launches(h->F) + 1;
+    return 1 + h->L * per_layer + launches(h->d) + 1;
+}
+}  // extern "C"

@@ -1,0 +1,240 @@
+"""ctypes binding of libforge_b200.so — the host-side mirror of forge's decode
+interface for Python callers (tests, bench). The library itself is C/CUDA;
+this module only marshals arguments. It refuses to run without the built
+shared library: there is no Python or CPU fallback of any kernel.
+
+Reference interface mirrored: the flame decode loop over nn_decoder_fwd +
+nn_decoder_predict (stdlib/flame/decoder_lib.hexa:93-208, 485-500) becomes
+ForgeModel.generate/step; forge's per-op GEMV entry
+(_hx_cuda_farr_packed_gemv_offset_gpu, self/cuda/runtime_cuda_emit.hexa:1858)
+becomes gemv_w4a16/gemv_bf16 on device pointers.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libforge_b200.so")
+
+FORGE_WEIGHT_BF16 = 0
+FORGE_WEIGHT_Q4_G128 = 1
+FORGE_PERM_NONE, FORGE_PERM_QKV, FORGE_PERM_GATEUP = 0, 1, 2
+
+
+class ForgeModelDesc(C.Structure):
+    _fields_ = [
+        ("n_layer", C.c_int32), ("d_model", C.c_int32), ("n_head", C.c_int32),
+        ("n_kv_head", C.c_int32), ("head_dim", C.c_int32), ("ffn", C.c_int32),
+        ("vocab", C.c_int32), ("rms_eps", C.c_float), ("rope_theta", C.c_float),
+        ("weight_kind", C.c_int32), ("tied_head", C.c_int32), ("max_batch", C.c_int32),
+        ("max_ctx", C.c_int32), ("tp_rank", C.c_int32), ("tp_size", C.c_int32),
+        ("act_mode", C.c_int32), ("reserved", C.c_int32 * 5),
+    ]
+
+
+class ForgeLayerWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2")]
+
+
+class ForgeShapeInfo(C.Structure):
+    _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("batch", C.c_int64)]
+
+
+class ForgeArgs(C.Structure):
+    _fields_ = [("farr_ids", C.c_int64 * 8), ("count", C.c_int)]
+
+
+def build(force: bool = False) -> str:
+    """Compiles libforge_b200.so for sm_100a with nvcc (no GPU needed)."""
+    if force or not os.path.exists(LIB_PATH):
+        subprocess.run(["make", "-C", os.path.join(HERE, "csrc"), "-j8"], check=True,
+                       stdout=subprocess.DEVNULL)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it (make -C hexa-lang_b200/csrc)")
+        L = C.CDLL(LIB_PATH)
+        vp, i64, i32 = C.c_void_p, C.c_int64, C.c_int
+        sig = {
+            "forge_b200_create": (i32, [C.POINTER(ForgeModelDesc), i32, C.POINTER(vp)]),
+            "forge_b200_destroy": (None, [vp]),
+            "forge_b200_last_error": (C.c_char_p, []),
+            "forge_b200_stream": (vp, [vp]),
+            "forge_b200_load_layer": (i32, [vp, i32, C.POINTER(ForgeLayerWeights)]),
+            "forge_b200_load_embedding": (i32, [vp, vp, vp, vp]),
+            "forge_b200_init_synthetic": (i32, [vp, C.c_uint64, C.c_float]),
+            "forge_b200_reset": (i32, [vp]),
+            "forge_b200_fill_kv_synthetic": (i32, [vp, C.c_uint64, i32, C.c_float]),
+            "forge_b200_set_positions": (i32, [vp, vp, i32]),
+            "forge_b200_get_kv": (i32, [vp, i32, i32, vp, vp]),
+            "forge_b200_decode_step": (i32, [vp, i32, vp, vp, vp]),
+            "forge_b200_decode_device": (i32, [vp, i32, i32]),
+            "forge_b200_generate": (i32, [vp, i32, vp, i32, i32, vp]),
+            "forge_b200_sync": (i32, [vp]),
+            "forge_b200_step_bytes": (i64, [vp, i32, i32]),
+            "forge_b200_launches_per_step": (i32, [vp, i32]),
+            "forge_gemv_w4a16_g128": (i32, [vp, vp, i64, i64, vp, i32, vp, i32, vp]),
+            "forge_gemv_bf16": (i32, [vp, i64, i64, vp, i32, vp, i32, vp]),
+            "forge_flash_decode_workspace_bytes": (i64, [i32, i32, i32, i32, i32]),
+            "forge_flash_decode": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp]),
+            "forge_fill_normal_bf16": (i32, [vp, i64, C.c_uint64, C.c_uint64, C.c_float, vp]),
+            "forge_fill_f32": (i32, [vp, i64, C.c_float, vp]),
+            "forge_q4_quantize_bf16": (i32, [vp, i64, i64, i32, vp, vp, vp]),
+            "forge_permute_rows_bf16": (i32, [vp, vp, i64, i64, i32, i64, vp]),
+            "forge_bf16_pack_tiles": (i32, [vp, i64, i64, vp, vp]),
+            "forge_q4_pack_tiles": (i32, [vp, vp, i64, i64, i32, vp, vp, vp]),
+            "forge_q4_unpack_tiles": (i32, [vp, vp, i64, i64, i32, vp, vp, vp]),
+            "forge_q4_tile_bytes": (i64, [i64, i64]),
+            "forge_q4_scale_tile_bytes": (i64, [i64, i64, i32]),
+            "forge_ops_check": (i32, []),
+            "forge_api_version_v1": (C.c_uint32, []),
+            "forge_api_version_v2": (C.c_uint32, []),
+        }
+        for name, (res, args) in sig.items():
+            if hasattr(L, name):
+                f = getattr(L, name)
+                f.restype = res
+                f.argtypes = args
+        _lib = L
+    return _lib
+
+
+class ForgeError(RuntimeError):
+    pass
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = lib().forge_b200_last_error().decode(errors="replace")
+        raise ForgeError(f"{what} failed ({rc}): {msg}")
+
+
+def _ptr(a) -> int:
+    """Data pointer of a numpy array or a torch tensor."""
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+class ForgeModel:
+    """One decode engine on one GPU (forge_b200_create / ..._destroy)."""
+
+    def __init__(self, n_layer, d_model, n_head, n_kv_head, head_dim, ffn, vocab, *,
+                 weight_kind=FORGE_WEIGHT_BF16, tied_head=False, max_batch=1, max_ctx=256,
+                 rms_eps=1e-5, rope_theta=10000.0, act_mode=0, device=0):
+        self.desc = ForgeModelDesc(n_layer, d_model, n_head, n_kv_head, head_dim, ffn, vocab,
+                                   rms_eps, rope_theta, weight_kind, int(tied_head), max_batch,
+                                   max_ctx, 0, 1, act_mode)
+        h = C.c_void_p()
+        check(lib().forge_b200_create(C.byref(self.desc), device, C.byref(h)), "forge_b200_create")
+        self.h = h
+        self.vocab = vocab
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().forge_b200_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def init_synthetic(self, seed=1234, std=0.02):
+        check(lib().forge_b200_init_synthetic(self.h, seed, std), "init_synthetic")
+
+    def load_layer(self, layer, wq, wk, wv, wo, wg, wu, wd, g1, g2):
+        w = ForgeLayerWeights(*[_ptr(a) for a in (wq, wk, wv, wo, wg, wu, wd, g1, g2)])
+        check(lib().forge_b200_load_layer(self.h, layer, C.byref(w)), "load_layer")
+
+    def load_embedding(self, emb, gF, head=None):
+        check(lib().forge_b200_load_embedding(self.h, _ptr(emb), _ptr(gF), _ptr(head)), "load_embedding")
+
+    def reset(self):
+        check(lib().forge_b200_reset(self.h), "reset")
+
+    def fill_kv_synthetic(self, seed, ctx_len, std=0.5):
+        check(lib().forge_b200_fill_kv_synthetic(self.h, seed, ctx_len, std), "fill_kv_synthetic")
+
+    def set_positions(self, pos):
+        import numpy as np
+        p = np.ascontiguousarray(pos, dtype=np.int32)
+        check(lib().forge_b200_set_positions(self.h, _ptr(p), len(p)), "set_positions")
+
+    def get_kv(self, layer, seq, n_kv, max_ctx, hd):
+        import numpy as np
+        k = np.zeros((n_kv, max_ctx, hd), np.uint16)
+        v = np.zeros_like(k)
+        check(lib().forge_b200_get_kv(self.h, layer, seq, _ptr(k), _ptr(v)), "get_kv")
+        return k, v
+
+    def step(self, tokens, want_logits=False):
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt = np.zeros(len(t), np.int32)
+        lg = np.zeros((len(t), self.vocab), np.float32) if want_logits else None
+        check(lib().forge_b200_decode_step(self.h, len(t), _ptr(t), _ptr(nxt), _ptr(lg)), "decode_step")
+        return (nxt, lg) if want_logits else nxt
+
+    def decode_device(self, batch, n_steps):
+        check(lib().forge_b200_decode_device(self.h, batch, n_steps), "decode_device")
+
+    def sync(self):
+        check(lib().forge_b200_sync(self.h), "sync")
+
+    def generate(self, prompt, n_gen):
+        import numpy as np
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        if p.ndim == 1:
+            p = p[None, :]
+        out = np.zeros((p.shape[0], n_gen), np.int32)
+        check(lib().forge_b200_generate(self.h, p.shape[0], _ptr(p), p.shape[1], n_gen, _ptr(out)),
+              "generate")
+        return out
+
+    def step_bytes(self, batch, ctx):
+        return lib().forge_b200_step_bytes(self.h, batch, ctx)
+
+    def launches_per_step(self, batch):
+        return lib().forge_b200_launches_per_step(self.h, batch)
+
+    @property
+    def stream(self):
+        return lib().forge_b200_stream(self.h)
+
+
+# ---- per-op helpers on torch CUDA tensors -----------------------------------
+def q4_pack(w_bf16_dev, group=128, stream=None):
+    """Quantise a logical [N][K] bf16 device tensor (torch.int16/uint16 view)
+    and pack it: returns (codes, scales, tiles, scale_tiles) torch tensors."""
+    import torch
+    N, K = w_bf16_dev.shape
+    dev = w_bf16_dev.device
+    codes = torch.empty((N, K // 2), dtype=torch.uint8, device=dev)
+    scales = torch.empty((N, K // group), dtype=torch.int16, device=dev)
+    tiles = torch.empty(lib().forge_q4_tile_bytes(N, K), dtype=torch.uint8, device=dev)
+    stiles = torch.empty(lib().forge_q4_scale_tile_bytes(N, K, group), dtype=torch.uint8, device=dev)
+    s = stream or 0
+    check(lib().forge_q4_quantize_bf16(_ptr(w_bf16_dev), N, K, group, _ptr(codes), _ptr(scales), s), "q4_quantize")
+    check(lib().forge_q4_pack_tiles(_ptr(codes), _ptr(scales), N, K, group, _ptr(tiles), _ptr(stiles), s), "q4_pack")
+    return codes, scales, tiles, stiles
+
+
+def bf16_pack(w_bf16_dev, stream=None):
+    import torch
+    N, K = w_bf16_dev.shape
+    tiles = torch.empty(N * K * 2, dtype=torch.uint8, device=w_bf16_dev.device)
+    check(lib().forge_bf16_pack_tiles(_ptr(w_bf16_dev), N, K, _ptr(tiles), stream or 0), "bf16_pack")
+    return tiles

@@ -1,0 +1,147 @@
+/* forge_b200.h — B200 (sm_100a) decode engine behind forge's C ABI.
+ *
+ * This is the _v2 surface that sits beside the unchanged forge_tier_v1.h
+ * (reference self/forge/forge_tier_v1.h:24-130, which says any ABI change
+ * needs a _v2 bump, :5-7). It adds:
+ *   1. the whole-model decode engine (ForgeB200 handle) that flame's decode
+ *      loop drives in place of nn_decoder_fwd + nn_decoder_predict
+ *      (stdlib/flame/decoder_lib.hexa:93-208, 485-500), with a KV cache;
+ *   2. per-op kernel entries on caller-owned device memory (the B200
+ *      replacements of _hx_cuda_farr_packed_gemv_offset_gpu,
+ *      self/cuda/runtime_cuda_emit.hexa:1858-1967, and of the attention
+ *      kernel _hx_cuda_kern_attn_dt_fwd, :2819-2895);
+ *   3. the int4 group-128 weight format (a generalisation of
+ *      stdlib/flame/quant_lib.hexa:41-141) and its packing;
+ *   4. the bf16 / int4 device-array descriptors (HexaFarrBf16 mirrors
+ *      self/cuda/runtime_bf16_emit.hexa:164-210).
+ * Every entry returns 0 on success or a negative FORGE_* code and leaves one
+ * line in forge_b200_last_error() (printed once to stderr). Streams are
+ * passed as `void*` (a cudaStream_t); no entry synchronises the device
+ * unless it says so. There is no CPU fallback: without a usable sm_100
+ * device every compute entry fails.
+ */
+#ifndef FORGE_B200_H
+#define FORGE_B200_H
+#include <stdint.h>
+#include "forge_tier_v1.h"
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FORGE_API_VERSION_V2_ENCODED ((uint32_t)0x00020000u)
+uint32_t forge_api_version_v2(void);
+
+/* ---- v2 kernel families (dispatched by forge_tier_dispatch_v2) --------- */
+#define FORGE_KERNEL_GEMV_W4A16_G128  16
+#define FORGE_KERNEL_GEMV_BF16        17
+#define FORGE_KERNEL_QKV_ROPE_FUSED   18
+#define FORGE_KERNEL_FLASH_DECODE     19
+#define FORGE_KERNEL_SWIGLU_FUSED     20
+#define FORGE_KERNEL_LMHEAD_ARGMAX    21
+#define FORGE_KERNEL_FLASH_PREFILL    22
+#define FORGE_KERNEL_DECODE_STEP      23
+#define FORGE_PREC_W4A16_G128_BF16    3
+
+/* ---- model ------------------------------------------------------------- */
+#define FORGE_WEIGHT_BF16     0
+#define FORGE_WEIGHT_Q4_G128  1
+
+typedef struct ForgeModelDesc {
+    int32_t n_layer, d_model, n_head, n_kv_head, head_dim, ffn, vocab;
+    float   rms_eps, rope_theta;
+    int32_t weight_kind;   /* FORGE_WEIGHT_*                                      */
+    int32_t tied_head;     /* 1: LM head = embedding table (flame ties them)      */
+    int32_t max_batch;     /* sequences decoded together                          */
+    int32_t max_ctx;       /* KV-cache positions per sequence                     */
+    int32_t tp_rank, tp_size; /* tensor parallel slot (1 = single GPU)           */
+    int32_t act_mode;      /* 0 auto, 1 exact (hi/lo bf16 split of fp32 activations),
+                              2 bf16 activations                                  */
+    int32_t reserved[5];
+} ForgeModelDesc;
+
+/* Host weights of one block in flame's orientation (W[out][in], row-major,
+ * decoder_block_lib.hexa:49-72): bf16 bit patterns; gains fp32. */
+typedef struct ForgeLayerWeights {
+    const uint16_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    const float *g1, *g2;
+} ForgeLayerWeights;
+
+typedef struct ForgeB200 ForgeB200;
+
+int         forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB200** out);
+void        forge_b200_destroy(ForgeB200* h);
+const char* forge_b200_last_error(void);
+void*       forge_b200_stream(ForgeB200* h);
+
+/* Weights: upload logical bf16 (quantised on the device when the model is
+ * int4), or generate N(0, std) synthetic weights on the device with gains
+ * 1.0 (tensor t of the model uses stream (seed, t << 40)). */
+int forge_b200_load_layer(ForgeB200* h, int layer, const ForgeLayerWeights* w);
+int forge_b200_load_embedding(ForgeB200* h, const uint16_t* emb, const float* final_gain,
+                              const uint16_t* head /* NULL when tied */);
+int forge_b200_init_synthetic(ForgeB200* h, uint64_t seed, float std);
+
+/* KV cache / positions. fill_kv_synthetic writes N(0, std) K/V for positions
+ * [0, ctx_len) of every sequence and sets every position to ctx_len. */
+int forge_b200_reset(ForgeB200* h);
+int forge_b200_fill_kv_synthetic(ForgeB200* h, uint64_t seed, int ctx_len, float std);
+int forge_b200_set_positions(ForgeB200* h, const int32_t* pos, int batch);
+int forge_b200_get_kv(ForgeB200* h, int layer, int seq, uint16_t* k_out, uint16_t* v_out);
+
+/* One decode step from host buffers (H2D tokens, graph launch, D2H next
+ * tokens and optional logits [batch][vocab]); synchronous. */
+int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tokens, int32_t* next_tokens,
+                           float* logits);
+/* n_steps device-resident greedy steps (each feeds its argmax to the next);
+ * asynchronous on the handle's stream. */
+int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps);
+/* Greedy generation: prompt [batch][n_prompt] fed token by token, then
+ * n_gen argmax tokens into out [batch][n_gen]; synchronous. */
+int forge_b200_generate(ForgeB200* h, int batch, const int32_t* prompt, int n_prompt, int n_gen,
+                        int32_t* out);
+/* Waits for the handle's stream; fails if a kernel raised its error word. */
+int forge_b200_sync(ForgeB200* h);
+/* Algorithmic HBM bytes of one decode step (weights + scales + head + KV
+ * read/write) at the given batch and context length. */
+int64_t forge_b200_step_bytes(ForgeB200* h, int batch, int ctx_len);
+/* Kernel launches per decode step (for the bench's launch count). */
+int forge_b200_launches_per_step(ForgeB200* h, int batch);
+
+/* ---- per-op entries on caller-owned device memory ------------------------ */
+/* y[b][n] = sum_k W[n][k] x[b][k]: W packed int4 (forge_q4_pack_tiles) or
+ * bf16 (forge_bf16_pack_tiles); x [batch][K] fp32, y [batch][N] fp32.
+ * exact = 1 feeds fp32 activations as hi/lo bf16 pairs. */
+int forge_gemv_w4a16_g128(const void* tiles, const void* scale_tiles, int64_t N, int64_t K,
+                          const float* x, int batch, float* y, int exact, void* stream);
+int forge_gemv_bf16(const void* tiles, int64_t N, int64_t K, const float* x, int batch, float* y,
+                    int exact, void* stream);
+
+/* Split-K flash-decode: q [B][H*hd] fp32, caches [B][Hkv][lmax][hd] bf16,
+ * pos [B] int32 (device), out [B][H*hd] fp32. workspace: at least
+ * forge_flash_decode_workspace_bytes(...) bytes, zeroed once before first use
+ * (the kernel leaves its counters at zero). */
+int64_t forge_flash_decode_workspace_bytes(int B, int H, int Hkv, int hd, int lmax);
+int forge_flash_decode(const float* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos,
+                       int B, int H, int Hkv, int hd, int lmax, float* out, void* workspace,
+                       void* stream);
+
+/* Weight preparation (device memory). */
+int forge_fill_normal_bf16(uint16_t* out, int64_t n, uint64_t seed, uint64_t offset, float std,
+                           void* stream);
+int forge_fill_f32(float* out, int64_t n, float v, void* stream);
+int forge_q4_quantize_bf16(const uint16_t* w, int64_t rows, int64_t K, int group, uint8_t* codes,
+                           uint16_t* scales, void* stream);
+int forge_permute_rows_bf16(const uint16_t* src, uint16_t* dst, int64_t rows, int64_t K, int kind,
+                            int64_t param, void* stream);
+int forge_bf16_pack_tiles(const uint16_t* w, int64_t N, int64_t K, void* tiles, void* stream);
+int forge_q4_pack_tiles(const uint8_t* codes, const uint16_t* scales, int64_t N, int64_t K,
+                        int group, void* tiles, void* scale_tiles, void* stream);
+int forge_q4_unpack_tiles(const void* tiles, const void* scale_tiles, int64_t N, int64_t K,
+                          int group, uint8_t* codes, uint16_t* scales, void* stream);
+int64_t forge_q4_tile_bytes(int64_t N, int64_t K);
+int64_t forge_q4_scale_tile_bytes(int64_t N, int64_t K, int group);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

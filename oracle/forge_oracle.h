@@ -1,0 +1,118 @@
+/* forge_oracle.h — CPU oracle for the flame -> forge decode hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY. This library is the checker: only tests/,
+ * __graft_entry__.smoke() and bench.py's CPU-baseline leg may load it.
+ * The product library (libforge_b200.so) never links or calls it.
+ *
+ * It restates, in plain C, the reference's decode semantics:
+ *   - nn_decoder_fwd / nn_decoder_predict   stdlib/flame/decoder_lib.hexa:93-208, 485-500
+ *   - nn_decoder_block_fwd                  stdlib/flame/decoder_block_lib.hexa:217-508
+ *   - RMSNorm / attention core / SwiGLU / RoPE / embedding / LM head
+ *                                           stdlib/flame/nn_lib.hexa:150-171, 221-278,
+ *                                           385-412, 509-562, 589-651
+ *   - int4 fake-quant / pack / unpack       stdlib/flame/quant_lib.hexa:33-141
+ *   - bf16 RNE rounding                     self/cuda/runtime_bf16_emit.hexa:264-286
+ *   - flame LCG fill                        stdlib/flame/tensor_lib.hexa:67-88
+ *   - split-K decode merge (flash-decode)   self/ml/flash_decode.hexa:1-45
+ * plus the KV-cache decode step (new work; proven equal to the full-recompute
+ * path by the tests) and the group-128 int4 generalisation of quant_lib.
+ */
+#ifndef FORGE_ORACLE_H
+#define FORGE_ORACLE_H
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- bf16 ------------------------------------------------------------ */
+uint16_t or_f32_to_bf16(float v);
+float    or_bf16_to_f32(uint16_t b);
+void     or_f32_to_bf16_n(const float* src, uint16_t* dst, int64_t n);
+void     or_bf16_to_f32_n(const uint16_t* src, float* dst, int64_t n);
+
+/* ---- flame LCG + quant_lib (f64, exactly as the reference) ------------ */
+void or_flame_fill_lcg(double* t, int64_t n, int64_t seed, double scale);
+void or_int4_quant_fwd(const double* w, double* wq_out, double* scale_out,
+                       double* qlevel_out, double* mask_out, int cout, int rest);
+void or_int4_pack(const double* w, uint8_t* packed_out, int n, double scale, int zero);
+void or_int4_unpack(const uint8_t* packed, double* w_out, int n, double scale, int zero);
+
+/* ---- group int4 (bf16 scales) ----------------------------------------- */
+/* codes: [rows][K/2] bytes, even k in the low nibble, code = q + 7.
+ * scales: [rows][K/group] bf16 bits. Returns 0, or -1 on bad shape. */
+int  or_q4g_quantize_bf16(const uint16_t* w, int64_t rows, int64_t K, int group,
+                          uint8_t* codes, uint16_t* scales);
+int  or_q4g_dequant(const uint8_t* codes, const uint16_t* scales, int64_t rows,
+                    int64_t K, int group, float* out);
+
+/* ---- synthetic data ---------------------------------------------------- */
+/* N(0, std) from a counter-based hash: element i of stream `seed` is a
+ * function of (seed, offset + i) only. Bit-identical to the device fill. */
+void   or_fill_normal_bf16(uint16_t* out, int64_t n, uint64_t seed, uint64_t offset, float std);
+double or_normal_at(uint64_t seed, uint64_t idx);
+/* RoPE tables [lmax][hd/2], float, built in double. */
+void   or_rope_table(float* cos_t, float* sin_t, int lmax, int hd, double theta);
+
+/* ---- model ------------------------------------------------------------- */
+enum { OR_MAT_F32 = 0, OR_MAT_BF16 = 1, OR_MAT_Q4 = 2 };
+typedef struct OrMat {
+    int32_t kind;        /* OR_MAT_*                                     */
+    int32_t group;       /* q4 group size along cols                     */
+    int64_t rows, cols;  /* W is [rows][cols] row-major: y = W x         */
+    const void* w;       /* float* / uint16_t* (bf16) / uint8_t* codes    */
+    const uint16_t* scales; /* q4 only: [rows][cols/group] bf16           */
+} OrMat;
+
+typedef struct OrLayer {
+    const float* g1;
+    OrMat wq, wk, wv, wo;
+    const float* g2;
+    OrMat wg, wu, wd;
+} OrLayer;
+
+typedef struct OrModel {
+    int32_t n_layer, d, n_head, n_kv, hd, ffn, vocab;
+    float   eps, theta;
+    const OrLayer* layers;  /* n_layer entries */
+    OrMat   emb;            /* [vocab][d]      */
+    const float* gF;        /* [d]             */
+    OrMat   head;           /* [vocab][d]; tied -> same as emb */
+} OrModel;
+
+/* decode flags */
+#define OR_KV_BF16   1   /* store K/V rounded to bf16 (device cache format) */
+#define OR_ACT_BF16  2   /* round every GEMV input vector to bf16           */
+#define OR_NO_ROPE   4   /* skip RoPE (pins the reference's rope-free decode_eager cpu_ref) */
+
+/* One KV-cache decode step for B sequences. kc/vc: [L][B][Hkv][lmax][hd]
+ * floats. Token b sits at position pos[b] (its K/V are written there) and
+ * attends to positions 0..pos[b]. logits: [B][V] (may be NULL); argmax: [B]
+ * (first max wins, decoder_lib.hexa:485-500). hidden_out: [B][d] final
+ * residual stream before the final norm (may be NULL). Returns 0 / -1. */
+int or_decode_step(const OrModel* m, float* kc, float* vc, int lmax, int B,
+                   const int32_t* tok, const int32_t* pos, int flags,
+                   float* logits, int32_t* argmax, double* hidden_out);
+
+/* Full recompute of the last-position logits over ids[0..T), no cache,
+ * f64 throughout — nn_decoder_fwd + tied/untied head (decoder_lib.hexa:93-208). */
+int or_full_forward(const OrModel* m, const int32_t* ids, int T, double* logits);
+
+/* Greedy decode: prompt of n_prompt ids, then n_gen argmax steps (batch 1).
+ * out_ids receives n_gen generated ids; margins (may be NULL) the top-1 minus
+ * top-2 logit gap of each generated step. */
+int or_greedy(const OrModel* m, int lmax, const int32_t* prompt, int n_prompt,
+              int n_gen, int flags, int32_t* out_ids, float* margins);
+
+/* Single-query split-K attention with LSE merge (flash_decode.hexa:14-27).
+ * q [hd], K/V [L][hd]; returns out [hd]. Used to pin the merge algebra. */
+void or_flash_decode_single(const float* q, const float* K, const float* V,
+                            int L, int hd, int chunk, double* out);
+
+/* Dense helpers used by known-answer tests: C[M][N] = A[M][K] B[K][N] (f64). */
+void or_matmul_f64(const double* A, const double* B, double* C, int M, int K, int N);
+
+int  or_num_threads(void);
+#ifdef __cplusplus
+}
+#endif
+#endif
