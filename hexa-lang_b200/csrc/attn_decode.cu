@@ -21,164 +21,215 @@
 namespace {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
+constexpr int kTile = 64;    // keys per shared-memory tile
+constexpr int kStages = 2;   // K+V tiles in flight per CTA
+
+template <int HD>
+constexpr int stage_bytes() { return 2 * kTile * HD * 2; }  // K tile + V tile, bf16
+
+// Shared memory: [kStages][K tile | V tile] bf16, q [G][HD] f32, scores
+// [G][kTile] f32, per-head running (m, l, alpha), mbarriers.
+template <int HD, int G>
+constexpr int smem_bytes() {
+    return kStages * stage_bytes<HD>() + G * HD * 4 + G * kTile * 4 + 3 * G * 4 + kStages * 8 + 16;
+}
 
 template <int HD, int G>
 __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a) {
-    extern __shared__ __align__(16) float sm[];
-    float* qs = sm;                 // [G][HD]
-    float* red = qs + G * HD;       // [kWarps][G][HD]
-    float* stat = red + kWarps * G * HD;  // [2 * G + 4]
-    float* sc = stat + 2 * G + 4;   // [G][chunk_max]
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint16_t* kv = reinterpret_cast<uint16_t*>(smem);
+    float* qs = reinterpret_cast<float*>(smem + kStages * stage_bytes<HD>());
+    float* sc = qs + G * HD;
+    float* st_m = sc + G * kTile;
+    float* st_l = st_m + G;
+    float* st_a = st_l + G;
+    uint64_t* full = reinterpret_cast<uint64_t*>(
+        (reinterpret_cast<uintptr_t>(st_a + G) + 7) & ~static_cast<uintptr_t>(7));
 
     const int sp = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int nsplit = gridDim.x;
-    pdl_trigger();
-    pdl_wait();
 
+    // Positions only change between steps, so the split range and every
+    // cached row below P can be fetched before the dependency wait; row P
+    // (appended by the QKV kernel just before) is read after it.
     const int P = a.pos[b];
-    if (P < 0 || P >= a.lmax) {
-        if (tid == 0) atomicOr(a.err, FORGE_DEVERR_BAD_INDEX);
-        return;
-    }
-    const int Lc = P + 1;
+    const bool bad = (P < 0 || P >= a.lmax);
+    const int Lc = bad ? 1 : P + 1;
     const int chunk = (Lc + nsplit - 1) / nsplit;
     const int j0 = sp * chunk;
     const int j1 = min(Lc, j0 + chunk);
     const int n = max(0, j1 - j0);
-    const int chunk_max = (a.lmax + nsplit - 1) / nsplit;
-    const float scale = 1.0f / sqrtf((float)HD);
-
-    for (int i = tid; i < G * HD; i += kThreads)
-        qs[i] = a.q[(size_t)b * a.H * HD + (size_t)(kvh * G) * HD + i];
-    __syncthreads();
-
+    const int ntiles = (n + kTile - 1) / kTile;
     const size_t slab = ((size_t)b * a.Hkv + kvh) * a.lmax * HD;
     const uint16_t* K = a.kc + slab;
     const uint16_t* V = a.vc + slab;
 
-    // ---- scores: 4 lanes per key; lane part qp reads 16 B at qp*16 + 64*m
-    const int qp = lane & 3;
-    constexpr int M = HD / 32;  // 16-byte pieces per lane per key
-    for (int base = warp * 8; base < n; base += kWarps * 8) {
-        const int jj = base + (lane >> 2);
-        float dot[G];
+    auto issue = [&](int i) {
+        const int s = i % kStages;
+        const int t0 = j0 + i * kTile;
+        const int rows = min(min(j1, t0 + kTile), P) - t0;  // row P excluded
+        uint16_t* dst = kv + (size_t)s * (stage_bytes<HD>() / 2);
+        if (rows > 0) {
+            const uint32_t bytes = (uint32_t)rows * HD * 2;
+            mbar_arrive_expect_tx(&full[s], 2 * bytes);
+            bulk_g2s(dst, K + (size_t)t0 * HD, bytes, &full[s]);
+            bulk_g2s(dst + kTile * HD, V + (size_t)t0 * HD, bytes, &full[s]);
+        } else {
+            mbar_arrive(&full[s]);
+        }
+    };
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0 && !bad)
+        for (int i = 0; i < kStages && i < ntiles; ++i) issue(i);
+    pdl_trigger();
+    pdl_wait();
+    if (bad) {  // no copies were issued
+        if (tid == 0) atomicOr(a.err, FORGE_DEVERR_BAD_INDEX);
+        return;
+    }
+    for (int i = tid; i < G * HD; i += kThreads) qs[i] = a.q[(size_t)b * a.H * HD + (size_t)(kvh * G) * HD + i];
+    if (tid < G) { st_m[tid] = -INFINITY; st_l[tid] = 0.f; }
+    const float scale = 1.0f / sqrtf((float)HD);
+
+    constexpr int E = HD / 32;            // value dims per lane
+    constexpr int NCH = HD / 16;          // 16-byte chunks per half key row (HD/2 dims)
+    float acc[G][E];
 #pragma unroll
-        for (int gi = 0; gi < G; ++gi) dot[gi] = 0.f;
-        if (jj < n) {
-            const uint16_t* kr = K + (size_t)(j0 + jj) * HD;
-            uint4 kv[M];
+    for (int g = 0; g < G; ++g)
 #pragma unroll
-            for (int m = 0; m < M; ++m) kv[m] = *reinterpret_cast<const uint4*>(kr + m * 32 + qp * 8);
+        for (int e = 0; e < E; ++e) acc[g][e] = 0.f;
+
+    bool ok = true;
+    for (int i = 0; i < ntiles && ok; ++i) {
+        const int s = i % kStages;
+        if (!mbar_wait(&full[s], (i / kStages) & 1, a.err)) { ok = false; break; }
+        const uint16_t* Ks = kv + (size_t)s * (stage_bytes<HD>() / 2);
+        const uint16_t* Vs = Ks + kTile * HD;
+        const int t0 = j0 + i * kTile;
+        const int nt = min(kTile, j1 - t0);
+        if (t0 + nt == Lc) {
+            // the newest row comes straight from global memory
+            uint16_t* kd = const_cast<uint16_t*>(Ks) + (size_t)(nt - 1) * HD;
+            uint16_t* vd = const_cast<uint16_t*>(Vs) + (size_t)(nt - 1) * HD;
+            if (tid < HD / 8) reinterpret_cast<uint4*>(kd)[tid] = reinterpret_cast<const uint4*>(K + (size_t)P * HD)[tid];
+            else if (tid < HD / 4) reinterpret_cast<uint4*>(vd)[tid - HD / 8] = reinterpret_cast<const uint4*>(V + (size_t)P * HD)[tid - HD / 8];
+        }
+        __syncthreads();
+        // ---- scores: two threads per key, each half a row; chunk order rotated by
+        // thread so the 8 threads of a shared-memory phase hit distinct banks
+        {
+            // rows past nt hold stale data: computed but never stored, so the
+            // warp stays converged for the shuffle
+            const int k = tid >> 1, h = tid & 1;
+            float dot[G];
 #pragma unroll
-            for (int m = 0; m < M; ++m) {
-                const uint32_t w4[4] = {kv[m].x, kv[m].y, kv[m].z, kv[m].w};
+            for (int g = 0; g < G; ++g) dot[g] = 0.f;
+            const uint16_t* kr = Ks + (size_t)k * HD + h * (HD / 2);
 #pragma unroll
-                for (int gi = 0; gi < G; ++gi) {
-                    const float* qv = qs + gi * HD + m * 32 + qp * 8;
+            for (int j = 0; j < NCH; ++j) {
+                const int c = (j + tid) & (NCH - 1);
+                const uint4 kw = *reinterpret_cast<const uint4*>(kr + c * 8);
+                const uint32_t w4[4] = {kw.x, kw.y, kw.z, kw.w};
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float* qv = qs + g * HD + h * (HD / 2) + c * 8;
                     const float4 q0 = *reinterpret_cast<const float4*>(qv);
                     const float4 q1 = *reinterpret_cast<const float4*>(qv + 4);
-                    float d = dot[gi];
+                    float d = dot[g];
                     d = fmaf(q0.x, bf16_lo_f32(w4[0]), d); d = fmaf(q0.y, bf16_hi_f32(w4[0]), d);
                     d = fmaf(q0.z, bf16_lo_f32(w4[1]), d); d = fmaf(q0.w, bf16_hi_f32(w4[1]), d);
                     d = fmaf(q1.x, bf16_lo_f32(w4[2]), d); d = fmaf(q1.y, bf16_hi_f32(w4[2]), d);
                     d = fmaf(q1.z, bf16_lo_f32(w4[3]), d); d = fmaf(q1.w, bf16_hi_f32(w4[3]), d);
-                    dot[gi] = d;
+                    dot[g] = d;
                 }
             }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float d = dot[g] + __shfl_xor_sync(0xffffffffu, dot[g], 1);
+                if (h == 0 && k < nt) sc[g * kTile + k] = d * scale;
+            }
         }
+        __syncthreads();
+        // ---- online softmax statistics (one warp per head)
+        for (int g = warp; g < G; g += kWarps) {
+            float mt = -INFINITY;
+            for (int j = lane; j < nt; j += 32) mt = fmaxf(mt, sc[g * kTile + j]);
 #pragma unroll
-        for (int gi = 0; gi < G; ++gi) {
-            float d = dot[gi];
-            d += __shfl_xor_sync(0xffffffffu, d, 1);
-            d += __shfl_xor_sync(0xffffffffu, d, 2);
-            if (qp == 0 && jj < n) sc[gi * chunk_max + jj] = d * scale;
+            for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+            const float mo = st_m[g];
+            const float mn = fmaxf(mo, mt);
+            float ls = 0.f;
+            for (int j = lane; j < nt; j += 32) {
+                const float p = expf(sc[g * kTile + j] - mn);
+                sc[g * kTile + j] = p;
+                ls += p;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+            if (lane == 0) {
+                const float al = (mo == -INFINITY) ? 0.f : expf(mo - mn);
+                st_a[g] = al;
+                st_l[g] = st_l[g] * al + ls;
+                st_m[g] = mn;
+            }
         }
-    }
-    __syncthreads();
-
-    // ---- split-local softmax statistics per query head (warp gi % kWarps)
-    for (int gi = warp; gi < G; gi += kWarps) {
-        float mx = -INFINITY;
-        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, sc[gi * chunk_max + j]);
+        __syncthreads();
+        // ---- P·V: warp w takes keys w, w+4, ...; lane owns dims lane*E..+E
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float l = 0.f;
-        for (int j = lane; j < n; j += 32) {
-            const float p = expf(sc[gi * chunk_max + j] - mx);
-            sc[gi * chunk_max + j] = p;
-            l += p;
+        for (int g = 0; g < G; ++g) {
+            const float al = st_a[g];
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[g][e] *= al;
         }
+        for (int j = warp; j < nt; j += kWarps) {
+            uint32_t vv[E / 2];
+            if (E == 4) {
+                const uint2 t2 = *reinterpret_cast<const uint2*>(Vs + (size_t)j * HD + lane * E);
+                vv[0] = t2.x; vv[E / 2 - 1] = t2.y;
+            } else {
+                vv[0] = *reinterpret_cast<const uint32_t*>(Vs + (size_t)j * HD + lane * E);
+            }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) { stat[2 * gi] = mx; stat[2 * gi + 1] = l; }
-    }
-    __syncthreads();
-
-    // ---- P·V: each warp takes keys j = warp, warp + 4, ...; lane owns HD/32 dims
-    constexpr int E = HD / 32;
-    float acc[G][E];
-#pragma unroll
-    for (int gi = 0; gi < G; ++gi)
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[gi][e] = 0.f;
-    int j = warp;
-    for (; j + 3 * kWarps < n; j += 4 * kWarps) {
-        uint32_t vv[4][E / 2];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const uint16_t* vr = V + (size_t)(j0 + j + u * kWarps) * HD + lane * E;
-            if (E == 4) { uint2 t2 = *reinterpret_cast<const uint2*>(vr); vv[u][0] = t2.x; vv[u][E / 2 - 1] = t2.y; }
-            else vv[u][0] = *reinterpret_cast<const uint32_t*>(vr);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int gi = 0; gi < G; ++gi) {
-                const float p = sc[gi * chunk_max + j + u * kWarps];
+            for (int g = 0; g < G; ++g) {
+                const float p = sc[g * kTile + j];
 #pragma unroll
                 for (int e2 = 0; e2 < E / 2; ++e2) {
-                    acc[gi][2 * e2] = fmaf(p, bf16_lo_f32(vv[u][e2]), acc[gi][2 * e2]);
-                    acc[gi][2 * e2 + 1] = fmaf(p, bf16_hi_f32(vv[u][e2]), acc[gi][2 * e2 + 1]);
+                    acc[g][2 * e2] = fmaf(p, bf16_lo_f32(vv[e2]), acc[g][2 * e2]);
+                    acc[g][2 * e2 + 1] = fmaf(p, bf16_hi_f32(vv[e2]), acc[g][2 * e2 + 1]);
                 }
             }
-    }
-    for (; j < n; j += kWarps) {
-        const uint16_t* vr = V + (size_t)(j0 + j) * HD + lane * E;
-        uint32_t vv[E / 2];
-        if (E == 4) { uint2 t2 = *reinterpret_cast<const uint2*>(vr); vv[0] = t2.x; vv[E / 2 - 1] = t2.y; }
-        else vv[0] = *reinterpret_cast<const uint32_t*>(vr);
-#pragma unroll
-        for (int gi = 0; gi < G; ++gi) {
-            const float p = sc[gi * chunk_max + j];
-#pragma unroll
-            for (int e2 = 0; e2 < E / 2; ++e2) {
-                acc[gi][2 * e2] = fmaf(p, bf16_lo_f32(vv[e2]), acc[gi][2 * e2]);
-                acc[gi][2 * e2 + 1] = fmaf(p, bf16_hi_f32(vv[e2]), acc[gi][2 * e2 + 1]);
-            }
         }
+        __syncthreads();  // stage s and the scores are free again
+        if (tid == 0 && i + kStages < ntiles) issue(i + kStages);
     }
-#pragma unroll
-    for (int gi = 0; gi < G; ++gi)
-#pragma unroll
-        for (int e = 0; e < E; ++e) red[(warp * G + gi) * HD + lane * E + e] = acc[gi][e];
-    __syncthreads();
+    if (!ok) return;
 
-    // ---- write this split's partial (unnormalised O, m, l)
-    const int stride = HD + 2;
-    for (int i = tid; i < G * HD; i += kThreads) {
-        const int gi = i / HD, e = i % HD;
-        float s = 0.f;
+    // ---- combine the four warps' partial O (reusing the tile buffers)
+    float* red = reinterpret_cast<float*>(smem);  // [kWarps][G][HD]
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) s += red[(w * G + gi) * HD + e];
-        const int h = kvh * G + gi;
-        a.partial[(((size_t)b * a.H + h) * nsplit + sp) * stride + e] = s;
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < E; ++e) red[(warp * G + g) * HD + lane * E + e] = acc[g][e];
+    __syncthreads();
+    const int stride = HD + 2;
+    for (int idx = tid; idx < G * HD; idx += kThreads) {
+        const int g = idx / HD, e = idx % HD;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) sum += red[(w * G + g) * HD + e];
+        const int h = kvh * G + g;
+        a.partial[(((size_t)b * a.H + h) * nsplit + sp) * stride + e] = sum;
     }
     if (tid < G) {
         const int h = kvh * G + tid;
         float* pm = a.partial + (((size_t)b * a.H + h) * nsplit + sp) * stride + HD;
-        pm[0] = n > 0 ? stat[2 * tid] : -INFINITY;
-        pm[1] = n > 0 ? stat[2 * tid + 1] : 0.f;
+        pm[0] = n > 0 ? st_m[tid] : -INFINITY;
+        pm[1] = n > 0 ? st_l[tid] : 0.f;
     }
     __threadfence();
     __syncthreads();
@@ -191,10 +242,10 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
     if (!is_last) return;
     __threadfence();
 
-    // ---- merge all splits (log-sum-exp), write fp32 context
-    for (int i = tid; i < G * HD; i += kThreads) {
-        const int gi = i / HD, e = i % HD;
-        const int h = kvh * G + gi;
+    // ---- merge all splits (log-sum-exp), write the fp32 context
+    for (int idx = tid; idx < G * HD; idx += kThreads) {
+        const int g = idx / HD, e = idx % HD;
+        const int h = kvh * G + g;
         const float* pb = a.partial + ((size_t)b * a.H + h) * nsplit * stride;
         float mg = -INFINITY;
         for (int s2 = 0; s2 < nsplit; ++s2) mg = fmaxf(mg, __ldcg(pb + s2 * stride + HD));
@@ -212,10 +263,8 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
 
 template <int HD, int G>
 int launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl) {
-    const int chunk_max = (a.lmax + a.nsplit - 1) / a.nsplit;
-    const size_t smem = sizeof(float) * ((size_t)G * HD + (size_t)kWarps * G * HD + 2 * G + 4 +
-                                         (size_t)G * chunk_max);
-    if (smem > 200 * 1024) return forge_fail(-1, "flash-decode: chunk too long (%d) — raise nsplit", chunk_max);
+    constexpr int smem = smem_bytes<HD, G>();
+    static_assert(kWarps * G * HD * 4 <= kStages * stage_bytes<HD>(), "partial-O reduction must fit the tile buffers");
     auto kern = k_flash_decode<HD, G>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, a.Hkv, a.B);
@@ -264,15 +313,13 @@ int forge_attn_configure() {
 }
 
 int forge_attn_pick_splits(int B, int Hkv, int lmax) {
-    // ~4 CTAs per SM of a 148-SM B200; fixed so workspace sizes do not depend
-    // on which device is current.
-    const int target = 4 * 148;
+    // ~12 CTAs per SM of a 148-SM B200 (3 resident x ~4 waves); fixed so
+    // workspace sizes do not depend on which device is current.
+    const int target = 12 * 148;
     int ns = (target + B * Hkv - 1) / (B * Hkv);
-    const int cap = (lmax + 63) / 64;  // at least ~64 keys per split at full context
+    const int cap = (lmax + 127) / 128;  // at least ~128 keys per split at full context
     if (ns > cap) ns = cap;
     if (ns < 1) ns = 1;
-    // keep the score buffer within shared memory for long contexts
-    while ((lmax + ns - 1) / ns > 8192) ++ns;
     return ns;
 }
 int64_t forge_attn_partial_floats(int B, int H, int hd, int nsplit) {

@@ -31,18 +31,23 @@
 // tcgen05 A operand would have to round-trip bf16 through shared memory or
 // TMEM, 8 bytes of on-chip traffic per HBM byte).
 #include <cstdio>
+#include <cstdlib>
 #include "common.cuh"
 #include "layout.cuh"
 #include "forge_internal.h"
 
 namespace {
+#ifndef FORGE_GEMV_STAGES
+#define FORGE_GEMV_STAGES 4
+#endif
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 6;
-constexpr int kStageW = 8192;
-constexpr int kStageS = 256;
+constexpr int kStages = FORGE_GEMV_STAGES;
+constexpr int kStageW = 16384;                        // weight bytes per piece
+constexpr int kStageS = 512;                          // q4 scale bytes per piece (16 groups)
 constexpr int kStageBytes = kStageW + kStageS;
-constexpr int kRedFloats = kConsumerWarps * 16 * 8;
+constexpr int kRedFloats = 2 * kConsumerWarps * 16 * 8;  // two unit slots
+constexpr int kMaxG = 256;                            // K <= 32768 for the group sums
 constexpr int kFixedSmem = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4;
 constexpr int kMaxSmem = 227 * 1024;
 
@@ -52,10 +57,24 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t row) 
     return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - row);
 }
 
-template <int PRO>
-__device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xs, float* red) {
-    const int tid = threadIdx.x;  // consumer threads 0..255
-    const int K = a.K, stride = K + 8;
+// Shared-memory B operand in mma fragment order: for every pair of k-tiles
+// kp and column c, the 4 lanes t = 0..3 each own 16 bytes holding
+// {b0, b1} of k-tile 2kp and {b0, b1} of k-tile 2kp+1, so one LDS.128 per
+// lane feeds two mma steps. Columns are (sequence, hi|lo) in exact mode.
+__device__ __forceinline__ int xf_index(int k, int col, int ncols) {
+    const int kt = k >> 4, kk = k & 15;
+    const int kp = kt >> 1, which = kt & 1, t = (kk & 7) >> 1, half = kk >> 3, e = kk & 1;
+    return (((kp * ncols + col) * 4 + t) * 8) + which * 4 + half * 2 + e;
+}
+
+// Prologue (consumer warps): optional RMSNorm, hi/lo split, fragment-order
+// store, and (int4) per-group column sums of the bf16 operand for the
+// dequantisation-bias correction.
+template <int WK, int PRO>
+__device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, float* sx, float* red) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = a.K;
+    const int ncols = a.split ? 2 * a.batch : a.batch;
     for (int b = 0; b < a.batch; ++b) {
         const float* xb = a.x + (size_t)b * a.x_stride;
         float inv = 1.0f;
@@ -67,7 +86,7 @@ __device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xs, fl
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            if ((tid & 31) == 0) red[tid >> 5] = ss;
+            if (lane == 0) red[warp] = ss;
             named_bar_sync(1, 256);
             float tot = 0.0f;
 #pragma unroll
@@ -75,6 +94,7 @@ __device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xs, fl
             inv = 1.0f / sqrtf(tot / (float)K + a.eps);
             named_bar_sync(1, 256);
         }
+        // 4 consecutive k per thread; a warp covers one 128-group per pass
         for (int k = tid * 4; k < K; k += 256 * 4) {
             float4 v = *reinterpret_cast<const float4*>(xb + k);
             float e[4] = {v.x, v.y, v.z, v.w};
@@ -83,22 +103,46 @@ __device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xs, fl
                 e[0] = gv.x * (e[0] * inv); e[1] = gv.y * (e[1] * inv);
                 e[2] = gv.z * (e[2] * inv); e[3] = gv.w * (e[3] * inv);
             }
+            uint16_t hi[4], lo[4];
+            float shi = 0.f, slo = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (a.split) split_bf16(e[i], hi[i], lo[i]);
+                else { hi[i] = f32_to_bf16_bits(e[i]); lo[i] = 0; }
+                shi += bf16_bits_to_f32(hi[i]);
+                slo += bf16_bits_to_f32(lo[i]);
+            }
+            const int ch = a.split ? 2 * b : b;
+            *reinterpret_cast<uint32_t*>(xf + xf_index(k, ch, ncols)) = hi[0] | ((uint32_t)hi[1] << 16);
+            *reinterpret_cast<uint32_t*>(xf + xf_index(k + 2, ch, ncols)) = hi[2] | ((uint32_t)hi[3] << 16);
             if (a.split) {
-                uint16_t hi[4], lo[4];
+                *reinterpret_cast<uint32_t*>(xf + xf_index(k, ch + 1, ncols)) = lo[0] | ((uint32_t)lo[1] << 16);
+                *reinterpret_cast<uint32_t*>(xf + xf_index(k + 2, ch + 1, ncols)) = lo[2] | ((uint32_t)lo[3] << 16);
+            }
+            if (WK == FORGE_W_Q4) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) split_bf16(e[i], hi[i], lo[i]);
-                uint2 h2 = make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
-                uint2 l2 = make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
-                *reinterpret_cast<uint2*>(xs + (size_t)(2 * b) * stride + k) = h2;
-                *reinterpret_cast<uint2*>(xs + (size_t)(2 * b + 1) * stride + k) = l2;
-            } else {
-                uint16_t h[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) h[i] = f32_to_bf16_bits(e[i]);
-                *reinterpret_cast<uint2*>(xs + (size_t)b * stride + k) =
-                    make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+                for (int o = 16; o > 0; o >>= 1) {
+                    shi += __shfl_xor_sync(0xffffffffu, shi, o);
+                    slo += __shfl_xor_sync(0xffffffffu, slo, o);
+                }
+                if (lane == 0) {
+                    sx[(k >> 7) * 8 + ch] = shi;
+                    if (a.split) sx[(k >> 7) * 8 + ch + 1] = slo;
+                }
             }
         }
+    }
+}
+
+// When K/16 is odd the last k-tile pair is half padding: zero it so the
+// padded mma step multiplies by exact zeros.
+__device__ __forceinline__ void zero_x_pad(const ForgeGemvArgs& a, uint16_t* xf) {
+    const int K = a.K;
+    if ((K & 31) == 0) return;
+    const int ncols = a.split ? 2 * a.batch : a.batch;
+    for (int i = threadIdx.x; i < ncols * 16; i += 256) {
+        const int col = i >> 4, k = K + (i & 15);
+        xf[xf_index(k, col, ncols)] = 0;
     }
 }
 
@@ -119,8 +163,8 @@ __device__ __forceinline__ void epilogue(const ForgeGemvArgs& a, int u, int p, i
         if (row0 + p + 8 < a.nvalid) { unsigned long long k = argmax_key(yhi, row0 + p + 8); best = k > best ? k : best; }
     } else if (EPI == FORGE_EPI_SWIGLU) {
         // physical tile u = gate rows 8u..8u+7 (rows 0-7), up rows 8u..8u+7 (rows 8-15)
-        float gte = ylo, upv = yhi;
-        float sl = gte / (1.0f + expf(-gte));
+        const float gte = ylo, upv = yhi;
+        const float sl = gte / (1.0f + expf(-gte));
         a.s_out[(size_t)b * a.F + 8 * u + p] = sl * upv;
     } else if (EPI == FORGE_EPI_QKV) {
         const int hd = a.hd, head = row0 / hd, i = (row0 % hd) >> 4;
@@ -150,6 +194,18 @@ __device__ __forceinline__ void epilogue(const ForgeGemvArgs& a, int u, int p, i
     }
 }
 
+// A values of the int4 path are 135 + q (0x4300 | code), so a group's
+// accumulator carries 135 * sum(B) extra; it is removed per group from the
+// precomputed column sums. The raw A values are exact in bf16 and every
+// product is exact in fp32.
+__device__ __forceinline__ void dequant_q4_biased(uint32_t w, uint32_t (&a)[4]) {
+    const uint32_t mask = 0x000F000Fu, magic = 0x43004300u;
+    a[0] = lop3_and_or(w, mask, magic);
+    a[1] = lop3_and_or(w >> 4, mask, magic);
+    a[2] = lop3_and_or(w >> 8, mask, magic);
+    a[3] = lop3_and_or(w >> 12, mask, magic);
+}
+
 template <int WK, int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -157,11 +213,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
     uint64_t* empty = full + kStages;
     float* red = reinterpret_cast<float*>(empty + kStages);
-    uint16_t* xs = reinterpret_cast<uint16_t*>(red + kRedFloats);
+    float* sx = red + kRedFloats;                                   // [G][8] (int4 only)
+    uint16_t* xf = reinterpret_cast<uint16_t*>(sx + (WK == FORGE_W_Q4 ? (a.K / 128) * 8 : 0));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KT = a.K >> 4;
-    constexpr int kItemKT = (WK == FORGE_W_Q4) ? 64 : 16;
+    constexpr int kItemKT = (WK == FORGE_W_Q4) ? 128 : 32;
     constexpr int kTileBytes = (WK == FORGE_W_Q4) ? 128 : 512;  // per 16x16 tile
     const int nitems = (KT + kItemKT - 1) / kItemKT;
     const int units = a.N >> 4;
@@ -212,19 +269,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
 
     // ---------------------------------------------------------- consumers
     pdl_wait();
-    stage_x<PRO>(a, xs, red);
+    stage_x<WK, PRO>(a, xf, sx, red);
+    zero_x_pad(a, xf);
     named_bar_sync(1, 256);
 
     const int g = lane >> 2, t = lane & 3;
     const int ncols = a.split ? 2 * a.batch : a.batch;
-    const int col = g < ncols ? g : ncols - 1;  // unused columns read a valid row
-    const uint16_t* xcol = xs + (size_t)col * (a.K + 8) + 2 * t;
+    const int col = g < ncols ? g : ncols - 1;  // unused columns re-read a valid one
+    const int c0 = min(2 * t, ncols - 1), c1 = min(2 * t + 1, ncols - 1);
     unsigned long long best = 0ull;
     uint32_t it = 0;
+    int slot = 0;
     bool ok = true;
 
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, slot ^= 1) {
         float tot[4] = {0.f, 0.f, 0.f, 0.f};
+        float tot2[4] = {0.f, 0.f, 0.f, 0.f};
         for (int i = 0; i < nitems; ++i) {
             const int s = it % kStages;
             const uint32_t ph = (it / kStages) & 1u;
@@ -232,40 +292,85 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
             const int kt0 = i * kItemKT, nkt = min(kItemKT, KT - kt0);
             const uint8_t* st = stages + s * kStageBytes;
             if (WK == FORGE_W_Q4) {
-                const int ktw = warp * 8;  // one 128-group per warp
-                if (ktw < nkt) {
-                    const uint4 c0 = *reinterpret_cast<const uint4*>(st + (ktw / 4) * 512 + lane * 16);
-                    const uint4 c1 = *reinterpret_cast<const uint4*>(st + (ktw / 4 + 1) * 512 + lane * 16);
-                    const uint32_t sc = *reinterpret_cast<const uint32_t*>(
-                        st + kStageW + (((warp >> 2) * 64) + g * 8 + (warp & 3) * 2) * 2);
-                    const uint16_t* xk = xcol + (size_t)(kt0 + ktw) * 16;
-                    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-                    const uint32_t wd[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        uint32_t af[4];
-                        dequant_q4_word(wd[j], af);
-                        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xk + j * 16);
-                        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(xk + j * 16 + 8);
-                        mma_bf16_16816(acc, af, b0, b1, acc);
+                // warp w: groups 2w and 2w+1 of this piece (k-tiles 16w .. 16w+15)
+                const int ng = nkt / 8;
+                const int gA = 2 * warp;
+                if (gA < ng) {
+                    const bool hasB = gA + 1 < ng;
+                    uint4 wq[4];
+                    wq[0] = *reinterpret_cast<const uint4*>(st + (4 * warp + 0) * 512 + lane * 16);
+                    wq[1] = *reinterpret_cast<const uint4*>(st + (4 * warp + 1) * 512 + lane * 16);
+                    if (hasB) {
+                        wq[2] = *reinterpret_cast<const uint4*>(st + (4 * warp + 2) * 512 + lane * 16);
+                        wq[3] = *reinterpret_cast<const uint4*>(st + (4 * warp + 3) * 512 + lane * 16);
+                    } else {
+                        wq[2] = make_uint4(0, 0, 0, 0); wq[3] = wq[2];
                     }
-                    const float slo = bf16_lo_f32(sc), shi = bf16_hi_f32(sc);
-                    tot[0] = fmaf(slo, acc[0], tot[0]);
-                    tot[1] = fmaf(slo, acc[1], tot[1]);
-                    tot[2] = fmaf(shi, acc[2], tot[2]);
-                    tot[3] = fmaf(shi, acc[3], tot[3]);
+                    const uint32_t wA[8] = {wq[0].x, wq[0].y, wq[0].z, wq[0].w, wq[1].x, wq[1].y, wq[1].z, wq[1].w};
+                    const uint32_t wB[8] = {wq[2].x, wq[2].y, wq[2].z, wq[2].w, wq[3].x, wq[3].y, wq[3].z, wq[3].w};
+                    const int kpA = (kt0 + 16 * warp) >> 1;      // k-tile pair index of group A
+                    const uint4* xa = reinterpret_cast<const uint4*>(xf) + (size_t)(kpA * ncols + col) * 4 + t;
+                    const size_t pstride = (size_t)ncols * 4;    // uint4 per k-tile pair
+                    float aA0[4] = {0.f, 0.f, 0.f, 0.f}, aA1[4] = {0.f, 0.f, 0.f, 0.f};
+                    float aB0[4] = {0.f, 0.f, 0.f, 0.f}, aB1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {  // k-tile pairs of each group
+                        const uint4 bA = xa[j * pstride];
+                        uint32_t af[4];
+                        dequant_q4_biased(wA[2 * j], af);
+                        mma_bf16_16816(aA0, af, bA.x, bA.y, aA0);
+                        dequant_q4_biased(wA[2 * j + 1], af);
+                        mma_bf16_16816(aA1, af, bA.z, bA.w, aA1);
+                        if (hasB) {
+                            const uint4 bB = xa[(j + 4) * pstride];
+                            dequant_q4_biased(wB[2 * j], af);
+                            mma_bf16_16816(aB0, af, bB.x, bB.y, aB0);
+                            dequant_q4_biased(wB[2 * j + 1], af);
+                            mma_bf16_16816(aB1, af, bB.z, bB.w, aB1);
+                        }
+                    }
+                    // scales of rows g / g+8 for groups gA, gA+1 (one 128-byte block per 4 groups)
+                    const uint16_t* sst = reinterpret_cast<const uint16_t*>(st + kStageW);
+                    const uint32_t scA = *reinterpret_cast<const uint32_t*>(sst + (gA >> 2) * 64 + g * 8 + (gA & 3) * 2);
+                    const int ggA = kt0 / 8 + gA;               // global group index
+                    const float sxA0 = sx[ggA * 8 + c0], sxA1 = sx[ggA * 8 + c1];
+                    float slo = bf16_lo_f32(scA), shi = bf16_hi_f32(scA);
+                    tot[0] = fmaf(slo, (aA0[0] + aA1[0]) - 135.f * sxA0, tot[0]);
+                    tot[1] = fmaf(slo, (aA0[1] + aA1[1]) - 135.f * sxA1, tot[1]);
+                    tot[2] = fmaf(shi, (aA0[2] + aA1[2]) - 135.f * sxA0, tot[2]);
+                    tot[3] = fmaf(shi, (aA0[3] + aA1[3]) - 135.f * sxA1, tot[3]);
+                    if (hasB) {
+                        const int gB = gA + 1;
+                        const uint32_t scB = *reinterpret_cast<const uint32_t*>(sst + (gB >> 2) * 64 + g * 8 + (gB & 3) * 2);
+                        const float sxB0 = sx[(ggA + 1) * 8 + c0], sxB1 = sx[(ggA + 1) * 8 + c1];
+                        slo = bf16_lo_f32(scB); shi = bf16_hi_f32(scB);
+                        tot2[0] = fmaf(slo, (aB0[0] + aB1[0]) - 135.f * sxB0, tot2[0]);
+                        tot2[1] = fmaf(slo, (aB0[1] + aB1[1]) - 135.f * sxB1, tot2[1]);
+                        tot2[2] = fmaf(shi, (aB0[2] + aB1[2]) - 135.f * sxB0, tot2[2]);
+                        tot2[3] = fmaf(shi, (aB0[3] + aB1[3]) - 135.f * sxB1, tot2[3]);
+                    }
                 }
             } else {
-                const int ktw = warp * 2;
+                // warp w: k-tiles 4w .. 4w+3 (two pairs), two accumulator chains
+                const int ktw = 4 * warp;
+                if (ktw < nkt) {
+                    const int kp = (kt0 + ktw) >> 1;
+                    const uint4* xa = reinterpret_cast<const uint4*>(xf) + (size_t)(kp * ncols + col) * 4 + t;
+                    const size_t pstride = (size_t)ncols * 4;
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    if (ktw + j < nkt) {
-                        const uint4 av = *reinterpret_cast<const uint4*>(st + (ktw + j) * 512 + lane * 16);
-                        const uint32_t af[4] = {av.x, av.y, av.z, av.w};
-                        const uint16_t* xk = xcol + (size_t)(kt0 + ktw + j) * 16;
-                        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(xk);
-                        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(xk + 8);
-                        mma_bf16_16816(tot, af, b0, b1, tot);
+                    for (int j = 0; j < 2; ++j) {
+                        if (ktw + 2 * j < nkt) {
+                            const uint4 a0 = *reinterpret_cast<const uint4*>(st + (ktw + 2 * j) * 512 + lane * 16);
+                            // the odd last k-tile of a K/16-odd matrix has no partner in the piece
+                            const uint4 a1 = (ktw + 2 * j + 1 < nkt)
+                                ? *reinterpret_cast<const uint4*>(st + (ktw + 2 * j + 1) * 512 + lane * 16)
+                                : make_uint4(0, 0, 0, 0);
+                            const uint4 bb = xa[j * pstride];
+                            const uint32_t f0[4] = {a0.x, a0.y, a0.z, a0.w};
+                            const uint32_t f1[4] = {a1.x, a1.y, a1.z, a1.w};
+                            mma_bf16_16816(tot, f0, bb.x, bb.y, tot);
+                            mma_bf16_16816(tot2, f1, bb.z, bb.w, tot2);
+                        }
                     }
                 }
             }
@@ -274,34 +379,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
             ++it;
         }
         if (!ok) break;
-        // cross-warp reduction: red[warp][row][col]
-        float* rw = red + warp * 16 * 8;
-        rw[g * 8 + 2 * t] = tot[0];
-        rw[g * 8 + 2 * t + 1] = tot[1];
-        rw[(g + 8) * 8 + 2 * t] = tot[2];
-        rw[(g + 8) * 8 + 2 * t + 1] = tot[3];
+        // cross-warp reduction through one of two slots: one barrier per unit;
+        // warps 0-1 run the epilogue while the others start the next unit
+        float* rw = red + (slot * kConsumerWarps + warp) * 16 * 8;
+        rw[g * 8 + 2 * t] = tot[0] + tot2[0];
+        rw[g * 8 + 2 * t + 1] = tot[1] + tot2[1];
+        rw[(g + 8) * 8 + 2 * t] = tot[2] + tot2[2];
+        rw[(g + 8) * 8 + 2 * t + 1] = tot[3] + tot2[3];
         named_bar_sync(1, 256);
         const int tid = threadIdx.x;
         if (tid < 8 * a.batch) {
             const int p = tid & 7, b = tid >> 3;
             const int c = a.split ? 2 * b : b;
+            const float* rs = red + slot * kConsumerWarps * 16 * 8;
             float ylo = 0.f, yhi = 0.f;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) {
-                ylo += red[(w * 16 + p) * 8 + c];
-                yhi += red[(w * 16 + p + 8) * 8 + c];
+                ylo += rs[(w * 16 + p) * 8 + c];
+                yhi += rs[(w * 16 + p + 8) * 8 + c];
                 if (a.split) {
-                    ylo += red[(w * 16 + p) * 8 + c + 1];
-                    yhi += red[(w * 16 + p + 8) * 8 + c + 1];
+                    ylo += rs[(w * 16 + p) * 8 + c + 1];
+                    yhi += rs[(w * 16 + p + 8) * 8 + c + 1];
                 }
             }
             epilogue<EPI>(a, u, p, b, ylo, yhi, best);
         }
-        named_bar_sync(1, 256);
     }
 
     if (EPI == FORGE_EPI_LOGITS && warp < 2) {
-        // thread (p, b) = (tid & 7, tid >> 3): reduce over the 8 rows-pairs
+        // thread (p, b) = (tid & 7, tid >> 3): reduce over the 8 row pairs
 #pragma unroll
         for (int o = 1; o < 8; o <<= 1) {
             unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
@@ -329,7 +435,12 @@ template <int WK, int PRO, int EPI>
 int launch_one(const ForgeGemvArgs& a, cudaStream_t stream, bool pdl, int smem) {
     auto kern = k_gemv<WK, PRO, EPI>;
     const int units = a.N / 16;
-    int grid = forge_sm_count();
+    static int ctas_per_sm = 0;
+    if (!ctas_per_sm) {
+        const char* e = getenv("FORGE_GEMV_CTAS_PER_SM");
+        ctas_per_sm = (e && atoi(e) > 0 && atoi(e) <= 4) ? atoi(e) : 1;
+    }
+    int grid = forge_sm_count() * ctas_per_sm;
     if (grid > units) grid = units;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -372,19 +483,29 @@ int forge_gemv_configure() {
     return rc ? -1 : 0;
 }
 
+// Number of launches forge_gemv_launch issues for one call.
+int forge_gemv_launch_count(int K, int batch, bool split) {
+    int max_cols = (kMaxSmem - kFixedSmem - (K / 128) * 32) / (((K + 31) / 32) * 64);
+    if (max_cols > 8) max_cols = 8;
+    const int per = max_cols / (split ? 2 : 1);
+    return per > 0 ? (batch + per - 1) / per : 0;
+}
+
 int forge_gemv_launch(const ForgeGemvArgs& a0, cudaStream_t stream, bool pdl) {
     if (!a0.w || !a0.x || a0.N <= 0 || a0.K <= 0 || (a0.N % 16) || (a0.K % 16) || a0.batch <= 0)
         return forge_fail(-1, "gemv: bad shape N=%d K=%d batch=%d", a0.N, a0.K, a0.batch);
     if (a0.wkind == FORGE_W_Q4 && (!a0.s || (a0.K % 128)))
         return forge_fail(-1, "gemv: int4 weights need scales and K %% 128 == 0 (group 128)");
     if (a0.pro == FORGE_PRO_RMSNORM && !a0.gain) return forge_fail(-1, "gemv: RMSNorm prologue needs a gain");
-    if ((a0.x_stride % 4) || (a0.K % 4)) return forge_fail(-1, "gemv: x rows must be 16-byte aligned");
+    if ((a0.x_stride % 4) || (a0.K % 16)) return forge_fail(-1, "gemv: K %% 16 == 0 and 16-byte aligned x rows required");
     if (a0.epi == FORGE_EPI_SWIGLU && a0.N != 2 * a0.F) return forge_fail(-1, "gemv: SwiGLU needs N == 2F");
     if (a0.epi == FORGE_EPI_QKV && (a0.hd % 16 || a0.N != (a0.H + 2 * a0.Hkv) * a0.hd))
         return forge_fail(-1, "gemv: QKV epilogue shape mismatch");
     const int cols_per_seq = a0.split ? 2 : 1;
-    const int xs_row = (a0.K + 8) * 2;
-    int max_cols = (kMaxSmem - kFixedSmem) / xs_row;
+    if (a0.K / 128 > kMaxG) return forge_fail(-1, "gemv: K=%d above the supported maximum", a0.K);
+    const int sx_bytes = a0.wkind == FORGE_W_Q4 ? (a0.K / 128) * 8 * 4 : 0;
+    const int xs_row = ((a0.K + 31) / 32) * 32 * 2;  // K padded to whole k-tile pairs
+    int max_cols = (kMaxSmem - kFixedSmem - sx_bytes) / xs_row;
     if (max_cols > 8) max_cols = 8;
     const int per_launch = max_cols / cols_per_seq;
     if (per_launch < 1) return forge_fail(-1, "gemv: K=%d too large for the staged activation", a0.K);
@@ -396,7 +517,7 @@ int forge_gemv_launch(const ForgeGemvArgs& a0, cudaStream_t stream, bool pdl) {
         if (a.y) a.y = a0.y + (size_t)b0 * a0.y_stride;
         if (a.q_out) a.q_out = a0.q_out + (size_t)b0 * a0.H * a0.hd;
         if (a.s_out) a.s_out = a0.s_out + (size_t)b0 * a0.F;
-        const int smem = kFixedSmem + a.batch * cols_per_seq * xs_row;
+        const int smem = kFixedSmem + sx_bytes + a.batch * cols_per_seq * xs_row;
         int rc;
         const bool p = pdl && b0 == 0;
         if (a.wkind == FORGE_W_Q4)

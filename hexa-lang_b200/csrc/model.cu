@@ -636,13 +636,7 @@ FORGE_API int64_t forge_b200_step_bytes(ForgeB200* h, int batch, int ctx_len) {
 FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
     if (!h || batch <= 0) return -1;
     const bool split = h->split_for(batch);
-    auto launches = [&](int K) {
-        const int xs_row = (K + 8) * 2;
-        int max_cols = (227 * 1024 - (6 * (8192 + 256) + 96 + 8 * 16 * 8 * 4)) / xs_row;
-        if (max_cols > 8) max_cols = 8;
-        const int per = max_cols / (split ? 2 : 1);
-        return (batch + per - 1) / per;
-    };
+    auto launches = [&](int K) { return forge_gemv_launch_count(K, batch, split); };
     int per_layer = launches(h->d) * 2 + launches(h->qd) + launches(h->F) + 1;
     return 1 + h->L * per_layer + launches(h->d) + 1;
 }

@@ -61,7 +61,15 @@ def test_decode_steps_match_oracle(forge, oracle, cuda, name, batch):
     kc, vc = om.new_cache(batch, lmax)
     rng = np.random.default_rng(5678 + batch)
     flags = oracle.OR_KV_BF16 | (oracle.OR_ACT_BF16 if act_bf16 else 0)
-    tol = 1e-3 if not act_bf16 else 2e-3
+    # The device rounds K/V (and, in bf16-activation mode, GEMV inputs) to
+    # bf16 from fp32 values that differ from the oracle's f64 values in the
+    # last bits; values sitting on a rounding tie then round one bf16 ulp
+    # apart, which moves logits by up to a few 1e-3 (logit std ~0.3-0.45).
+    # Bounds: max |dlogit| 5e-3 exact-activation mode, 1e-2 bf16 mode — both
+    # inside the 2e-2 (bf16) / 5e-2 (int4) gates — and a median below 2e-4
+    # (exact activations) or 1e-3 (bf16 activations).
+    tol = 5e-3 if not act_bf16 else 1e-2
+    med_tol = 2e-4 if not act_bf16 else 1e-3
     fm.reset()
     worst = 0.0
     for p in range(20):
@@ -71,6 +79,7 @@ def test_decode_steps_match_oracle(forge, oracle, cuda, name, batch):
         err = np.abs(lg - ref_lg).max()
         worst = max(worst, err)
         assert err < tol, f"step {p}: max |dlogit| {err}"
+        assert np.median(np.abs(lg - ref_lg)) < med_tol
         for b in range(batch):
             top2 = np.sort(ref_lg[b])[-2:]
             if top2[1] - top2[0] > 10 * tol:
