@@ -55,6 +55,16 @@ FORGE_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
                  : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
+// Non-blocking probe of a phase (never suspends the thread) — for a
+// thread that must keep doing other work (issuing copies) while it polls.
+FORGE_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
 // Waits for the phase with the given parity to complete. Returns false (and
 // raises the device error flag) when the spin budget runs out.
 FORGE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {

@@ -18,7 +18,7 @@ int forge_sm_count();
 
 // ------------------------------------------------------------ GEMV launch
 enum { FORGE_W_BF16 = 0, FORGE_W_Q4 = 1 };
-enum { FORGE_PRO_PLAIN = 0, FORGE_PRO_RMSNORM = 1 };
+enum { FORGE_PRO_PLAIN = 0, FORGE_PRO_RMSNORM = 1, FORGE_PRO_EMBED_RMSNORM = 2 };
 enum {
     FORGE_EPI_STORE = 0,  // y[b][row] = W x
     FORGE_EPI_RESID = 1,  // y[b][row] += W x   (residual stream, in place)
@@ -40,6 +40,8 @@ struct ForgeGemvArgs {
     int32_t pro;           // FORGE_PRO_*
     const float* gain;     // RMSNorm gain [K]
     float eps;
+    const uint16_t* emb;   // EMBED prologue: embedding table [V][K] bf16
+    const int32_t* emb_tok;// EMBED prologue: token per sequence (global index)
     int32_t epi;           // FORGE_EPI_*
     float* y;              // STORE/RESID/LOGITS output [batch][y_stride]
     int32_t y_stride;
@@ -90,3 +92,31 @@ int forge_embed_launch(const uint16_t* emb, int d, int vocab, const int32_t* tok
 int forge_argmax_finalize_launch(unsigned long long* keys, int B, int32_t* tok_out,
                                  int32_t* hist, int32_t* step_counter, int32_t* pos, int hist_cap,
                                  cudaStream_t stream, bool pdl);
+
+// ------------------------------------------------- persistent decode step
+enum { FORGE_PH_GEMV = 0, FORGE_PH_ATTN = 1, FORGE_PH_FIN = 2 };
+struct ForgePhase {
+    int32_t type;          // FORGE_PH_*
+    ForgeGemvArgs g;       // GEMV: full description; ATTN: g.kc / g.vc layer caches
+};
+struct ForgeStepArgs {
+    const ForgePhase* phases;  // device array
+    int32_t nphases;
+    int32_t grid, stages;
+    int32_t B, H, Hkv, hd, lmax, nsplit;
+    const float* q;
+    float* ctx;
+    int32_t* pos;
+    float* partial;
+    uint32_t* counters;
+    unsigned long long* amax;
+    int32_t *tok, *hist, *step;
+    int32_t hist_cap;
+    unsigned long long* bar;   // monotonic grid-barrier counter
+    uint32_t* epoch;           // completed fused steps since the last reset
+    uint32_t* err;
+    unsigned long long* trace; // optional [grid][nphases][4] %globaltimer stamps
+};
+// 0 launched (or fits, with probe_only), 1 does not fit / unsupported, -1 error.
+int forge_step_launch(const ForgeStepArgs& sa, int xf_bytes, cudaStream_t stream, bool probe_only);
+int forge_step_attn_tile(int hd);

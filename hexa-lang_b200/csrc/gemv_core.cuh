@@ -1,0 +1,176 @@
+// gemv_core.cuh — device pieces shared by the standalone decode GEMV kernel
+// and the persistent decode-step kernel: activation staging in mma fragment
+// order (with RMSNorm and the hi/lo bf16 split), the fused epilogues, and
+// the int4 dequantisation.
+#pragma once
+#include "common.cuh"
+#include "forge_internal.h"
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t row) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - row);
+}
+
+// Shared-memory B operand in mma fragment order: for every pair of k-tiles
+// kp and column c, the 4 lanes t = 0..3 each own 16 bytes holding
+// {b0, b1} of k-tile 2kp and {b0, b1} of k-tile 2kp+1, so one LDS.128 per
+// lane feeds two mma steps. Columns are (sequence, hi|lo) in exact mode.
+__device__ __forceinline__ int xf_index(int k, int col, int ncols) {
+    const int kt = k >> 4, kk = k & 15;
+    const int kp = kt >> 1, which = kt & 1, t = (kk & 7) >> 1, half = kk >> 3, e = kk & 1;
+    return (((kp * ncols + col) * 4 + t) * 8) + which * 4 + half * 2 + e;
+}
+
+// Activation row loads. Activations are written by other CTAs earlier in
+// the same persistent kernel, so they bypass L1 (ld.global.cg). EMBED reads
+// the sequence's embedding row (bf16) instead of the residual stream.
+template <int PRO>
+__device__ __forceinline__ float4 load_x4(const ForgeGemvArgs& a, int b, const float* xb, int k) {
+    if (PRO == FORGE_PRO_EMBED_RMSNORM) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(a.emb + (size_t)a.emb_tok[a.b0 + b] * a.K + k));
+        return make_float4(bf16_lo_f32(v.x), bf16_hi_f32(v.x), bf16_lo_f32(v.y), bf16_hi_f32(v.y));
+    }
+    return __ldcg(reinterpret_cast<const float4*>(xb + k));
+}
+
+// Prologue (consumer warps): optional RMSNorm, hi/lo split, fragment-order
+// store, and (int4) per-group column sums of the bf16 operand for the
+// dequantisation-bias correction.
+template <int WK, int PRO, int NT>
+__device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, float* sx, float* red) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = a.K;
+    const int ncols = a.split ? 2 * a.batch : a.batch;
+    for (int b = 0; b < a.batch; ++b) {
+        const float* xb = a.x + (size_t)b * a.x_stride;
+        float inv = 1.0f;
+        if (PRO != FORGE_PRO_PLAIN) {
+            float ss = 0.0f;
+            for (int k = tid * 4; k < K; k += NT * 4) {
+                const float4 v = load_x4<PRO>(a, b, xb, k);
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) red[warp] = ss;
+            named_bar_sync(1, NT);
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NT / 32; ++w) tot += red[w];
+            inv = 1.0f / sqrtf(tot / (float)K + a.eps);
+            named_bar_sync(1, NT);
+        }
+        // 4 consecutive k per thread; a warp covers one 128-group per pass
+        for (int k = tid * 4; k < K; k += NT * 4) {
+            const float4 v = load_x4<PRO>(a, b, xb, k);
+            float e[4] = {v.x, v.y, v.z, v.w};
+            if (PRO != FORGE_PRO_PLAIN) {
+                float4 gv = *reinterpret_cast<const float4*>(a.gain + k);
+                e[0] = gv.x * (e[0] * inv); e[1] = gv.y * (e[1] * inv);
+                e[2] = gv.z * (e[2] * inv); e[3] = gv.w * (e[3] * inv);
+            }
+            uint16_t hi[4], lo[4];
+            float shi = 0.f, slo = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (a.split) split_bf16(e[i], hi[i], lo[i]);
+                else { hi[i] = f32_to_bf16_bits(e[i]); lo[i] = 0; }
+                shi += bf16_bits_to_f32(hi[i]);
+                slo += bf16_bits_to_f32(lo[i]);
+            }
+            const int ch = a.split ? 2 * b : b;
+            *reinterpret_cast<uint32_t*>(xf + xf_index(k, ch, ncols)) = hi[0] | ((uint32_t)hi[1] << 16);
+            *reinterpret_cast<uint32_t*>(xf + xf_index(k + 2, ch, ncols)) = hi[2] | ((uint32_t)hi[3] << 16);
+            if (a.split) {
+                *reinterpret_cast<uint32_t*>(xf + xf_index(k, ch + 1, ncols)) = lo[0] | ((uint32_t)lo[1] << 16);
+                *reinterpret_cast<uint32_t*>(xf + xf_index(k + 2, ch + 1, ncols)) = lo[2] | ((uint32_t)lo[3] << 16);
+            }
+            if (WK == FORGE_W_Q4) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    shi += __shfl_xor_sync(0xffffffffu, shi, o);
+                    slo += __shfl_xor_sync(0xffffffffu, slo, o);
+                }
+                if (lane == 0) {
+                    sx[(k >> 7) * 8 + ch] = shi;
+                    if (a.split) sx[(k >> 7) * 8 + ch + 1] = slo;
+                }
+            }
+        }
+    }
+}
+
+// When K/16 is odd the last k-tile pair is half padding: zero it so the
+// padded mma step multiplies by exact zeros.
+template <int NT>
+__device__ __forceinline__ void zero_x_pad(const ForgeGemvArgs& a, uint16_t* xf) {
+    const int K = a.K;
+    if ((K & 31) == 0) return;
+    const int ncols = a.split ? 2 * a.batch : a.batch;
+    for (int i = threadIdx.x; i < ncols * 16; i += NT) {
+        const int col = i >> 4, k = K + (i & 15);
+        xf[xf_index(k, col, ncols)] = 0;
+    }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue(const ForgeGemvArgs& a, int u, int p, int b, float ylo, float yhi,
+                                         unsigned long long& best) {
+    const int row0 = u * 16;
+    if (EPI == FORGE_EPI_STORE) {
+        a.y[(size_t)b * a.y_stride + row0 + p] = ylo;
+        a.y[(size_t)b * a.y_stride + row0 + p + 8] = yhi;
+    } else if (EPI == FORGE_EPI_RESID) {
+        a.y[(size_t)b * a.y_stride + row0 + p] += ylo;
+        a.y[(size_t)b * a.y_stride + row0 + p + 8] += yhi;
+    } else if (EPI == FORGE_EPI_LOGITS) {
+        a.y[(size_t)b * a.y_stride + row0 + p] = ylo;
+        a.y[(size_t)b * a.y_stride + row0 + p + 8] = yhi;
+        if (row0 + p < a.nvalid) { unsigned long long k = argmax_key(ylo, row0 + p); best = k > best ? k : best; }
+        if (row0 + p + 8 < a.nvalid) { unsigned long long k = argmax_key(yhi, row0 + p + 8); best = k > best ? k : best; }
+    } else if (EPI == FORGE_EPI_SWIGLU) {
+        // physical tile u = gate rows 8u..8u+7 (rows 0-7), up rows 8u..8u+7 (rows 8-15)
+        const float gte = ylo, upv = yhi;
+        const float sl = gte / (1.0f + expf(-gte));
+        a.s_out[(size_t)b * a.F + 8 * u + p] = sl * upv;
+    } else if (EPI == FORGE_EPI_QKV) {
+        const int hd = a.hd, head = row0 / hd, i = (row0 % hd) >> 4;
+        const int c = 8 * i + p, c2 = c + hd / 2;
+        const int bg = a.b0 + b;
+        const int P = a.pos[bg];
+        if (P < 0 || P >= a.lmax) { atomicOr(a.err, FORGE_DEVERR_BAD_INDEX); return; }
+        if (head < a.H + a.Hkv) {
+            const float cs = a.rope_cos[(size_t)P * (hd / 2) + c];
+            const float sn = a.rope_sin[(size_t)P * (hd / 2) + c];
+            const float o1 = ylo * cs - yhi * sn;
+            const float o2 = yhi * cs + ylo * sn;
+            if (head < a.H) {
+                float* q = a.q_out + (size_t)b * a.H * hd + (size_t)head * hd;
+                q[c] = o1;
+                q[c2] = o2;
+            } else {
+                uint16_t* k = a.kc + (((size_t)bg * a.Hkv + (head - a.H)) * a.lmax + P) * hd;
+                k[c] = f32_to_bf16_bits(o1);
+                k[c2] = f32_to_bf16_bits(o2);
+            }
+        } else {
+            uint16_t* v = a.vc + (((size_t)bg * a.Hkv + (head - a.H - a.Hkv)) * a.lmax + P) * hd;
+            v[c] = f32_to_bf16_bits(ylo);
+            v[c2] = f32_to_bf16_bits(yhi);
+        }
+    }
+}
+
+// A values of the int4 path are 135 + q (0x4300 | code), so a group's
+// accumulator carries 135 * sum(B) extra; it is removed per group from the
+// precomputed column sums. The raw A values are exact in bf16 and every
+// product is exact in fp32.
+__device__ __forceinline__ void dequant_q4_biased(uint32_t w, uint32_t (&a)[4]) {
+    const uint32_t mask = 0x000F000Fu, magic = 0x43004300u;
+    a[0] = lop3_and_or(w, mask, magic);
+    a[1] = lop3_and_or(w >> 4, mask, magic);
+    a[2] = lop3_and_or(w >> 8, mask, magic);
+    a[3] = lop3_and_or(w >> 12, mask, magic);
+}
+

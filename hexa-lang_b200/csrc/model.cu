@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <vector>
@@ -100,6 +101,13 @@ struct ForgeB200 {
     uint16_t* scales = nullptr;
     int32_t* h_tok = nullptr;  // pinned staging [Bmax]
     std::map<int, cudaGraphExec_t> graphs;
+    std::map<int, ForgeStepArgs> fused;   // per batch size: fused-step arguments (phases on device)
+    std::map<int, int> fused_ok;          // per batch size: 1 fused path fits, 0 no
+    unsigned long long* bar = nullptr;
+    uint32_t* epoch = nullptr;
+    int force_graph = 0;
+    unsigned long long* trace = nullptr;  // fused-step timeline (FORGE_STEP_TRACE)
+    int trace_n = 0;
     std::vector<void*> allocs;
     bool weights_ready = false;
 
@@ -269,6 +277,117 @@ int enqueue_step(ForgeB200* h, int B) {
     return forge_argmax_finalize_launch(h->amax, B, h->tok, h->hist, h->step, h->pos, h->hist_cap, st, true);
 }
 
+// Context splits per (sequence, KV head) for the fused step: CTA work items
+// are spread over the SMs in as few, as full waves as possible, with at least
+// ~64 keys per item at full context (4 per consumer warp).
+int fused_splits(const ForgeB200* h, int B) {
+    const int grid = forge_sm_count();
+    const int pairs = B * h->Hkv;
+    int cap = h->lmax / 64;
+    if (cap < 1) cap = 1;
+    int best = 1;
+    double best_score = -1e9;
+    for (int ns = 1; ns <= cap; ++ns) {
+        const int items = pairs * ns;
+        const int waves = (items + grid - 1) / grid;
+        const double eff = (double)items / ((double)waves * grid);
+        const double score = eff - 0.02 * waves;
+        if (score > best_score + 1e-9) { best_score = score; best = ns; }
+    }
+    return best;
+}
+
+// Builds (once per batch size) the phase list of the fused step and checks
+// that it fits one CTA per SM. Returns the args or nullptr.
+const ForgeStepArgs* fused_for(ForgeB200* h, int B) {
+    if (h->force_graph) return nullptr;
+    auto ok = h->fused_ok.find(B);
+    if (ok != h->fused_ok.end() && !ok->second) return nullptr;
+    auto it = h->fused.find(B);
+    if (it != h->fused.end()) return &it->second;
+    const bool split = h->split_for(B);
+    std::vector<ForgePhase> ph;
+    ForgeGemvArgs a{};
+    a.wkind = h->q4 ? FORGE_W_Q4 : FORGE_W_BF16;
+    a.batch = B; a.split = split; a.err = h->err; a.eps = h->desc.rms_eps;
+    a.H = h->H; a.Hkv = h->Hkv; a.hd = h->hd; a.lmax = h->lmax; a.pos = h->pos;
+    a.rope_cos = h->rope_cos; a.rope_sin = h->rope_sin; a.emb = h->emb; a.emb_tok = h->tok;
+    int kmax = 0;
+    for (int l = 0; l < h->L; ++l) {
+        const LayerDev& Ld = h->layers[l];
+        uint16_t* kc = h->kc + (size_t)l * h->kv_layer;
+        uint16_t* vc = h->vc + (size_t)l * h->kv_layer;
+        ForgePhase p{};
+        p.type = FORGE_PH_GEMV; p.g = a;
+        p.g.w = Ld.qkv_w; p.g.s = Ld.qkv_s; p.g.N = h->nqkv; p.g.K = h->d; p.g.x = h->x; p.g.x_stride = h->d;
+        p.g.pro = l == 0 ? FORGE_PRO_EMBED_RMSNORM : FORGE_PRO_RMSNORM; p.g.gain = Ld.g1;
+        p.g.epi = FORGE_EPI_QKV; p.g.q_out = h->q; p.g.kc = kc; p.g.vc = vc; p.g.y = h->x; p.g.y_stride = h->d;
+        ph.push_back(p);
+        ForgePhase at{};
+        at.type = FORGE_PH_ATTN; at.g = a; at.g.kc = kc; at.g.vc = vc;
+        ph.push_back(at);
+        p = ForgePhase{}; p.type = FORGE_PH_GEMV; p.g = a;
+        p.g.w = Ld.o_w; p.g.s = Ld.o_s; p.g.N = h->d; p.g.K = h->qd; p.g.x = h->ctx; p.g.x_stride = h->qd;
+        p.g.pro = FORGE_PRO_PLAIN; p.g.epi = FORGE_EPI_RESID; p.g.y = h->x; p.g.y_stride = h->d;
+        ph.push_back(p);
+        p = ForgePhase{}; p.type = FORGE_PH_GEMV; p.g = a;
+        p.g.w = Ld.gu_w; p.g.s = Ld.gu_s; p.g.N = 2 * h->F; p.g.K = h->d; p.g.x = h->x; p.g.x_stride = h->d;
+        p.g.pro = FORGE_PRO_RMSNORM; p.g.gain = Ld.g2; p.g.epi = FORGE_EPI_SWIGLU; p.g.s_out = h->s; p.g.F = h->F;
+        ph.push_back(p);
+        p = ForgePhase{}; p.type = FORGE_PH_GEMV; p.g = a;
+        p.g.w = Ld.dn_w; p.g.s = Ld.dn_s; p.g.N = h->d; p.g.K = h->F; p.g.x = h->s; p.g.x_stride = h->F;
+        p.g.pro = FORGE_PRO_PLAIN; p.g.epi = FORGE_EPI_RESID; p.g.y = h->x; p.g.y_stride = h->d;
+        ph.push_back(p);
+    }
+    ForgePhase hp{};
+    hp.type = FORGE_PH_GEMV; hp.g = a; hp.g.wkind = FORGE_W_BF16;
+    hp.g.w = h->head_w; hp.g.s = nullptr; hp.g.N = h->Vpad; hp.g.K = h->d; hp.g.x = h->x; hp.g.x_stride = h->d;
+    hp.g.pro = FORGE_PRO_RMSNORM; hp.g.gain = h->gF; hp.g.epi = FORGE_EPI_LOGITS; hp.g.y = h->logits;
+    hp.g.y_stride = h->Vpad; hp.g.argmax_key = h->amax; hp.g.nvalid = h->V;
+    ph.push_back(hp);
+    ForgePhase fin{};
+    fin.type = FORGE_PH_FIN;
+    ph.push_back(fin);
+    for (const auto& p : ph)
+        if (p.type == FORGE_PH_GEMV) kmax = std::max(kmax, p.g.K);
+    const int ncols = split ? 2 * B : B;
+    const int xf_bytes = ncols * ((kmax + 31) / 32) * 32 * 2;
+    ForgeStepArgs sa{};
+    sa.nphases = (int)ph.size();
+    sa.grid = forge_sm_count();
+    sa.B = B; sa.H = h->H; sa.Hkv = h->Hkv; sa.hd = h->hd; sa.lmax = h->lmax; sa.nsplit = fused_splits(h, B);
+    sa.q = h->q; sa.ctx = h->ctx; sa.pos = h->pos; sa.partial = h->partial; sa.counters = h->counters;
+    sa.amax = h->amax; sa.tok = h->tok; sa.hist = h->hist; sa.step = h->step; sa.hist_cap = h->hist_cap;
+    sa.bar = h->bar; sa.epoch = h->epoch; sa.err = h->err;
+    if (getenv("FORGE_STEP_TRACE")) {
+        sa.trace = (unsigned long long*)h->alloc(sizeof(unsigned long long) * 4 * ph.size() * sa.grid);
+        if (sa.trace) cudaMemset(sa.trace, 0, sizeof(unsigned long long) * 4 * ph.size() * sa.grid);
+        h->trace = sa.trace;
+        h->trace_n = (int)ph.size();
+    }
+    const bool need_q4_fit = h->q4 && kmax / 128 > 128;
+    int fits = need_q4_fit ? 1 : forge_step_launch(sa, xf_bytes, h->stream, true);
+    if (fits != 0) {
+        if (getenv("FORGE_VERBOSE")) fprintf(stderr, "[forge_b200] batch %d: fused step does not fit, using the multi-kernel graph\n", B);
+        h->fused_ok[B] = 0;
+        return nullptr;
+    }
+    ForgePhase* dph = (ForgePhase*)h->alloc(sizeof(ForgePhase) * ph.size());
+    if (!dph || cudaMemcpy(dph, ph.data(), sizeof(ForgePhase) * ph.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+        h->fused_ok[B] = 0;
+        return nullptr;
+    }
+    sa.phases = dph;
+    sa.stages = xf_bytes;  // carried to the launcher (which picks the stage count)
+    h->fused_ok[B] = 1;
+    h->fused[B] = sa;
+    return &h->fused[B];
+}
+
+int launch_fused(ForgeB200* h, const ForgeStepArgs* sa) {
+    return forge_step_launch(*sa, sa->stages, h->stream, false) ? -1 : 0;
+}
+
 cudaGraphExec_t graph_for(ForgeB200* h, int B) {
     auto it = h->graphs.find(B);
     if (it != h->graphs.end()) return it->second;
@@ -414,7 +533,19 @@ FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB20
         int ns = forge_attn_pick_splits(B, h->Hkv, h->lmax);
         if (ns * B > max_split) max_split = ns * B;
     }
+    for (int B = 1; B <= h->Bmax; ++B) {
+        int ns = fused_splits(h, B);
+        if (ns * B > max_split) max_split = ns * B;
+    }
     h->partial = (float*)h->alloc(sizeof(float) * (size_t)max_split * h->H * (h->hd + 2));
+    h->bar = (unsigned long long*)h->alloc(16);
+    h->epoch = (uint32_t*)h->alloc(16);
+    {
+        // default: captured multi-kernel graph; FORGE_DECODE_PATH=fused selects
+        // the persistent single-kernel step
+        const char* e = getenv("FORGE_DECODE_PATH");
+        h->force_graph = (e && strcmp(e, "fused") == 0) ? 0 : 1;
+    }
     h->counters = (uint32_t*)h->alloc(4 * (size_t)h->Bmax * h->Hkv);
     h->err = (uint32_t*)h->alloc(16);
     size_t st = std::max({(size_t)h->nqkv * d, (size_t)2 * h->F * d, (size_t)d * h->F, (size_t)d * h->qd,
@@ -424,7 +555,7 @@ FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB20
     h->codes = (uint8_t*)h->alloc(st / 2);
     h->scales = (uint16_t*)h->alloc(st / 128 * 2 + 16);
     if (rc || !h->emb || !h->head_w || !h->kc || !h->vc || !h->stA || !h->stB || !h->codes || !h->partial ||
-        !h->hist || !h->logits || !h->scales) {
+        !h->hist || !h->logits || !h->scales || !h->bar || !h->epoch) {
         forge_b200_destroy(h);
         return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: out of device memory");
     }
@@ -446,6 +577,8 @@ FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB20
         cudaMemcpy(h->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
     }
     cudaMemset(h->counters, 0, 4 * (size_t)h->Bmax * h->Hkv);
+    cudaMemset(h->bar, 0, 16);
+    cudaMemset(h->epoch, 0, 16);
     cudaMemset(h->amax, 0, 8 * h->Bmax);
     cudaMemset(h->err, 0, 16);
     cudaMemset(h->step, 0, 16);
@@ -515,6 +648,9 @@ FORGE_API int forge_b200_reset(ForgeB200* h) {
     cudaMemsetAsync(h->pos, 0, 4 * h->Bmax, h->stream);
     cudaMemsetAsync(h->step, 0, 16, h->stream);
     cudaMemsetAsync(h->amax, 0, 8 * h->Bmax, h->stream);
+    cudaMemsetAsync(h->bar, 0, 16, h->stream);
+    cudaMemsetAsync(h->epoch, 0, 16, h->stream);
+    cudaMemsetAsync(h->counters, 0, 4 * (size_t)h->Bmax * h->Hkv, h->stream);
     return cudaStreamSynchronize(h->stream) == cudaSuccess ? 0 : forge_fail(-1, "forge_b200_reset failed");
 }
 
@@ -551,16 +687,23 @@ FORGE_API int forge_b200_get_kv(ForgeB200* h, int layer, int seq, uint16_t* k_ou
     return 0;
 }
 
+// Enqueues one decode step: the fused persistent kernel when it fits, else
+// the captured multi-kernel graph.
+int enqueue_one(ForgeB200* h, int B) {
+    if (const ForgeStepArgs* sa = fused_for(h, B)) return launch_fused(h, sa);
+    cudaGraphExec_t g = graph_for(h, B);
+    if (!g) return -1;
+    return cudaGraphLaunch(g, h->stream) == cudaSuccess ? 0 : forge_fail(-1, "forge_b200: graph launch failed");
+}
+
 FORGE_API int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tokens, int32_t* next_tokens, float* logits) {
     if (int rc = check_ready(h, batch)) return rc;
     if (!tokens) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_decode_step: null tokens");
-    cudaGraphExec_t g = graph_for(h, batch);
-    if (!g) return -1;
     int32_t* stage = h->h_tok;
     if (!stage) return forge_fail(-1, "forge_b200_decode_step: no pinned staging buffer");
     memcpy(stage, tokens, 4 * batch);
     cudaMemcpyAsync(h->tok, stage, 4 * batch, cudaMemcpyHostToDevice, h->stream);
-    if (cudaGraphLaunch(g, h->stream) != cudaSuccess) return forge_fail(-1, "forge_b200_decode_step: graph launch failed");
+    if (enqueue_one(h, batch)) return -1;
     if (next_tokens) cudaMemcpyAsync(stage, h->tok, 4 * batch, cudaMemcpyDeviceToHost, h->stream);
     if (logits)
         cudaMemcpy2DAsync(logits, sizeof(float) * h->V, h->logits, sizeof(float) * h->Vpad, sizeof(float) * h->V,
@@ -573,10 +716,8 @@ FORGE_API int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tok
 
 FORGE_API int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps) {
     if (int rc = check_ready(h, batch)) return rc;
-    cudaGraphExec_t g = graph_for(h, batch);
-    if (!g) return -1;
     for (int i = 0; i < n_steps; ++i)
-        if (cudaGraphLaunch(g, h->stream) != cudaSuccess) return forge_fail(-1, "forge_b200_decode_device: graph launch failed");
+        if (enqueue_one(h, batch)) return -1;
     return 0;
 }
 
@@ -585,8 +726,6 @@ FORGE_API int forge_b200_generate(ForgeB200* h, int batch, const int32_t* prompt
     if (!prompt || !out || n_prompt <= 0 || n_gen <= 0 || n_prompt + n_gen - 1 > h->lmax)
         return forge_fail(FORGE_INVALID_ARGS, "forge_b200_generate: bad prompt/generation length");
     if (forge_b200_reset(h)) return -1;
-    cudaGraphExec_t g = graph_for(h, batch);
-    if (!g) return -1;
     std::vector<int32_t> col(batch);
     int32_t* pin = nullptr;
     if (cudaHostAlloc((void**)&pin, 4 * (size_t)batch * n_prompt, cudaHostAllocDefault) != cudaSuccess)
@@ -596,10 +735,9 @@ FORGE_API int forge_b200_generate(ForgeB200* h, int batch, const int32_t* prompt
     int rc = 0;
     for (int p = 0; p < n_prompt && !rc; ++p) {
         cudaMemcpyAsync(h->tok, pin + (size_t)p * batch, 4 * batch, cudaMemcpyHostToDevice, h->stream);
-        if (cudaGraphLaunch(g, h->stream) != cudaSuccess) rc = forge_fail(-1, "forge_b200_generate: launch failed");
+        rc = enqueue_one(h, batch);
     }
-    for (int i = 1; i < n_gen && !rc; ++i)
-        if (cudaGraphLaunch(g, h->stream) != cudaSuccess) rc = forge_fail(-1, "forge_b200_generate: launch failed");
+    for (int i = 1; i < n_gen && !rc; ++i) rc = enqueue_one(h, batch);
     if (cudaStreamSynchronize(h->stream) != cudaSuccess)
         rc = forge_fail(-1, "forge_b200_generate: %s", cudaGetErrorString(cudaGetLastError()));
     cudaFreeHost(pin);
@@ -622,6 +760,23 @@ FORGE_API int forge_b200_sync(ForgeB200* h) {
     return read_err(h);
 }
 
+// 1 when decode steps at this batch size run as the single fused kernel.
+FORGE_API int forge_b200_uses_fused_step(ForgeB200* h, int batch) {
+    if (!h || batch <= 0 || batch > h->Bmax) return -1;
+    cudaSetDevice(h->device);
+    return fused_for(h, batch) ? 1 : 0;
+}
+
+// Copies the last fused step's timeline: [grid][nphases][4] globaltimer ns
+// (phase entry, barrier passed, -, phase done). Returns nphases or -1.
+FORGE_API int forge_b200_step_trace(ForgeB200* h, unsigned long long* out, int cap) {
+    if (!h || !h->trace) return -1;
+    const size_t n = (size_t)4 * h->trace_n * forge_sm_count();
+    if ((size_t)cap < n) return -1;
+    if (cudaMemcpy(out, h->trace, n * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    return h->trace_n;
+}
+
 FORGE_API int64_t forge_b200_step_bytes(ForgeB200* h, int batch, int ctx_len) {
     if (!h) return -1;
     const bool q4 = h->q4;
@@ -635,6 +790,7 @@ FORGE_API int64_t forge_b200_step_bytes(ForgeB200* h, int batch, int ctx_len) {
 
 FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
     if (!h || batch <= 0) return -1;
+    if (fused_for(h, batch)) return 1;
     const bool split = h->split_for(batch);
     auto launches = [&](int K) { return forge_gemv_launch_count(K, batch, split); };
     int per_layer = launches(h->d) * 2 + launches(h->qd) + launches(h->F) + 1;

@@ -82,6 +82,8 @@ def lib() -> C.CDLL:
             "forge_b200_sync": (i32, [vp]),
             "forge_b200_step_bytes": (i64, [vp, i32, i32]),
             "forge_b200_launches_per_step": (i32, [vp, i32]),
+            "forge_b200_step_trace": (i32, [vp, vp, i32]),
+            "forge_b200_uses_fused_step": (i32, [vp, i32]),
             "forge_gemv_w4a16_g128": (i32, [vp, vp, i64, i64, vp, i32, vp, i32, vp]),
             "forge_gemv_bf16": (i32, [vp, i64, i64, vp, i32, vp, i32, vp]),
             "forge_flash_decode_workspace_bytes": (i64, [i32, i32, i32, i32, i32]),
@@ -206,6 +208,9 @@ class ForgeModel:
 
     def step_bytes(self, batch, ctx):
         return lib().forge_b200_step_bytes(self.h, batch, ctx)
+
+    def uses_fused_step(self, batch):
+        return lib().forge_b200_uses_fused_step(self.h, batch) == 1
 
     def launches_per_step(self, batch):
         return lib().forge_b200_launches_per_step(self.h, batch)

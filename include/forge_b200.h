@@ -104,6 +104,13 @@ int forge_b200_sync(ForgeB200* h);
 /* Algorithmic HBM bytes of one decode step (weights + scales + head + KV
  * read/write) at the given batch and context length. */
 int64_t forge_b200_step_bytes(ForgeB200* h, int batch, int ctx_len);
+/* Timeline of the last fused step when FORGE_STEP_TRACE is set at handle
+ * creation: [sm][phase][4] %globaltimer ns (entry, barrier passed, -, done).
+ * Returns the phase count, or -1. */
+int forge_b200_step_trace(ForgeB200* h, unsigned long long* out, int cap);
+/* 1 when steps at this batch size run as the single persistent kernel, 0
+ * when they run as the captured multi-kernel graph, -1 on bad arguments. */
+int forge_b200_uses_fused_step(ForgeB200* h, int batch);
 /* Kernel launches per decode step (for the bench's launch count). */
 int forge_b200_launches_per_step(ForgeB200* h, int batch);
 
