@@ -139,6 +139,23 @@ FORGE_DEV void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0
           "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
 }
 
+// mma.sync m16n8k32 u8 (A, codes) x s8 (B, activations) -> s32, exact.
+FORGE_DEV void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Unpacks the two words of one 16x32 int4 k-tile (layout.cuh) into the four
+// u8 A-fragment registers: low nibbles are rows g, high nibbles rows g+8.
+FORGE_DEV void dequant_q4_u8(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
+    a[0] = w0 & 0x0F0F0F0Fu;
+    a[1] = (w0 >> 4) & 0x0F0F0F0Fu;
+    a[2] = w1 & 0x0F0F0F0Fu;
+    a[3] = (w1 >> 4) & 0x0F0F0F0Fu;
+}
+
 // Dequantises one packed int4 word (8 codes, code = q + 7) into the four
 // bf16x2 A-fragment registers of a 16x16 tile. Nibble j and j+4 land in the
 // low/high halves of register j; 0x4300|n is the bf16 value 128+n, and

@@ -39,7 +39,8 @@ constexpr int kPiece = 16384;         // weight bytes per ring stage
 constexpr int kPieceS = 512;          // int4 scale bytes per ring stage
 constexpr int kStage = kPiece + kPieceS;
 constexpr int kRedSlot = kCW * 16 * 8;
-constexpr int kSxFloats = 128 * 8;    // K <= 16384 for int4 phases
+constexpr int kMaxGroups = 128;       // K <= 16384 for int4 phases
+constexpr int kSxFloats = kMaxGroups * 12;  // [G][4] scales + [G][8] column sums
 constexpr int kProdBytes = 128;
 constexpr int kPhaseBytes = (int)((sizeof(ForgePhase) + 15) / 16 * 16);
 
@@ -236,8 +237,15 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
     const int nitems = (KT + kItemKT - 1) / kItemKT;
     const int units = a.N >> 4;
 
-    stage_x<WK, PRO, kNT>(a, m.xf, m.sx, m.red);
-    zero_x_pad<kNT>(a, m.xf);
+    float* sxf = m.sx;
+    int* ssum = reinterpret_cast<int*>(m.sx + kMaxGroups * 4);
+    uint8_t* xq = reinterpret_cast<uint8_t*>(m.xf);
+    if (WK == FORGE_W_Q4) {
+        stage_x_q8<PRO, kNT>(a, xq, sxf, ssum, m.red);
+    } else {
+        stage_x<PRO, kNT>(a, m.xf, m.red);
+        zero_x_pad<kNT>(a, m.xf);
+    }
     if (PRO == FORGE_PRO_EMBED_RMSNORM && blockIdx.x == 0) {
         // the residual stream starts as the embedding row (written once)
         for (int b = 0; b < a.batch; ++b)
@@ -250,12 +258,11 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
     named_bar_sync(1, kNT);
 
     const int g = lane >> 2, t = lane & 3;
-    const int ncols = a.split ? 2 * a.batch : a.batch;
+    const int ncols = (WK == FORGE_W_Q4 || a.split) ? 2 * a.batch : a.batch;
     const int col = g < ncols ? g : ncols - 1;
-    const int c0 = min(2 * t, ncols - 1), c1 = min(2 * t + 1, ncols - 1);
-    const size_t pstride = (size_t)ncols * 4;
+    const int rc = (WK == FORGE_W_Q4) ? a.batch : ncols;  // reduction columns per row
     unsigned long long best = 0ull;
-    const int slot_floats = kCW * 16 * ncols;
+    const int slot_floats = kCW * 16 * rc;
     int R = 4096 / (2 * slot_floats);
     R = R < 1 ? 1 : (R > 8 ? 8 : R);
     int ui = 0;
@@ -269,31 +276,15 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
             const uint8_t* st = m.ring + (size_t)s * kStage;
             if (WK == FORGE_W_Q4) {
                 const int ng = nkt / 8;
-                if (warp < ng) {  // warp w: group w of the piece (k-tiles 8w .. 8w+7)
+                if (warp < ng) {  // warp w: group w of the piece (int8 tensor-core path)
                     const uint4 w0 = *reinterpret_cast<const uint4*>(st + (2 * warp) * 512 + lane * 16);
                     const uint4 w1 = *reinterpret_cast<const uint4*>(st + (2 * warp + 1) * 512 + lane * 16);
-                    const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                    const int kp = (kt0 + 8 * warp) >> 1;
-                    const uint4* xa = reinterpret_cast<const uint4*>(m.xf) + (size_t)(kp * ncols + col) * 4 + t;
-                    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint4 bb = xa[j * pstride];
-                        uint32_t af[4];
-                        dequant_q4_biased(wd[2 * j], af);
-                        mma_bf16_16816(a0, af, bb.x, bb.y, a0);
-                        dequant_q4_biased(wd[2 * j + 1], af);
-                        mma_bf16_16816(a1, af, bb.z, bb.w, a1);
-                    }
                     const uint16_t* sst = reinterpret_cast<const uint16_t*>(st + kPiece);
                     const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (warp >> 2) * 64 + g * 8 + (warp & 3) * 2);
-                    const int gg = kt0 / 8 + warp;
-                    const float sx0 = m.sx[gg * 8 + c0], sx1 = m.sx[gg * 8 + c1];
-                    const float slo = bf16_lo_f32(sc), shi = bf16_hi_f32(sc);
-                    tot[0] = fmaf(slo, (a0[0] + a1[0]) - 135.f * sx0, tot[0]);
-                    tot[1] = fmaf(slo, (a0[1] + a1[1]) - 135.f * sx1, tot[1]);
-                    tot[2] = fmaf(shi, (a0[2] + a1[2]) - 135.f * sx0, tot[2]);
-                    tot[3] = fmaf(shi, (a0[3] + a1[3]) - 135.f * sx1, tot[3]);
+                    float y0, y1;
+                    q4_group(w0, w1, xq, kt0 / 8 + warp, ncols, col, t, sc, sxf, ssum, a.batch, y0, y1);
+                    tot[0] += y0;
+                    tot[1] += y1;
                 }
             } else {
                 const int ktw = 2 * warp;  // warp w: k-tiles 2w, 2w+1
@@ -317,14 +308,21 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
         // one of two slot groups; one barrier per R units, then the epilogue
         // threads finish those units while the other warps continue
         const int grp = (ui / R) & 1, si = ui % R;
-        float* rw = m.red + ((size_t)(grp * R + si) * kCW + warp) * 16 * ncols;
-        if (2 * t < ncols) {
-            rw[g * ncols + 2 * t] = tot[0] + tot2[0];
-            rw[(g + 8) * ncols + 2 * t] = tot[2] + tot2[2];
-        }
-        if (2 * t + 1 < ncols) {
-            rw[g * ncols + 2 * t + 1] = tot[1] + tot2[1];
-            rw[(g + 8) * ncols + 2 * t + 1] = tot[3] + tot2[3];
+        float* rw = m.red + ((size_t)(grp * R + si) * kCW + warp) * 16 * rc;
+        if (WK == FORGE_W_Q4) {
+            if (t < a.batch) {
+                rw[g * rc + t] = tot[0];
+                rw[(g + 8) * rc + t] = tot[1];
+            }
+        } else {
+            if (2 * t < ncols) {
+                rw[g * rc + 2 * t] = tot[0] + tot2[0];
+                rw[(g + 8) * rc + 2 * t] = tot[2] + tot2[2];
+            }
+            if (2 * t + 1 < ncols) {
+                rw[g * rc + 2 * t + 1] = tot[1] + tot2[1];
+                rw[(g + 8) * rc + 2 * t + 1] = tot[3] + tot2[3];
+            }
         }
         if (si == R - 1 || u + (int)gridDim.x >= units) {
             named_bar_sync(1, kNT);
@@ -333,18 +331,19 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
             const int et = kNT - 1 - (int)threadIdx.x;
             if (et < 8 * a.batch) {
                 const int p = et & 7, b = et >> 3;
-                const int c = a.split ? 2 * b : b;
+                const int c = (WK == FORGE_W_Q4) ? b : (a.split ? 2 * b : b);
+                const bool two = WK != FORGE_W_Q4 && a.split;
                 for (int k = 0; k <= si; ++k) {
                     const int uk = blockIdx.x + (ui - si + k) * (int)gridDim.x;
-                    const float* rs = m.red + (size_t)(grp * R + k) * kCW * 16 * ncols;
+                    const float* rs = m.red + (size_t)(grp * R + k) * kCW * 16 * rc;
                     float ylo = 0.f, yhi = 0.f;
 #pragma unroll
                     for (int w = 0; w < kCW; ++w) {
-                        ylo += rs[(w * 16 + p) * ncols + c];
-                        yhi += rs[(w * 16 + p + 8) * ncols + c];
-                        if (a.split) {
-                            ylo += rs[(w * 16 + p) * ncols + c + 1];
-                            yhi += rs[(w * 16 + p + 8) * ncols + c + 1];
+                        ylo += rs[(w * 16 + p) * rc + c];
+                        yhi += rs[(w * 16 + p + 8) * rc + c];
+                        if (two) {
+                            ylo += rs[(w * 16 + p) * rc + c + 1];
+                            yhi += rs[(w * 16 + p + 8) * rc + c + 1];
                         }
                     }
                     epilogue<EPI>(a, uk, p, b, ylo, yhi, best);

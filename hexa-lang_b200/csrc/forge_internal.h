@@ -66,7 +66,7 @@ struct ForgeGemvArgs {
 // mma column block). pdl: launch with programmatic stream serialization.
 int forge_gemv_launch(const ForgeGemvArgs& a, cudaStream_t stream, bool pdl);
 int forge_gemv_configure();
-int forge_gemv_launch_count(int K, int batch, bool split);
+int forge_gemv_launch_count(int K, int batch, bool split, bool q4);
 
 // ------------------------------------------------------ flash-decode launch
 struct ForgeAttnArgs {

@@ -59,8 +59,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
     uint64_t* empty = full + kStages;
     float* red = reinterpret_cast<float*>(empty + kStages);
-    float* sx = red + kRedFloats;                                   // [G][8] (int4 only)
-    uint16_t* xf = reinterpret_cast<uint16_t*>(sx + (WK == FORGE_W_Q4 ? (a.K / 128) * 8 : 0));
+    // int4: per-group activation scales [G][4] and column sums [G][8], then
+    // the int8 activations; bf16: the bf16 hi/lo activations
+    float* sxf = red + kRedFloats;
+    int* ssum = reinterpret_cast<int*>(sxf + (WK == FORGE_W_Q4 ? (a.K / 128) * 4 : 0));
+    uint16_t* xf = reinterpret_cast<uint16_t*>(ssum + (WK == FORGE_W_Q4 ? (a.K / 128) * 8 : 0));
+    uint8_t* xq = reinterpret_cast<uint8_t*>(xf);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KT = a.K >> 4;
@@ -115,12 +119,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
 
     // ---------------------------------------------------------- consumers
     pdl_wait();
-    stage_x<WK, PRO, 256>(a, xf, sx, red);
-    zero_x_pad<256>(a, xf);
+    if (WK == FORGE_W_Q4) {
+        stage_x_q8<PRO, 256>(a, xq, sxf, ssum, red);
+    } else {
+        stage_x<PRO, 256>(a, xf, red);
+        zero_x_pad<256>(a, xf);
+    }
     named_bar_sync(1, 256);
 
     const int g = lane >> 2, t = lane & 3;
-    const int ncols = a.split ? 2 * a.batch : a.batch;
+    const int ncols = (WK == FORGE_W_Q4 || a.split) ? 2 * a.batch : a.batch;
+    constexpr int RC = (WK == FORGE_W_Q4) ? 4 : 8;  // reduction columns per row
     const int col = g < ncols ? g : ncols - 1;  // unused columns re-read a valid one
     const int c0 = min(2 * t, ncols - 1), c1 = min(2 * t + 1, ncols - 1);
     unsigned long long best = 0ull;
@@ -138,62 +147,29 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
             const int kt0 = i * kItemKT, nkt = min(kItemKT, KT - kt0);
             const uint8_t* st = stages + s * kStageBytes;
             if (WK == FORGE_W_Q4) {
-                // warp w: groups 2w and 2w+1 of this piece (k-tiles 16w .. 16w+15)
+                // warp w: groups 2w and 2w+1 of this piece (int8 tensor-core path)
                 const int ng = nkt / 8;
                 const int gA = 2 * warp;
                 if (gA < ng) {
-                    const bool hasB = gA + 1 < ng;
-                    uint4 wq[4];
-                    wq[0] = *reinterpret_cast<const uint4*>(st + (4 * warp + 0) * 512 + lane * 16);
-                    wq[1] = *reinterpret_cast<const uint4*>(st + (4 * warp + 1) * 512 + lane * 16);
-                    if (hasB) {
-                        wq[2] = *reinterpret_cast<const uint4*>(st + (4 * warp + 2) * 512 + lane * 16);
-                        wq[3] = *reinterpret_cast<const uint4*>(st + (4 * warp + 3) * 512 + lane * 16);
-                    } else {
-                        wq[2] = make_uint4(0, 0, 0, 0); wq[3] = wq[2];
-                    }
-                    const uint32_t wA[8] = {wq[0].x, wq[0].y, wq[0].z, wq[0].w, wq[1].x, wq[1].y, wq[1].z, wq[1].w};
-                    const uint32_t wB[8] = {wq[2].x, wq[2].y, wq[2].z, wq[2].w, wq[3].x, wq[3].y, wq[3].z, wq[3].w};
-                    const int kpA = (kt0 + 16 * warp) >> 1;      // k-tile pair index of group A
-                    const uint4* xa = reinterpret_cast<const uint4*>(xf) + (size_t)(kpA * ncols + col) * 4 + t;
-                    const size_t pstride = (size_t)ncols * 4;    // uint4 per k-tile pair
-                    float aA0[4] = {0.f, 0.f, 0.f, 0.f}, aA1[4] = {0.f, 0.f, 0.f, 0.f};
-                    float aB0[4] = {0.f, 0.f, 0.f, 0.f}, aB1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {  // k-tile pairs of each group
-                        const uint4 bA = xa[j * pstride];
-                        uint32_t af[4];
-                        dequant_q4_biased(wA[2 * j], af);
-                        mma_bf16_16816(aA0, af, bA.x, bA.y, aA0);
-                        dequant_q4_biased(wA[2 * j + 1], af);
-                        mma_bf16_16816(aA1, af, bA.z, bA.w, aA1);
-                        if (hasB) {
-                            const uint4 bB = xa[(j + 4) * pstride];
-                            dequant_q4_biased(wB[2 * j], af);
-                            mma_bf16_16816(aB0, af, bB.x, bB.y, aB0);
-                            dequant_q4_biased(wB[2 * j + 1], af);
-                            mma_bf16_16816(aB1, af, bB.z, bB.w, aB1);
-                        }
-                    }
-                    // scales of rows g / g+8 for groups gA, gA+1 (one 128-byte block per 4 groups)
                     const uint16_t* sst = reinterpret_cast<const uint16_t*>(st + kStageW);
-                    const uint32_t scA = *reinterpret_cast<const uint32_t*>(sst + (gA >> 2) * 64 + g * 8 + (gA & 3) * 2);
-                    const int ggA = kt0 / 8 + gA;               // global group index
-                    const float sxA0 = sx[ggA * 8 + c0], sxA1 = sx[ggA * 8 + c1];
-                    float slo = bf16_lo_f32(scA), shi = bf16_hi_f32(scA);
-                    tot[0] = fmaf(slo, (aA0[0] + aA1[0]) - 135.f * sxA0, tot[0]);
-                    tot[1] = fmaf(slo, (aA0[1] + aA1[1]) - 135.f * sxA1, tot[1]);
-                    tot[2] = fmaf(shi, (aA0[2] + aA1[2]) - 135.f * sxA0, tot[2]);
-                    tot[3] = fmaf(shi, (aA0[3] + aA1[3]) - 135.f * sxA1, tot[3]);
-                    if (hasB) {
+                    const int ggA = kt0 / 8 + gA;
+                    float y0, y1;
+                    {
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(st + (4 * warp + 0) * 512 + lane * 16);
+                        const uint4 w1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 1) * 512 + lane * 16);
+                        const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (gA >> 2) * 64 + g * 8 + (gA & 3) * 2);
+                        q4_group(w0, w1, xq, ggA, ncols, col, t, sc, sxf, ssum, a.batch, y0, y1);
+                        tot[0] += y0;
+                        tot[1] += y1;
+                    }
+                    if (gA + 1 < ng) {
                         const int gB = gA + 1;
-                        const uint32_t scB = *reinterpret_cast<const uint32_t*>(sst + (gB >> 2) * 64 + g * 8 + (gB & 3) * 2);
-                        const float sxB0 = sx[(ggA + 1) * 8 + c0], sxB1 = sx[(ggA + 1) * 8 + c1];
-                        slo = bf16_lo_f32(scB); shi = bf16_hi_f32(scB);
-                        tot2[0] = fmaf(slo, (aB0[0] + aB1[0]) - 135.f * sxB0, tot2[0]);
-                        tot2[1] = fmaf(slo, (aB0[1] + aB1[1]) - 135.f * sxB1, tot2[1]);
-                        tot2[2] = fmaf(shi, (aB0[2] + aB1[2]) - 135.f * sxB0, tot2[2]);
-                        tot2[3] = fmaf(shi, (aB0[3] + aB1[3]) - 135.f * sxB1, tot2[3]);
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(st + (4 * warp + 2) * 512 + lane * 16);
+                        const uint4 w1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 3) * 512 + lane * 16);
+                        const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (gB >> 2) * 64 + g * 8 + (gB & 3) * 2);
+                        q4_group(w0, w1, xq, ggA + 1, ncols, col, t, sc, sxf, ssum, a.batch, y0, y1);
+                        tot2[0] += y0;
+                        tot2[1] += y1;
                     }
                 }
             } else {
@@ -227,25 +203,40 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
         if (!ok) break;
         // cross-warp reduction through one of two slots: one barrier per unit;
         // warps 0-1 run the epilogue while the others start the next unit
-        float* rw = red + (slot * kConsumerWarps + warp) * 16 * 8;
-        rw[g * 8 + 2 * t] = tot[0] + tot2[0];
-        rw[g * 8 + 2 * t + 1] = tot[1] + tot2[1];
-        rw[(g + 8) * 8 + 2 * t] = tot[2] + tot2[2];
-        rw[(g + 8) * 8 + 2 * t + 1] = tot[3] + tot2[3];
+        float* rw = red + (slot * kConsumerWarps + warp) * 16 * RC;
+        if (WK == FORGE_W_Q4) {  // lane (g, t): rows g / g+8 of sequence t
+            if (t < a.batch) {
+                rw[g * RC + t] = tot[0] + tot2[0];
+                rw[(g + 8) * RC + t] = tot[1] + tot2[1];
+            }
+        } else {
+            rw[g * 8 + 2 * t] = tot[0] + tot2[0];
+            rw[g * 8 + 2 * t + 1] = tot[1] + tot2[1];
+            rw[(g + 8) * 8 + 2 * t] = tot[2] + tot2[2];
+            rw[(g + 8) * 8 + 2 * t + 1] = tot[3] + tot2[3];
+        }
         named_bar_sync(1, 256);
         const int tid = threadIdx.x;
         if (tid < 8 * a.batch) {
             const int p = tid & 7, b = tid >> 3;
-            const int c = a.split ? 2 * b : b;
-            const float* rs = red + slot * kConsumerWarps * 16 * 8;
+            const float* rs = red + slot * kConsumerWarps * 16 * RC;
             float ylo = 0.f, yhi = 0.f;
+            if (WK == FORGE_W_Q4) {
 #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) {
-                ylo += rs[(w * 16 + p) * 8 + c];
-                yhi += rs[(w * 16 + p + 8) * 8 + c];
-                if (a.split) {
-                    ylo += rs[(w * 16 + p) * 8 + c + 1];
-                    yhi += rs[(w * 16 + p + 8) * 8 + c + 1];
+                for (int w = 0; w < kConsumerWarps; ++w) {
+                    ylo += rs[(w * 16 + p) * RC + b];
+                    yhi += rs[(w * 16 + p + 8) * RC + b];
+                }
+            } else {
+                const int c = a.split ? 2 * b : b;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; ++w) {
+                    ylo += rs[(w * 16 + p) * 8 + c];
+                    yhi += rs[(w * 16 + p + 8) * 8 + c];
+                    if (a.split) {
+                        ylo += rs[(w * 16 + p) * 8 + c + 1];
+                        yhi += rs[(w * 16 + p + 8) * 8 + c + 1];
+                    }
                 }
             }
             epilogue<EPI>(a, u, p, b, ylo, yhi, best);
@@ -330,10 +321,11 @@ int forge_gemv_configure() {
 }
 
 // Number of launches forge_gemv_launch issues for one call.
-int forge_gemv_launch_count(int K, int batch, bool split) {
-    int max_cols = (kMaxSmem - kFixedSmem - (K / 128) * 32) / (((K + 31) / 32) * 64);
+int forge_gemv_launch_count(int K, int batch, bool split, bool q4) {
+    const int row = q4 ? K : ((K + 31) / 32) * 64;
+    int max_cols = (kMaxSmem - kFixedSmem - (q4 ? (K / 128) * 48 : 0)) / row;
     if (max_cols > 8) max_cols = 8;
-    const int per = max_cols / (split ? 2 : 1);
+    const int per = max_cols / ((split || q4) ? 2 : 1);
     return per > 0 ? (batch + per - 1) / per : 0;
 }
 
@@ -347,10 +339,12 @@ int forge_gemv_launch(const ForgeGemvArgs& a0, cudaStream_t stream, bool pdl) {
     if (a0.epi == FORGE_EPI_SWIGLU && a0.N != 2 * a0.F) return forge_fail(-1, "gemv: SwiGLU needs N == 2F");
     if (a0.epi == FORGE_EPI_QKV && (a0.hd % 16 || a0.N != (a0.H + 2 * a0.Hkv) * a0.hd))
         return forge_fail(-1, "gemv: QKV epilogue shape mismatch");
-    const int cols_per_seq = a0.split ? 2 : 1;
+    const bool q4 = a0.wkind == FORGE_W_Q4;
+    const int cols_per_seq = (q4 || a0.split) ? 2 : 1;
     if (a0.K / 128 > kMaxG) return forge_fail(-1, "gemv: K=%d above the supported maximum", a0.K);
-    const int sx_bytes = a0.wkind == FORGE_W_Q4 ? (a0.K / 128) * 8 * 4 : 0;
-    const int xs_row = ((a0.K + 31) / 32) * 32 * 2;  // K padded to whole k-tile pairs
+    const int sx_bytes = q4 ? (a0.K / 128) * 12 * 4 : 0;
+    // bf16: K padded to whole k-tile pairs, 2 bytes; int4: int8 activations
+    const int xs_row = q4 ? a0.K : ((a0.K + 31) / 32) * 32 * 2;
     int max_cols = (kMaxSmem - kFixedSmem - sx_bytes) / xs_row;
     if (max_cols > 8) max_cols = 8;
     const int per_launch = max_cols / cols_per_seq;

@@ -34,11 +34,10 @@ __device__ __forceinline__ float4 load_x4(const ForgeGemvArgs& a, int b, const f
     return __ldcg(reinterpret_cast<const float4*>(xb + k));
 }
 
-// Prologue (consumer warps): optional RMSNorm, hi/lo split, fragment-order
-// store, and (int4) per-group column sums of the bf16 operand for the
-// dequantisation-bias correction.
-template <int WK, int PRO, int NT>
-__device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, float* sx, float* red) {
+// bf16-weight prologue (consumer warps): optional RMSNorm, hi/lo bf16 split,
+// fragment-order store.
+template <int PRO, int NT>
+__device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, float* red) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.K;
     const int ncols = a.split ? 2 * a.batch : a.batch;
@@ -71,13 +70,10 @@ __device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, fl
                 e[2] = gv.z * (e[2] * inv); e[3] = gv.w * (e[3] * inv);
             }
             uint16_t hi[4], lo[4];
-            float shi = 0.f, slo = 0.f;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 if (a.split) split_bf16(e[i], hi[i], lo[i]);
                 else { hi[i] = f32_to_bf16_bits(e[i]); lo[i] = 0; }
-                shi += bf16_bits_to_f32(hi[i]);
-                slo += bf16_bits_to_f32(lo[i]);
             }
             const int ch = a.split ? 2 * b : b;
             *reinterpret_cast<uint32_t*>(xf + xf_index(k, ch, ncols)) = hi[0] | ((uint32_t)hi[1] << 16);
@@ -85,17 +81,6 @@ __device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, fl
             if (a.split) {
                 *reinterpret_cast<uint32_t*>(xf + xf_index(k, ch + 1, ncols)) = lo[0] | ((uint32_t)lo[1] << 16);
                 *reinterpret_cast<uint32_t*>(xf + xf_index(k + 2, ch + 1, ncols)) = lo[2] | ((uint32_t)lo[3] << 16);
-            }
-            if (WK == FORGE_W_Q4) {
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    shi += __shfl_xor_sync(0xffffffffu, shi, o);
-                    slo += __shfl_xor_sync(0xffffffffu, slo, o);
-                }
-                if (lane == 0) {
-                    sx[(k >> 7) * 8 + ch] = shi;
-                    if (a.split) sx[(k >> 7) * 8 + ch + 1] = slo;
-                }
             }
         }
     }
@@ -174,3 +159,118 @@ __device__ __forceinline__ void dequant_q4_biased(uint32_t w, uint32_t (&a)[4]) 
     a[3] = lop3_and_or(w >> 12, mask, magic);
 }
 
+
+// ------------------------------------------------------------------ int8
+// Byte offset of activation (k, col) in the int8 fragment-order buffer: for
+// each pair of 32-wide k-tiles and column, lane t owns 16 bytes = {b0, b1} of
+// the even tile and {b0, b1} of the odd tile of mma.m16n8k32 (b0: k 4t..4t+3,
+// b1: k 16+4t..16+4t+3).
+__device__ __forceinline__ int xq_index(int k, int col, int ncols) {
+    const int kt = k >> 5, kk = k & 31;
+    const int kp = kt >> 1, which = kt & 1, t = (kk & 15) >> 2, half = kk >> 4, i = kk & 3;
+    return (((kp * ncols + col) * 4 + t) * 16) + which * 8 + half * 4 + i;
+}
+
+// int4-weight prologue: activations become int8 pairs per 128-group and
+// sequence b: s = max|x| / 127, hi = rint(x / s), lo = rint((x - s*hi)*256/s)
+// (both clamped to +-127), so x = s*(hi + lo/256) to ~2^-16 of the group
+// maximum. Columns 2b / 2b+1 hold hi / lo. Per group it records s (sxf[g][b])
+// and the column sums of hi and lo (ssum[g][2b], ssum[g][2b+1]) that remove
+// the +7 code bias of the weights after the integer dot product.
+template <int PRO, int NT>
+__device__ __forceinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, float* sxf, int* ssum,
+                                           float* red) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = a.K;
+    const int ncols = 2 * a.batch;
+    for (int b = 0; b < a.batch; ++b) {
+        const float* xb = a.x + (size_t)b * a.x_stride;
+        float inv = 1.0f;
+        if (PRO != FORGE_PRO_PLAIN) {
+            float ss = 0.0f;
+            for (int k = tid * 4; k < K; k += NT * 4) {
+                const float4 v = load_x4<PRO>(a, b, xb, k);
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) red[warp] = ss;
+            named_bar_sync(1, NT);
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NT / 32; ++w) tot += red[w];
+            inv = 1.0f / sqrtf(tot / (float)K + a.eps);
+            named_bar_sync(1, NT);
+        }
+        // a warp covers one 128-group per pass (NT * 4 is a multiple of 128)
+        for (int k = tid * 4; k < K; k += NT * 4) {
+            const float4 v = load_x4<PRO>(a, b, xb, k);
+            float e[4] = {v.x, v.y, v.z, v.w};
+            if (PRO != FORGE_PRO_PLAIN) {
+                const float4 gv = *reinterpret_cast<const float4*>(a.gain + k);
+                e[0] = gv.x * (e[0] * inv); e[1] = gv.y * (e[1] * inv);
+                e[2] = gv.z * (e[2] * inv); e[3] = gv.w * (e[3] * inv);
+            }
+            float amax = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
+            const float is = amax > 0.f ? 127.0f / amax : 0.0f;
+            uint32_t hw = 0, lw = 0;
+            int shi = 0, slo = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float hq = fminf(fmaxf(rintf(e[i] * is), -127.f), 127.f);
+                const float lq = fminf(fmaxf(rintf((e[i] - sc * hq) * (256.0f * is)), -127.f), 127.f);
+                const int hi = (int)hq, lo = (int)lq;
+                shi += hi;
+                slo += lo;
+                hw |= (uint32_t)(hi & 0xFF) << (8 * i);
+                lw |= (uint32_t)(lo & 0xFF) << (8 * i);
+            }
+            *reinterpret_cast<uint32_t*>(xq + xq_index(k, 2 * b, ncols)) = hw;
+            *reinterpret_cast<uint32_t*>(xq + xq_index(k, 2 * b + 1, ncols)) = lw;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                shi += __shfl_xor_sync(0xffffffffu, shi, o);
+                slo += __shfl_xor_sync(0xffffffffu, slo, o);
+            }
+            if (lane == 0) {
+                const int g = k >> 7;
+                sxf[g * 4 + b] = sc;
+                ssum[g * 8 + 2 * b] = shi;
+                ssum[g * 8 + 2 * b + 1] = slo;
+            }
+        }
+    }
+}
+
+// One 128-group of int4 weights against the int8 activations: 2 chunks
+// (4 k-tiles of 32) in two independent integer accumulators, then the code
+// bias (7 * column sum), the hi/lo recombination and the two scales.
+// Returns the contributions to rows g and g+8 for sequence t (lanes with
+// t >= batch compute garbage that is never stored).
+__device__ __forceinline__ void q4_group(const uint4 w0, const uint4 w1, const uint8_t* xq, int gg, int ncols,
+                                         int col, int t, uint32_t scale_pair, const float* sxf, const int* ssum,
+                                         int batch, float& y0, float& y1) {
+    int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+    const uint4* xa = reinterpret_cast<const uint4*>(xq) + (size_t)((2 * gg) * ncols + col) * 4 + t;
+    const uint4 b0 = xa[0];
+    const uint4 b1 = xa[(size_t)ncols * 4];
+    uint32_t af[4];
+    dequant_q4_u8(w0.x, w0.y, af);
+    mma_u8s8_16832(c0, af, b0.x, b0.y);
+    dequant_q4_u8(w0.z, w0.w, af);
+    mma_u8s8_16832(c1, af, b0.z, b0.w);
+    dequant_q4_u8(w1.x, w1.y, af);
+    mma_u8s8_16832(c0, af, b1.x, b1.y);
+    dequant_q4_u8(w1.z, w1.w, af);
+    mma_u8s8_16832(c1, af, b1.z, b1.w);
+    const int tb = t < batch ? t : batch - 1;
+    const int shi = ssum[gg * 8 + 2 * tb], slo = ssum[gg * 8 + 2 * tb + 1];
+    const float sx = sxf[gg * 4 + tb];
+    const float v0 = (float)(c0[0] + c1[0] - 7 * shi) + (float)(c0[1] + c1[1] - 7 * slo) * (1.0f / 256.0f);
+    const float v1 = (float)(c0[2] + c1[2] - 7 * shi) + (float)(c0[3] + c1[3] - 7 * slo) * (1.0f / 256.0f);
+    y0 = bf16_lo_f32(scale_pair) * sx * v0;
+    y1 = bf16_hi_f32(scale_pair) * sx * v1;
+}

@@ -9,9 +9,12 @@
 //      lane l = 4g + t holds A[g][2t,2t+1] A[g+8][2t,2t+1] A[g][2t+8,2t+9]
 //      A[g+8][2t+8,2t+9] (the mma A-fragment order).
 //  q4 tiles    : [N/16][K/64][32 lanes][4 words]          512 B per 16x64 chunk
-//      word w of lane l covers k-tile 4c+w; nibble j of the word holds
-//      element (row g + 8*(j&1), k 2t + 8*((j>>1)&1) + (j>>2)), code = q + 7,
-//      so (word >> 4i) & 0x000F000F are the two nibbles of A register i.
+//      int4 codes feed the int8 tensor-core path (mma.m16n8k32 .u8 x .s8):
+//      words 2j and 2j+1 of lane l = 4g + t hold the 16x32 k-tile j of the
+//      chunk; byte i of word 2j+h holds, in its low nibble, the code of
+//      (row g, k 16h + 4t + i) and in its high nibble (row g+8, same k), so
+//      (w & 0x0F0F0F0F) and ((w >> 4) & 0x0F0F0F0F) are A-fragment registers
+//      of unsigned codes (code = q + 7).
 //  q4 scales   : [N/16][ceil(G/4)][8 g][4 groups][2 (row g, row g+8)] bf16
 //      one 16-byte load per lane gives the scales of rows g and g+8 for four
 //      consecutive 128-groups (groups past G are zero padding).
@@ -35,12 +38,12 @@ FORGE_HD int64_t bf16_tile_offset(int64_t r, int64_t k, int64_t K) {
 
 // (word byte offset, nibble index) of element (r, k) in the q4 tile layout.
 FORGE_HD int64_t q4_tile_word_offset(int64_t r, int64_t k, int64_t K, int* nibble) {
-    int64_t rt = r >> 4, kt = k >> 4, c = kt >> 2;
-    int w = (int)(kt & 3);
-    int rr = (int)(r & 15), kk = (int)(k & 15);
-    int g = rr & 7, up = rr >> 3, t = (kk & 7) >> 1, kh = kk >> 3, e = kk & 1;
-    int lane = g * 4 + t;
-    *nibble = e * 4 + kh * 2 + up;
+    int64_t rt = r >> 4, c = k >> 6;
+    int kt32 = (int)((k >> 5) & 1), kk = (int)(k & 31);
+    int rr = (int)(r & 15), g = rr & 7, up = rr >> 3;
+    int t = (kk & 15) >> 2, i = kk & 3, h16 = kk >> 4;
+    int lane = g * 4 + t, w = kt32 * 2 + h16;
+    *nibble = i * 2 + up;
     return ((rt * (K >> 6) + c) * 32 + lane) * 16 + w * 4;
 }
 

@@ -301,6 +301,9 @@ int fused_splits(const ForgeB200* h, int B) {
 // that it fits one CTA per SM. Returns the args or nullptr.
 const ForgeStepArgs* fused_for(ForgeB200* h, int B) {
     if (h->force_graph) return nullptr;
+    // one mma column block per GEMV: int4 (hi/lo int8) and exact bf16 use two
+    // columns per sequence, plain bf16 one
+    if ((h->q4 || h->split_for(B)) ? B > 4 : B > 8) return nullptr;
     auto ok = h->fused_ok.find(B);
     if (ok != h->fused_ok.end() && !ok->second) return nullptr;
     auto it = h->fused.find(B);
@@ -348,10 +351,14 @@ const ForgeStepArgs* fused_for(ForgeB200* h, int B) {
     ForgePhase fin{};
     fin.type = FORGE_PH_FIN;
     ph.push_back(fin);
+    int xf_bytes = 0;
     for (const auto& p : ph)
-        if (p.type == FORGE_PH_GEMV) kmax = std::max(kmax, p.g.K);
-    const int ncols = split ? 2 * B : B;
-    const int xf_bytes = ncols * ((kmax + 31) / 32) * 32 * 2;
+        if (p.type == FORGE_PH_GEMV) {
+            kmax = std::max(kmax, p.g.K);
+            const int need = p.g.wkind == FORGE_W_Q4 ? 2 * B * p.g.K
+                                                     : (split ? 2 * B : B) * ((p.g.K + 31) / 32) * 32 * 2;
+            xf_bytes = std::max(xf_bytes, need);
+        }
     ForgeStepArgs sa{};
     sa.nphases = (int)ph.size();
     sa.grid = forge_sm_count();
@@ -792,8 +799,8 @@ FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
     if (!h || batch <= 0) return -1;
     if (fused_for(h, batch)) return 1;
     const bool split = h->split_for(batch);
-    auto launches = [&](int K) { return forge_gemv_launch_count(K, batch, split); };
+    auto launches = [&](int K) { return forge_gemv_launch_count(K, batch, split, h->q4); };
     int per_layer = launches(h->d) * 2 + launches(h->qd) + launches(h->F) + 1;
-    return 1 + h->L * per_layer + launches(h->d) + 1;
+    return 1 + h->L * per_layer + forge_gemv_launch_count(h->d, batch, split, false) + 1;
 }
 }  // extern "C"

@@ -187,23 +187,24 @@ __device__ __forceinline__ uint32_t code_at(const uint8_t* codes, int64_t r, int
     uint8_t b = codes[(r * K + k) >> 1];
     return (k & 1) ? (b >> 4) : (b & 15u);
 }
-// One thread per packed 32-bit word of the q4 tile layout.
+// One thread per packed 32-bit word of the q4 tile layout (layout.cuh).
 __global__ void k_pack_q4_tiles(const uint8_t* __restrict__ codes, int64_t N, int64_t K,
                                 uint32_t* __restrict__ out) {
     const int64_t nword = N * K / 8;
     for (int64_t wi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; wi < nword;
          wi += (int64_t)gridDim.x * blockDim.x) {
-        int w = (int)(wi & 3);
-        int lane = (int)((wi >> 2) & 31), g = lane >> 2, t = lane & 3;
-        int64_t chunk = wi >> 7;
-        int64_t rt = chunk / (K >> 6), c = chunk % (K >> 6);
-        int64_t kt = c * 4 + w;
+        const int w = (int)(wi & 3);
+        const int lane = (int)((wi >> 2) & 31), g = lane >> 2, t = lane & 3;
+        const int64_t chunk = wi >> 7;
+        const int64_t rt = chunk / (K >> 6), c = chunk % (K >> 6);
+        const int kt32 = w >> 1, h16 = w & 1;
         uint32_t word = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            int up = j & 1, kh = (j >> 1) & 1, e = j >> 2;
-            int64_t r = rt * 16 + g + 8 * up, k = kt * 16 + 2 * t + 8 * kh + e;
-            word |= code_at(codes, r, k, K) << (4 * j);
+        for (int i = 0; i < 4; ++i) {
+            const int64_t k = c * 64 + kt32 * 32 + h16 * 16 + t * 4 + i;
+            const uint32_t lo = code_at(codes, rt * 16 + g, k, K);
+            const uint32_t hi = code_at(codes, rt * 16 + g + 8, k, K);
+            word |= (lo | (hi << 4)) << (8 * i);
         }
         out[wi] = word;
     }

@@ -63,12 +63,14 @@ def _upload(om, fm, cfg):
 def test_decode_steps_match_oracle(forge, oracle, cuda, name, batch, path):
     cfg = CONFIGS[name]
     lmax = 48
-    act_bf16 = batch > 4
+    # bf16-weight models round GEMV inputs to bf16 above 4 sequences; int4
+    # models always use hi/lo int8 activations (no oracle rounding)
+    act_bf16 = batch > 4 and not cfg["q4"]
     om, fm = _models(oracle, forge, cfg, batch, lmax)
     _upload(om, fm, cfg)
     if path == "graph":
         assert not fm.uses_fused_step(batch)
-    elif batch <= 2:
+    elif batch <= 4:
         assert fm.uses_fused_step(batch), "the fused step must fit at this size"
     kc, vc = om.new_cache(batch, lmax)
     rng = np.random.default_rng(5678 + batch)
@@ -81,7 +83,7 @@ def test_decode_steps_match_oracle(forge, oracle, cuda, name, batch, path):
     # inside the 2e-2 (bf16) / 5e-2 (int4) gates — and a median below 2e-4
     # (exact activations) or 1e-3 (bf16 activations).
     tol = 5e-3 if not act_bf16 else 1e-2
-    med_tol = 2e-4 if not act_bf16 else 1.5e-3
+    med_tol = (8e-4 if cfg["q4"] else 2e-4) if not act_bf16 else 1.5e-3
     fm.reset()
     worst = 0.0
     for p in range(20):
