@@ -88,6 +88,9 @@ def lib() -> C.CDLL:
             "forge_gemv_bf16": (i32, [vp, i64, i64, vp, i32, vp, i32, vp]),
             "forge_flash_decode_workspace_bytes": (i64, [i32, i32, i32, i32, i32]),
             "forge_flash_decode": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp]),
+            "forge_flash_decode_noalloc": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]),
+            "forge_flash_decode_noalloc_capacity": (i64, []),
+            "forge_flash_decode_noalloc_status": (i32, []),
             "forge_fill_normal_bf16": (i32, [vp, i64, C.c_uint64, C.c_uint64, C.c_float, vp]),
             "forge_fill_f32": (i32, [vp, i64, C.c_float, vp]),
             "forge_q4_quantize_bf16": (i32, [vp, i64, i64, i32, vp, vp, vp]),

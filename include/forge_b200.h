@@ -132,6 +132,22 @@ int forge_flash_decode(const float* q, const uint16_t* kc, const uint16_t* vc, c
                        int B, int H, int Hkv, int hd, int lmax, float* out, void* workspace,
                        void* stream);
 
+/* Allocation-free split-K flash-decode, for callers that cannot allocate
+ * device memory (their device memory belongs to another allocator, they run
+ * during stream capture, or their memory budget is fixed): same arguments and
+ * results as forge_flash_decode, but the scratch comes from one fixed
+ * library-owned device array of forge_flash_decode_noalloc_capacity() bytes
+ * (4 MiB) per GPU, held until the process exits; shapes needing more are
+ * rejected with FORGE_INVALID_ARGS. Calls share that array, so calls that
+ * overlap on the GPU race; order them on one stream. The first call on a
+ * device looks up the array's device address and should happen before any
+ * stream capture. No counterpart in the reference: it is an addition of
+ * this library. */
+int64_t forge_flash_decode_noalloc_capacity(void);
+int forge_flash_decode_noalloc(const float* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos,
+                               int B, int H, int Hkv, int hd, int lmax, float* out, void* stream);
+int forge_flash_decode_noalloc_status(void);
+
 /* Weight preparation (device memory). */
 int forge_fill_normal_bf16(uint16_t* out, int64_t n, uint64_t seed, uint64_t offset, float std,
                            void* stream);
