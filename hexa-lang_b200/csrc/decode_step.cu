@@ -29,7 +29,7 @@
 #include "gemv_core.cuh"
 
 namespace {
-constexpr int kCW = 16;               // consumer warps
+constexpr int kCW = 8;                // consumer warps
 constexpr int kNT = kCW * 32;         // consumer threads
 #ifndef FORGE_STEP_PRODUCER_WARP_DEF
 #define FORGE_STEP_PRODUCER_WARP_DEF 1
@@ -66,6 +66,7 @@ struct Smem {
     uint16_t* xf;
     struct Prod* prod;
     ForgePhase* ph;  // shared copy of the current phase's descriptor
+    unsigned long long* tr;  // this CTA's trace row for the current phase (or null)
 };
 
 // Producer cursor (touched by thread 0 only): next item to issue.
@@ -256,6 +257,7 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
             }
     }
     named_bar_sync(1, kNT);
+    if (m.tr && threadIdx.x == 0) m.tr[2] = globaltimer_ns();
 
     const int g = lane >> 2, t = lane & 3;
     const int ncols = (WK == FORGE_W_Q4 || a.split) ? 2 * a.batch : a.batch;
@@ -275,29 +277,46 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
             const int kt0 = i * kItemKT, nkt = min(kItemKT, KT - kt0);
             const uint8_t* st = m.ring + (size_t)s * kStage;
             if (WK == FORGE_W_Q4) {
+                // warp w: groups 2w and 2w+1 of the piece (int8 tensor-core path)
                 const int ng = nkt / 8;
-                if (warp < ng) {  // warp w: group w of the piece (int8 tensor-core path)
-                    const uint4 w0 = *reinterpret_cast<const uint4*>(st + (2 * warp) * 512 + lane * 16);
-                    const uint4 w1 = *reinterpret_cast<const uint4*>(st + (2 * warp + 1) * 512 + lane * 16);
+                const int gA = 2 * warp;
+                if (gA < ng) {
                     const uint16_t* sst = reinterpret_cast<const uint16_t*>(st + kPiece);
-                    const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (warp >> 2) * 64 + g * 8 + (warp & 3) * 2);
                     float y0, y1;
-                    q4_group(w0, w1, xq, kt0 / 8 + warp, ncols, col, t, sc, sxf, ssum, a.batch, y0, y1);
-                    tot[0] += y0;
-                    tot[1] += y1;
+                    {
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(st + (4 * warp) * 512 + lane * 16);
+                        const uint4 w1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 1) * 512 + lane * 16);
+                        const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (gA >> 2) * 64 + g * 8 + (gA & 3) * 2);
+                        q4_group(w0, w1, xq, kt0 / 8 + gA, ncols, col, t, sc, sxf, ssum, a.batch, y0, y1);
+                        tot[0] += y0;
+                        tot[1] += y1;
+                    }
+                    if (gA + 1 < ng) {
+                        const int gB = gA + 1;
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(st + (4 * warp + 2) * 512 + lane * 16);
+                        const uint4 w1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 3) * 512 + lane * 16);
+                        const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (gB >> 2) * 64 + g * 8 + (gB & 3) * 2);
+                        q4_group(w0, w1, xq, kt0 / 8 + gB, ncols, col, t, sc, sxf, ssum, a.batch, y0, y1);
+                        tot2[0] += y0;
+                        tot2[1] += y1;
+                    }
                 }
             } else {
-                const int ktw = 2 * warp;  // warp w: k-tiles 2w, 2w+1
-                if (ktw < nkt) {
-                    const uint4 w0 = *reinterpret_cast<const uint4*>(st + ktw * 512 + lane * 16);
-                    const uint4 w1 = (ktw + 1 < nkt) ? *reinterpret_cast<const uint4*>(st + (ktw + 1) * 512 + lane * 16)
-                                                     : make_uint4(0, 0, 0, 0);
-                    const int kp = (kt0 + ktw) >> 1;
-                    const uint4 bb = *(reinterpret_cast<const uint4*>(m.xf) + (size_t)(kp * ncols + col) * 4 + t);
-                    const uint32_t f0[4] = {w0.x, w0.y, w0.z, w0.w};
-                    const uint32_t f1[4] = {w1.x, w1.y, w1.z, w1.w};
-                    mma_bf16_16816(tot, f0, bb.x, bb.y, tot);
-                    mma_bf16_16816(tot2, f1, bb.z, bb.w, tot2);
+                const int ktw = 4 * warp;  // warp w: k-tiles 4w .. 4w+3 (two pairs)
+#pragma unroll
+                for (int jp = 0; jp < 2; ++jp) {
+                    const int kt = ktw + 2 * jp;
+                    if (kt < nkt) {
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(st + kt * 512 + lane * 16);
+                        const uint4 w1 = (kt + 1 < nkt) ? *reinterpret_cast<const uint4*>(st + (kt + 1) * 512 + lane * 16)
+                                                        : make_uint4(0, 0, 0, 0);
+                        const int kp = (kt0 + kt) >> 1;
+                        const uint4 bb = *(reinterpret_cast<const uint4*>(m.xf) + (size_t)(kp * ncols + col) * 4 + t);
+                        const uint32_t f0[4] = {w0.x, w0.y, w0.z, w0.w};
+                        const uint32_t f1[4] = {w1.x, w1.y, w1.z, w1.w};
+                        mma_bf16_16816(tot, f0, bb.x, bb.y, tot);
+                        mma_bf16_16816(tot2, f1, bb.z, bb.w, tot2);
+                    }
                 }
             }
             __syncwarp();
@@ -311,8 +330,8 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
         float* rw = m.red + ((size_t)(grp * R + si) * kCW + warp) * 16 * rc;
         if (WK == FORGE_W_Q4) {
             if (t < a.batch) {
-                rw[g * rc + t] = tot[0];
-                rw[(g + 8) * rc + t] = tot[1];
+                rw[g * rc + t] = tot[0] + tot2[0];
+                rw[(g + 8) * rc + t] = tot[1] + tot2[1];
             }
         } else {
             if (2 * t < ncols) {
@@ -442,78 +461,75 @@ __device__ void attn_phase(const Smem& m, const ForgeStepArgs& sa, const ForgePh
 #pragma unroll
             for (int e = 0; e < E; ++e) acc[g][e] = 0.f;
         }
-        for (int base = k0; base < k1; base += 32) {
+        // blocks of 8 keys: 4 lanes per key for the scores (lane part qp reads
+        // dims qp*8 + 32m), lane-owned dims for P·V; the K and V loads of a
+        // block are issued together, one memory round trip per block
+        const int kj = lane >> 2, qp = lane & 3;
+        constexpr int M = HD / 32;
+        for (int base = k0; base < k1; base += 8) {
+#if !FORGE_STEP_PRODUCER_WARP
             if (tid == 0) pump(m, sa, S, consumed);  // keep prefetching the next weights
-            const int j = base + lane;
+#endif
+            const int j = base + kj;
             const bool valid = j < k1;
-            float sc[G];
+            const int jc = valid ? j : k0;
+            uint4 kw[M];
 #pragma unroll
-            for (int g = 0; g < G; ++g) sc[g] = 0.f;
-            if (valid) {
-                const uint4* kr = reinterpret_cast<const uint4*>(Kg + (size_t)j * HD);
-#pragma unroll 4
-                for (int c = 0; c < HD / 8; ++c) {
-                    const uint4 kw = __ldcs(kr + c);
-                    const uint32_t w4[4] = {kw.x, kw.y, kw.z, kw.w};
+            for (int mm = 0; mm < M; ++mm)
+                kw[mm] = __ldcs(reinterpret_cast<const uint4*>(Kg + (size_t)jc * HD + mm * 32 + qp * 8));
+            uint32_t vv[8][E / 2];
 #pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        const float4 q0 = *reinterpret_cast<const float4*>(m.qs + g * HD + c * 8);
-                        const float4 q1 = *reinterpret_cast<const float4*>(m.qs + g * HD + c * 8 + 4);
-                        float d = sc[g];
-                        d = fmaf(q0.x, bf16_lo_f32(w4[0]), d); d = fmaf(q0.y, bf16_hi_f32(w4[0]), d);
-                        d = fmaf(q0.z, bf16_lo_f32(w4[1]), d); d = fmaf(q0.w, bf16_hi_f32(w4[1]), d);
-                        d = fmaf(q1.x, bf16_lo_f32(w4[2]), d); d = fmaf(q1.y, bf16_hi_f32(w4[2]), d);
-                        d = fmaf(q1.z, bf16_lo_f32(w4[3]), d); d = fmaf(q1.w, bf16_hi_f32(w4[3]), d);
-                        sc[g] = d;
-                    }
+            for (int u = 0; u < 8; ++u) {
+                const int jv = min(base + u, k1 - 1);
+                const uint16_t* vr = Vg + (size_t)jv * HD + lane * E;
+                if (E == 4) {
+                    const uint2 t2 = __ldcs(reinterpret_cast<const uint2*>(vr));
+                    vv[u][0] = t2.x; vv[u][E / 2 - 1] = t2.y;
+                } else {
+                    vv[u][0] = __ldcs(reinterpret_cast<const unsigned int*>(vr));
                 }
             }
-            const int nk = min(32, k1 - base);
+            float pk[G];
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                const float s = valid ? sc[g] * scale : -INFINITY;
-                float t = s;
+                float d = 0.f;
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, o));
+                for (int mm = 0; mm < M; ++mm) {
+                    const float4 q0 = *reinterpret_cast<const float4*>(m.qs + g * HD + mm * 32 + qp * 8);
+                    const float4 q1 = *reinterpret_cast<const float4*>(m.qs + g * HD + mm * 32 + qp * 8 + 4);
+                    d = fmaf(q0.x, bf16_lo_f32(kw[mm].x), d); d = fmaf(q0.y, bf16_hi_f32(kw[mm].x), d);
+                    d = fmaf(q0.z, bf16_lo_f32(kw[mm].y), d); d = fmaf(q0.w, bf16_hi_f32(kw[mm].y), d);
+                    d = fmaf(q1.x, bf16_lo_f32(kw[mm].z), d); d = fmaf(q1.y, bf16_hi_f32(kw[mm].z), d);
+                    d = fmaf(q1.z, bf16_lo_f32(kw[mm].w), d); d = fmaf(q1.w, bf16_hi_f32(kw[mm].w), d);
+                }
+                d += __shfl_xor_sync(0xffffffffu, d, 1);
+                d += __shfl_xor_sync(0xffffffffu, d, 2);
+                const float sv = valid ? d * scale : -INFINITY;
+                float t = sv;
+                t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 4));
+                t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 8));
+                t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 16));
                 const float mn = fmaxf(mx[g], t);
                 const float al = (mx[g] == -INFINITY) ? 0.f : expf(mx[g] - mn);
-                const float p = valid ? expf(s - mn) : 0.f;
-                float ps = p;
+                const float p = valid ? expf(sv - mn) : 0.f;
+                float ps = qp == 0 ? p : 0.f;
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
                 ls[g] = ls[g] * al + ps;
                 mx[g] = mn;
 #pragma unroll
                 for (int e = 0; e < E; ++e) acc[g][e] *= al;
-                sc[g] = p;
+                pk[g] = p;
             }
-            // P·V: V rows of the block are loaded 8 at a time (independent
-            // loads in flight); key jj's probability is broadcast from lane jj
-            for (int j8 = 0; j8 < nk; j8 += 8) {
-                uint32_t vv[8][E / 2];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int jj = min(j8 + u, nk - 1);
-                    const uint16_t* vr = Vg + (size_t)(base + jj) * HD + lane * E;
-                    if (E == 4) {
-                        const uint2 t2 = __ldcs(reinterpret_cast<const uint2*>(vr));
-                        vv[u][0] = t2.x; vv[u][E / 2 - 1] = t2.y;
-                    } else {
-                        vv[u][0] = __ldcs(reinterpret_cast<const unsigned int*>(vr));
-                    }
-                }
+            for (int u = 0; u < 8; ++u) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+                for (int g = 0; g < G; ++g) {
+                    const float p = __shfl_sync(0xffffffffu, pk[g], 4 * u);
 #pragma unroll
-                    for (int g = 0; g < G; ++g) {
-                        const float p = __shfl_sync(0xffffffffu, sc[g], (j8 + u) & 31);
-                        if (j8 + u < nk) {
-#pragma unroll
-                            for (int e2 = 0; e2 < E / 2; ++e2) {
-                                acc[g][2 * e2] = fmaf(p, bf16_lo_f32(vv[u][e2]), acc[g][2 * e2]);
-                                acc[g][2 * e2 + 1] = fmaf(p, bf16_hi_f32(vv[u][e2]), acc[g][2 * e2 + 1]);
-                            }
-                        }
+                    for (int e2 = 0; e2 < E / 2; ++e2) {
+                        acc[g][2 * e2] = fmaf(p, bf16_lo_f32(vv[u][e2]), acc[g][2 * e2]);
+                        acc[g][2 * e2 + 1] = fmaf(p, bf16_hi_f32(vv[u][e2]), acc[g][2 * e2 + 1]);
                     }
                 }
             }
@@ -632,6 +648,7 @@ __global__ void __launch_bounds__(kThreadsMK, 1) k_decode_step(const ForgeStepAr
         if (p > 0) grid_wait(m, sa, (epoch * nbar + (unsigned long long)p) * gridDim.x, S, it);
         else named_bar_sync(1, kNT);
         const ForgePhase& ph = *m.ph;
+        m.tr = tr ? tr + p * 4 : nullptr;
         if (tr && threadIdx.x == 0) tr[p * 4 + 1] = globaltimer_ns();
         if (ph.type == FORGE_PH_GEMV) {
             gemv_dispatch(m, sa, ph.g, it, S);

@@ -48,7 +48,7 @@ constexpr int kStageW = 16384;                        // weight bytes per piece
 constexpr int kStageS = 512;                          // q4 scale bytes per piece (16 groups)
 constexpr int kStageBytes = kStageW + kStageS;
 constexpr int kRedFloats = 2 * kConsumerWarps * 16 * 8;  // two unit slots
-constexpr int kMaxG = 256;                            // K <= 32768 for the group sums
+constexpr int kMaxG = 128;                            // K <= 16384 (staging keeps K/4/threads float4 in registers)
 constexpr int kFixedSmem = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4;
 constexpr int kMaxSmem = 227 * 1024;
 

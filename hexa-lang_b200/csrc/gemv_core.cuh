@@ -37,7 +37,7 @@ __device__ __forceinline__ float4 load_x4(const ForgeGemvArgs& a, int b, const f
 // bf16-weight prologue (consumer warps): optional RMSNorm, hi/lo bf16 split,
 // fragment-order store.
 template <int PRO, int NT>
-__device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, float* red) {
+__device__ __noinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, float* red) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.K;
     const int ncols = a.split ? 2 * a.batch : a.batch;
@@ -178,20 +178,32 @@ __device__ __forceinline__ int xq_index(int k, int col, int ncols) {
 // and the column sums of hi and lo (ssum[g][2b], ssum[g][2b+1]) that remove
 // the +7 code bias of the weights after the integer dot product.
 template <int PRO, int NT>
-__device__ __forceinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, float* sxf, int* ssum,
-                                           float* red) {
+__device__ __noinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, float* sxf, int* ssum,
+                                        float* red) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.K;
     const int ncols = 2 * a.batch;
+    // up to MAXV float4 per thread stay in registers between the norm and the
+    // quantisation (one global read); longer rows are read twice
+    constexpr int MAXV = (16384 / (NT * 4)) < 8 ? (16384 / (NT * 4)) : 8;
+    const bool resident = K <= NT * 4 * MAXV;
     for (int b = 0; b < a.batch; ++b) {
         const float* xb = a.x + (size_t)b * a.x_stride;
-        float inv = 1.0f;
-        if (PRO != FORGE_PRO_PLAIN) {
-            float ss = 0.0f;
-            for (int k = tid * 4; k < K; k += NT * 4) {
+        float4 xv[MAXV];
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            const int k = tid * 4 + i * NT * 4;
+            xv[i] = k < K ? load_x4<PRO>(a, b, xb, k) : make_float4(0.f, 0.f, 0.f, 0.f);
+            ss += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
+        }
+        if (PRO != FORGE_PRO_PLAIN && !resident)
+            for (int k = tid * 4 + MAXV * NT * 4; k < K; k += NT * 4) {
                 const float4 v = load_x4<PRO>(a, b, xb, k);
                 ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
             }
+        float inv = 1.0f;
+        if (PRO != FORGE_PRO_PLAIN) {
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
             if (lane == 0) red[warp] = ss;
@@ -203,9 +215,20 @@ __device__ __forceinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, 
             named_bar_sync(1, NT);
         }
         // a warp covers one 128-group per pass (NT * 4 is a multiple of 128)
-        for (int k = tid * 4; k < K; k += NT * 4) {
-            const float4 v = load_x4<PRO>(a, b, xb, k);
-            float e[4] = {v.x, v.y, v.z, v.w};
+        const int passes = (K + NT * 4 - 1) / (NT * 4);
+        for (int i = 0; i < passes; ++i) {
+            const int k = tid * 4 + i * NT * 4;
+            if (k >= K) continue;  // whole warps skip together (K % 128 == 0)
+            float4 v4;
+            if (i < MAXV) {
+                v4 = xv[0];
+#pragma unroll
+                for (int r = 1; r < MAXV; ++r)
+                    if (i == r) v4 = xv[r];
+            } else {
+                v4 = load_x4<PRO>(a, b, xb, k);
+            }
+            float e[4] = {v4.x, v4.y, v4.z, v4.w};
             if (PRO != FORGE_PRO_PLAIN) {
                 const float4 gv = *reinterpret_cast<const float4*>(a.gain + k);
                 e[0] = gv.x * (e[0] * inv); e[1] = gv.y * (e[1] * inv);
@@ -219,14 +242,14 @@ __device__ __forceinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, 
             uint32_t hw = 0, lw = 0;
             int shi = 0, slo = 0;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float hq = fminf(fmaxf(rintf(e[i] * is), -127.f), 127.f);
-                const float lq = fminf(fmaxf(rintf((e[i] - sc * hq) * (256.0f * is)), -127.f), 127.f);
+            for (int j = 0; j < 4; ++j) {
+                const float hq = fminf(fmaxf(rintf(e[j] * is), -127.f), 127.f);
+                const float lq = fminf(fmaxf(rintf((e[j] - sc * hq) * (256.0f * is)), -127.f), 127.f);
                 const int hi = (int)hq, lo = (int)lq;
                 shi += hi;
                 slo += lo;
-                hw |= (uint32_t)(hi & 0xFF) << (8 * i);
-                lw |= (uint32_t)(lo & 0xFF) << (8 * i);
+                hw |= (uint32_t)(hi & 0xFF) << (8 * j);
+                lw |= (uint32_t)(lo & 0xFF) << (8 * j);
             }
             *reinterpret_cast<uint32_t*>(xq + xq_index(k, 2 * b, ncols)) = hw;
             *reinterpret_cast<uint32_t*>(xq + xq_index(k, 2 * b + 1, ncols)) = lw;
