@@ -29,6 +29,10 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 MODEL = dict(n_layer=32, d=4096, n_head=32, n_kv=32, hd=128, ffn=11008, vocab=32000)
 CTX = 2048
+# dram__bytes_read.sum + dram__bytes_write.sum of one k_gemv launch (int4
+# gate/up 22016 x 4096, batch 1) from the ncu capture summarised in
+# profiles/; None until that capture exists.
+GEMV_TRAFFIC = None
 
 
 def peaks():
@@ -181,35 +185,20 @@ def run_reference(args, world, rank):
     }))
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
-    ap.add_argument("--warmup", type=int, default=8)
-    ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--impl", default="forge", choices=["forge", "reference"])
-    ap.add_argument("--no-cpu", action="store_true")
-    args = ap.parse_args()
-    world, rank, local, pg = dist_setup()
-    if args.impl == "reference":
-        run_reference(args, world, rank)
-        return
-    import torch
-    import forge_b200 as fb
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    m, B, K, W = MODEL, args.batch, args.steps, max(3, args.warmup)
+def run_decode(fb, torch, pg, local, world, rank, B, K, W):
+    """K timed greedy steps of the 7B int4 model at batch B (device-resident
+    tokens), then K steps through the host C-ABI call (e2e)."""
+    m = MODEL
     lmax = CTX + W + 2 * K + 8
     fm = fb.ForgeModel(m["n_layer"], m["d"], m["n_head"], m["n_kv"], m["hd"], m["ffn"], m["vocab"],
                        weight_kind=fb.FORGE_WEIGHT_Q4_G128, tied_head=False, max_batch=B, max_ctx=lmax,
                        device=local)
     fm.init_synthetic(1234 + rank, 0.02)
     fm.fill_kv_synthetic(99 + rank, CTX, 0.5)
-    ctx0 = CTX
     # warm-up (graph capture + replays)
     fm.decode_device(B, W)
     fm.sync()
-    ctx_mid = ctx0 + W + K // 2
+    ctx_mid = CTX + W + K // 2
     stream = torch.cuda.ExternalStream(fm.stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(pg)
@@ -243,32 +232,77 @@ def main():
     step_bytes = fm.step_bytes(B, ctx_mid)
     launches = fm.launches_per_step(B) * K
     peak, peak_kind = peaks()
-    gemv_ms, gemv_bytes = time_dominant_gemv(fb, torch, dev)
-    achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
     step_gbs = step_bytes / (ms / 1e3) / 1e9
     fm.close()
-    if rank != 0:
-        return
-    cpu = None if args.no_cpu else cpu_sample(B, CTX)
-    out = {
-        "metric": "decode tok/s (7B-shape int4 g128, bs%d, ctx %d)" % (B, CTX),
-        "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4 weights (g128 bf16 scales), bf16 KV/head, fp32 accumulate",
-        "data": "synthetic",
-        "config": {"workload": "7b_int4_decode", "n_layer": 32, "d_model": 4096, "heads": 32, "head_dim": 128,
-                   "ffn": 11008, "vocab": 32000, "batch": B, "ctx": CTX, "parallelism": "replicas" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (3.9 GB streamed per step)"},
+    return {
+        "batch": B, "value": value, "ms_per_step": ms, "clocks": clk.summary(),
         "hbm_roofline_step": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "peak_gbs": peak,
                               "frac": step_gbs / peak, "peak_kind": peak_kind,
                               "frac_of_8tbs_nominal": step_gbs / 8000.0},
-        "roofline": {"bound": "hbm", "kernel": "k_gemv<int4, gate/up 22016x4096>", "achieved": achieved,
-                     "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
-                     "peak_kind": peak_kind, "launch_ms": gemv_ms, "bytes_per_launch": gemv_bytes},
         "e2e": {"value": world * B / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                 "d2h_bytes_per_step": 4 * B, "ms_per_step": e2e_ms},
         "gpu_launches": launches,
-        "clocks": clk.summary(),
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", default="forge", choices=["forge", "reference"])
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--also-batch", type=int, nargs="*", default=[32],
+                    help="further batch sizes measured after the main one (reported under batch_sweep)")
+    ap.add_argument("--only-gemv", action="store_true", help="run only the dominant GEMV (for profiling)")
+    args = ap.parse_args()
+    world, rank, local, pg = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    import torch
+    import forge_b200 as fb
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if args.only_gemv:
+        # the dominant kernel alone, for profiling: a few launches of the 7B
+        # gate/up int4 GEMV (22016 x 4096) over 4 weight copies (180 MB)
+        ms, nbytes = time_dominant_gemv(fb, torch, dev, reps=3)
+        print(json.dumps({"kernel": "k_gemv int4 22016x4096 bs1", "ms": ms, "bytes": nbytes}))
+        return
+    B, K, W = args.batch, args.steps, max(3, args.warmup)
+    r = run_decode(fb, torch, pg, local, world, rank, B, K, W)
+    extra = []
+    for B2 in args.also_batch:
+        if B2 != B:
+            r2 = run_decode(fb, torch, pg, local, world, rank, B2, max(3, K // 4), W)
+            extra.append({k: r2[k] for k in ("batch", "value", "ms_per_step", "hbm_roofline_step", "e2e", "gpu_launches")})
+    peak, peak_kind = peaks()
+    gemv_ms, gemv_bytes = time_dominant_gemv(fb, torch, dev)
+    achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
+    if rank != 0:
+        return
+    cpu = None if args.no_cpu else cpu_sample(B, CTX)
+    B = r["batch"]
+    out = {
+        "metric": "decode tok/s (7B-shape int4 g128, bs%d, ctx %d)" % (B, CTX),
+        "value": r["value"], "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4 weights (g128 bf16 scales), bf16 KV/head, fp32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": "7b_int4_decode", "n_layer": 32, "d_model": 4096, "heads": 32, "head_dim": 128,
+                   "ffn": 11008, "vocab": 32000, "batch": B, "ctx": CTX,
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (3.9 GB streamed per step)"},
+        "hbm_roofline_step": r["hbm_roofline_step"],
+        "roofline": {"bound": "hbm", "kernel": "k_gemv<int4, gate/up 22016x4096>", "achieved": achieved,
+                     "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": GEMV_TRAFFIC,
+                     "peak_kind": peak_kind, "launch_ms": gemv_ms, "bytes_per_launch": gemv_bytes},
+        "e2e": r["e2e"],
+        "gpu_launches": r["gpu_launches"],
+        "clocks": r["clocks"],
+        "batch_sweep": extra,
         "cpu_baseline": cpu,
     }
     print(json.dumps(out))

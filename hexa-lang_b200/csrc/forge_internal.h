@@ -120,3 +120,13 @@ struct ForgeStepArgs {
 // 0 launched (or fits, with probe_only), 1 does not fit / unsupported, -1 error.
 int forge_step_launch(const ForgeStepArgs& sa, int xf_bytes, cudaStream_t stream, bool probe_only);
 int forge_step_attn_tile(int hd);
+
+// ------------------------------------------------------------ dispatch glue
+struct ForgeB200;
+struct ForgeShapeInfo;
+struct ForgeArgs;
+// Row widths of a handle's activations: 0 model dim, 1 query width H*hd,
+// 2 vocabulary; 0 for a null handle.
+extern "C" int64_t forge_b200_width(const ForgeB200* h, int which);
+// v2 FLASH_PREFILL family.
+int forge_prefill_dispatch(const ForgeShapeInfo* s, const ForgeArgs* in, const ForgeArgs* out);

@@ -67,6 +67,21 @@ __global__ void k_finalize(unsigned long long* keys, int B, int32_t* tok, int32_
     if (threadIdx.x == 0) *step = s + 1;
 }
 
+// Token ids out of the packed argmax keys (keys reset for the next use),
+// without touching positions or the step history.
+__global__ void k_argmax_extract(unsigned long long* keys, int B, int32_t* tok) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) {
+        const unsigned long long k = keys[b];
+        tok[b] = k ? (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull)) : 0;
+        keys[b] = 0ull;
+    }
+}
+
+__global__ void k_add_i32(int32_t* p, int n, int32_t v) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] += v;
+}
+
 __global__ void k_set_i32(int32_t* p, int n, int32_t v) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = v;
 }
@@ -224,56 +239,81 @@ int load_embed_impl(ForgeB200* h, const Src& emb, const Src* head, const float* 
     return cudaStreamSynchronize(h->stream) == cudaSuccess ? 0 : forge_fail(-1, "forge_b200: embedding prep failed");
 }
 
-int enqueue_step(ForgeB200* h, int B) {
-    cudaStream_t st = h->stream;
-    const bool split = h->split_for(B);
-    if (forge_embed_launch(h->emb, h->d, h->V, h->tok, B, h->x, h->err, st, false)) return -1;
-    for (int l = 0; l < h->L; ++l) {
-        const LayerDev& Ld = h->layers[l];
-        uint16_t* kc = h->kc + (size_t)l * h->kv_layer;
-        uint16_t* vc = h->vc + (size_t)l * h->kv_layer;
-        ForgeGemvArgs a{};
-        a.wkind = h->q4 ? FORGE_W_Q4 : FORGE_W_BF16;
-        a.batch = B;
-        a.split = split;
-        a.err = h->err;
-        // QKV + RoPE + KV append
-        ForgeGemvArgs g = a;
-        g.w = Ld.qkv_w; g.s = Ld.qkv_s; g.N = h->nqkv; g.K = h->d;
-        g.x = h->x; g.x_stride = h->d; g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g1; g.eps = h->desc.rms_eps;
-        g.epi = FORGE_EPI_QKV; g.q_out = h->q; g.kc = kc; g.vc = vc; g.pos = h->pos;
-        g.H = h->H; g.Hkv = h->Hkv; g.hd = h->hd; g.lmax = h->lmax;
-        g.rope_cos = h->rope_cos; g.rope_sin = h->rope_sin;
-        if (forge_gemv_launch(g, st, true)) return -1;
-        // attention
-        ForgeAttnArgs at{};
-        at.q = h->q; at.kc = kc; at.vc = vc; at.pos = h->pos; at.B = B; at.H = h->H; at.Hkv = h->Hkv;
-        at.hd = h->hd; at.lmax = h->lmax; at.nsplit = forge_attn_pick_splits(B, h->Hkv, h->lmax);
-        at.partial = h->partial; at.counters = h->counters; at.out = h->ctx; at.err = h->err;
-        if (forge_attn_launch(at, st, true)) return -1;
-        // O projection + residual
-        g = a;
-        g.w = Ld.o_w; g.s = Ld.o_s; g.N = h->d; g.K = h->qd; g.x = h->ctx; g.x_stride = h->qd;
-        g.pro = FORGE_PRO_PLAIN; g.epi = FORGE_EPI_RESID; g.y = h->x; g.y_stride = h->d;
-        if (forge_gemv_launch(g, st, true)) return -1;
-        // gate/up + SwiGLU
-        g = a;
-        g.w = Ld.gu_w; g.s = Ld.gu_s; g.N = 2 * h->F; g.K = h->d; g.x = h->x; g.x_stride = h->d;
-        g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g2; g.eps = h->desc.rms_eps;
-        g.epi = FORGE_EPI_SWIGLU; g.s_out = h->s; g.F = h->F;
-        if (forge_gemv_launch(g, st, true)) return -1;
-        // down + residual
-        g = a;
-        g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = h->s; g.x_stride = h->F;
-        g.pro = FORGE_PRO_PLAIN; g.epi = FORGE_EPI_RESID; g.y = h->x; g.y_stride = h->d;
-        if (forge_gemv_launch(g, st, true)) return -1;
-    }
-    ForgeGemvArgs g{};
-    g.wkind = FORGE_W_BF16; g.batch = B; g.split = split; g.err = h->err;
-    g.w = h->head_w; g.N = h->Vpad; g.K = h->d; g.x = h->x; g.x_stride = h->d;
+// The launches of one decode step, block by block. Each helper reads and
+// writes the given device arrays; the step itself passes the handle's own.
+ForgeGemvArgs gemv_base(const ForgeB200* h, int B) {
+    ForgeGemvArgs a{};
+    a.wkind = h->q4 ? FORGE_W_Q4 : FORGE_W_BF16;
+    a.batch = B;
+    a.split = h->split_for(B);
+    a.err = h->err;
+    return a;
+}
+
+// RMSNorm + QKV + RoPE, K/V appended at each sequence's position.
+int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl) {
+    const LayerDev& Ld = h->layers[l];
+    ForgeGemvArgs g = gemv_base(h, B);
+    g.w = Ld.qkv_w; g.s = Ld.qkv_s; g.N = h->nqkv; g.K = h->d;
+    g.x = x; g.x_stride = h->d; g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g1; g.eps = h->desc.rms_eps;
+    g.epi = FORGE_EPI_QKV; g.q_out = q; g.kc = h->kc + (size_t)l * h->kv_layer; g.vc = h->vc + (size_t)l * h->kv_layer;
+    g.pos = h->pos; g.H = h->H; g.Hkv = h->Hkv; g.hd = h->hd; g.lmax = h->lmax;
+    g.rope_cos = h->rope_cos; g.rope_sin = h->rope_sin;
+    return forge_gemv_launch(g, h->stream, pdl);
+}
+
+// Split-K flash-decode over positions 0..pos of every sequence.
+int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pdl) {
+    ForgeAttnArgs at{};
+    at.q = q; at.kc = h->kc + (size_t)l * h->kv_layer; at.vc = h->vc + (size_t)l * h->kv_layer; at.pos = h->pos;
+    at.B = B; at.H = h->H; at.Hkv = h->Hkv; at.hd = h->hd; at.lmax = h->lmax;
+    at.nsplit = forge_attn_pick_splits(B, h->Hkv, h->lmax);
+    at.partial = h->partial; at.counters = h->counters; at.out = ctx; at.err = h->err;
+    return forge_attn_launch(at, h->stream, pdl);
+}
+
+// x += Wo ctx
+int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool pdl) {
+    const LayerDev& Ld = h->layers[l];
+    ForgeGemvArgs g = gemv_base(h, B);
+    g.w = Ld.o_w; g.s = Ld.o_s; g.N = h->d; g.K = h->qd; g.x = ctx; g.x_stride = h->qd;
+    g.pro = FORGE_PRO_PLAIN; g.epi = FORGE_EPI_RESID; g.y = x; g.y_stride = h->d;
+    return forge_gemv_launch(g, h->stream, pdl);
+}
+
+// x += Wd (silu(Wg n) * (Wu n)), n = RMSNorm(x) * g2
+int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl) {
+    const LayerDev& Ld = h->layers[l];
+    ForgeGemvArgs g = gemv_base(h, B);
+    g.w = Ld.gu_w; g.s = Ld.gu_s; g.N = 2 * h->F; g.K = h->d; g.x = x; g.x_stride = h->d;
+    g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g2; g.eps = h->desc.rms_eps;
+    g.epi = FORGE_EPI_SWIGLU; g.s_out = h->s; g.F = h->F;
+    if (forge_gemv_launch(g, h->stream, pdl)) return -1;
+    g = gemv_base(h, B);
+    g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = h->s; g.x_stride = h->F;
+    g.pro = FORGE_PRO_PLAIN; g.epi = FORGE_EPI_RESID; g.y = x; g.y_stride = h->d;
+    return forge_gemv_launch(g, h->stream, pdl);
+}
+
+// final RMSNorm + LM head into the handle's logits, argmax keys updated
+int enqueue_head(ForgeB200* h, int B, const float* x, bool pdl) {
+    ForgeGemvArgs g = gemv_base(h, B);
+    g.wkind = FORGE_W_BF16;
+    g.w = h->head_w; g.s = nullptr; g.N = h->Vpad; g.K = h->d; g.x = x; g.x_stride = h->d;
     g.pro = FORGE_PRO_RMSNORM; g.gain = h->gF; g.eps = h->desc.rms_eps;
     g.epi = FORGE_EPI_LOGITS; g.y = h->logits; g.y_stride = h->Vpad; g.argmax_key = h->amax; g.nvalid = h->V;
-    if (forge_gemv_launch(g, st, true)) return -1;
+    return forge_gemv_launch(g, h->stream, pdl);
+}
+
+int enqueue_step(ForgeB200* h, int B) {
+    cudaStream_t st = h->stream;
+    if (forge_embed_launch(h->emb, h->d, h->V, h->tok, B, h->x, h->err, st, false)) return -1;
+    for (int l = 0; l < h->L; ++l) {
+        if (enqueue_qkv(h, l, B, h->x, h->q, true) || enqueue_attn(h, l, B, h->q, h->ctx, true) ||
+            enqueue_oproj(h, l, B, h->ctx, h->x, true) || enqueue_mlp(h, l, B, h->x, true))
+            return -1;
+    }
+    if (enqueue_head(h, B, h->x, true)) return -1;
     return forge_argmax_finalize_launch(h->amax, B, h->tok, h->hist, h->step, h->pos, h->hist_cap, st, true);
 }
 
@@ -567,8 +607,15 @@ FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB20
         return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: out of device memory");
     }
     if (cudaHostAlloc((void**)&h->h_tok, 4 * h->Bmax, cudaHostAllocDefault) != cudaSuccess) h->h_tok = nullptr;
-    // RoPE tables in double (nn_lib.hexa:509-531), stored fp32 [lmax][hd/2]
-    {
+    // RoPE tables in double (nn_lib.hexa:509-531), stored fp32 [lmax][hd/2];
+    // rope_theta <= 0 turns the rotation off (cos 1, sin 0), the form of the
+    // reference's single-layer decode check (tool/decode_eager_baseline.cu)
+    if (m.rope_theta <= 0.f) {
+        const size_t n = (size_t)h->lmax * (h->hd / 2);
+        std::vector<float> c(n, 1.0f), s(n, 0.0f);
+        cudaMemcpy(h->rope_cos, c.data(), n * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(h->rope_sin, s.data(), n * 4, cudaMemcpyHostToDevice);
+    } else {
         const int half = h->hd / 2;
         std::vector<float> c((size_t)h->lmax * half), s((size_t)h->lmax * half);
         const double lnb = std::log((double)m.rope_theta);
@@ -694,6 +741,23 @@ FORGE_API int forge_b200_get_kv(ForgeB200* h, int layer, int seq, uint16_t* k_ou
     return 0;
 }
 
+FORGE_API int forge_b200_set_kv(ForgeB200* h, int layer, int seq, const uint16_t* k, const uint16_t* v, int n_pos) {
+    if (!h || layer < 0 || layer >= h->L || seq < 0 || seq >= h->Bmax || !k || !v || n_pos < 0 || n_pos > h->lmax)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_set_kv: bad args");
+    cudaSetDevice(h->device);
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess) return forge_fail(-1, "forge_b200_set_kv: sync failed");
+    const size_t per_seq = (size_t)h->Hkv * h->lmax * h->hd;
+    const size_t off = (size_t)layer * h->kv_layer + (size_t)seq * per_seq;
+    const size_t row = (size_t)h->hd * 2, pitch = (size_t)h->lmax * row;
+    // host [Hkv][n_pos][hd] -> cache [Hkv][lmax][hd]
+    if (n_pos && (cudaMemcpy2D(h->kc + off, pitch, k, (size_t)n_pos * row, (size_t)n_pos * row, h->Hkv,
+                               cudaMemcpyHostToDevice) != cudaSuccess ||
+                  cudaMemcpy2D(h->vc + off, pitch, v, (size_t)n_pos * row, (size_t)n_pos * row, h->Hkv,
+                               cudaMemcpyHostToDevice) != cudaSuccess))
+        return forge_fail(-1, "forge_b200_set_kv: H2D failed");
+    return 0;
+}
+
 // Enqueues one decode step: the fused persistent kernel when it fits, else
 // the captured multi-kernel graph.
 int enqueue_one(ForgeB200* h, int B) {
@@ -803,4 +867,75 @@ FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
     int per_layer = launches(h->d) * 2 + launches(h->qd) + launches(h->F) + 1;
     return 1 + h->L * per_layer + forge_gemv_launch_count(h->d, batch, split, false) + 1;
 }
+int64_t forge_b200_width(const ForgeB200* h, int which) {
+    if (!h) return 0;
+    return which == 0 ? h->d : which == 1 ? h->qd : h->V;
+}
+
+// ---- block-level entries (the v2 fused families) ------------------------------
+// Each runs one block of one layer on the handle's stream, on device arrays
+// the caller owns, at the handle's current positions; they are the pieces
+// forge_b200_decode_step chains, with the same kernels and arguments.
+namespace {
+int check_block(ForgeB200* h, int layer, int B) {
+    if (int rc = check_ready(h, B)) return rc;
+    if (layer < 0 || layer >= h->L) return forge_fail(FORGE_INVALID_ARGS, "forge_b200: layer %d outside 0..%d", layer, h->L - 1);
+    return 0;
+}
+}  // namespace
+
+FORGE_API int forge_b200_qkv_rope(ForgeB200* h, int layer, int batch, const float* x, float* q) {
+    if (int rc = check_block(h, layer, batch)) return rc;
+    if (!x || !q) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_qkv_rope: null array");
+    return enqueue_qkv(h, layer, batch, x, q, false);
+}
+
+FORGE_API int forge_b200_attention(ForgeB200* h, int layer, int batch, const float* q, float* ctx) {
+    if (int rc = check_block(h, layer, batch)) return rc;
+    if (!q || !ctx) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_attention: null array");
+    return enqueue_attn(h, layer, batch, q, ctx, false);
+}
+
+FORGE_API int forge_b200_o_proj(ForgeB200* h, int layer, int batch, const float* ctx, float* x) {
+    if (int rc = check_block(h, layer, batch)) return rc;
+    if (!ctx || !x) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_o_proj: null array");
+    return enqueue_oproj(h, layer, batch, ctx, x, false);
+}
+
+FORGE_API int forge_b200_mlp(ForgeB200* h, int layer, int batch, const float* x, float* y) {
+    if (int rc = check_block(h, layer, batch)) return rc;
+    if (!x || !y) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_mlp: null array");
+    if (x != y) {
+        cudaError_t e = cudaMemcpyAsync(y, x, (size_t)batch * h->d * 4, cudaMemcpyDeviceToDevice, h->stream);
+        if (e != cudaSuccess) return forge_fail(-1, "forge_b200_mlp: copy: %s", cudaGetErrorString(e));
+    }
+    return enqueue_mlp(h, layer, batch, y, false);
+}
+
+FORGE_API int forge_b200_lm_head(ForgeB200* h, int batch, const float* x, int32_t* tok, float* logits) {
+    if (int rc = check_ready(h, batch)) return rc;
+    if (!x || !tok) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_lm_head: null array");
+    if (enqueue_head(h, batch, x, false)) return -1;
+    k_argmax_extract<<<1, 1024, 0, h->stream>>>(h->amax, batch, tok);
+    if (int rc = forge_check_launch("argmax extract")) return rc;
+    if (logits) {
+        cudaError_t e = cudaMemcpy2DAsync(logits, (size_t)h->V * 4, h->logits, (size_t)h->Vpad * 4, (size_t)h->V * 4,
+                                          batch, cudaMemcpyDeviceToDevice, h->stream);
+        if (e != cudaSuccess) return forge_fail(-1, "forge_b200_lm_head: logits copy: %s", cudaGetErrorString(e));
+    }
+    return 0;
+}
+
+FORGE_API int forge_b200_embed(ForgeB200* h, int batch, const int32_t* tok, float* x) {
+    if (int rc = check_ready(h, batch)) return rc;
+    if (!tok || !x) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_embed: null array");
+    return forge_embed_launch(h->emb, h->d, h->V, tok, batch, x, h->err, h->stream, false);
+}
+
+FORGE_API int forge_b200_advance(ForgeB200* h, int batch) {
+    if (int rc = check_ready(h, batch)) return rc;
+    k_add_i32<<<1, 256, 0, h->stream>>>(h->pos, batch, 1);
+    return forge_check_launch("advance positions");
+}
 }  // extern "C"
+

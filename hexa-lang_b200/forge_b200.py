@@ -46,6 +46,54 @@ class ForgeArgs(C.Structure):
     _fields_ = [("farr_ids", C.c_int64 * 8), ("count", C.c_int)]
 
 
+class HexaFarrBf16(C.Structure):
+    """Same layout for HexaFarrF32 / HexaFarrI32 (4-byte elements)."""
+    _fields_ = [("h_buf", C.c_void_p), ("d_buf", C.c_void_p), ("len", C.c_int64), ("loc", C.c_int),
+                ("owns", C.c_int)]
+
+
+HexaFarrF32 = HexaFarrI32 = HexaFarrBf16
+
+
+class HexaFarrW(C.Structure):
+    _fields_ = [("d_tiles", C.c_void_p), ("d_scales", C.c_void_p), ("rows", C.c_int64), ("cols", C.c_int64),
+                ("tile_bytes", C.c_int64), ("scale_bytes", C.c_int64), ("kind", C.c_int32), ("group", C.c_int32),
+                ("packed", C.c_int32), ("owns", C.c_int32)]
+
+
+class HexaKvCache(C.Structure):
+    _fields_ = [("d_k", C.c_void_p), ("d_v", C.c_void_p), ("d_pos", C.c_void_p), ("n_layer", C.c_int64),
+                ("batch", C.c_int64), ("n_kv_head", C.c_int64), ("max_ctx", C.c_int64), ("head_dim", C.c_int64),
+                ("owns", C.c_int), ("reserved", C.c_int)]
+
+
+# v1 / v2 constants (include/forge_tier_v1.h, include/forge_b200.h)
+FORGE_OK, FORGE_FALLBACK_USED, FORGE_KERNEL_UNSUPPORTED = 0, 1, -1
+FORGE_REGIME_UNSUPPORTED, FORGE_PRECISION_UNSUPPORTED, FORGE_INVALID_ARGS, FORGE_ABI_MISMATCH = -2, -3, -4, -5
+FORGE_KERNEL_MATMUL, FORGE_KERNEL_FFN_FUSED, FORGE_KERNEL_FWD_BWD_LINEAR = 1, 2, 3
+FORGE_KERNEL_ATTN_DT_FWD, FORGE_KERNEL_ATTN_DT_BWD, FORGE_KERNEL_RMSNORM_MH = 4, 5, 6
+FORGE_KERNEL_SILU_GATE, FORGE_KERNEL_ROPE_MH = 7, 8
+FORGE_KERNEL_GEMV_W4A16_G128, FORGE_KERNEL_GEMV_BF16, FORGE_KERNEL_QKV_ROPE_FUSED = 16, 17, 18
+FORGE_KERNEL_FLASH_DECODE, FORGE_KERNEL_SWIGLU_FUSED, FORGE_KERNEL_LMHEAD_ARGMAX = 19, 20, 21
+FORGE_KERNEL_FLASH_PREFILL, FORGE_KERNEL_DECODE_STEP = 22, 23
+FORGE_PREC_FP64, FORGE_PREC_LAYERCAST_BF16_FP32, FORGE_PREC_PURE_BF16, FORGE_PREC_W4A16_G128_BF16 = 0, 1, 2, 3
+FORGE_DET_DEFAULT, FORGE_DET_PEDANTIC = 0, 1
+HEXA_FARR_W_BF16, HEXA_FARR_W_Q4_G128 = 0, 1
+
+
+def forge_args(*slots) -> ForgeArgs:
+    """ForgeArgs from descriptor pointers (ctypes objects or ints)."""
+    a = ForgeArgs()
+    for i, v in enumerate(slots):
+        if v is None:
+            v = 0
+        elif not isinstance(v, int):
+            v = C.cast(v, C.c_void_p).value or 0
+        a.farr_ids[i] = v
+    a.count = len(slots)
+    return a
+
+
 def build(force: bool = False) -> str:
     """Compiles libforge_b200.so for sm_100a with nvcc (no GPU needed)."""
     if force or not os.path.exists(LIB_PATH):
@@ -102,6 +150,42 @@ def lib() -> C.CDLL:
             "forge_q4_scale_tile_bytes": (i64, [i64, i64, i32]),
             "forge_ops_check": (i32, []),
             "forge_api_version_v1": (C.c_uint32, []),
+            "forge_tier_dispatch_v1": (i32, [i32, C.POINTER(ForgeShapeInfo), i32, i32, i32,
+                                             C.POINTER(ForgeArgs), C.POINTER(ForgeArgs)]),
+            "forge_tier_dispatch_v2": (i32, [i32, C.POINTER(ForgeShapeInfo), i32, i32, i32,
+                                             C.POINTER(ForgeArgs), C.POINTER(ForgeArgs)]),
+            "forge_register_specialized_v1": (i32, [i32, C.POINTER(ForgeShapeInfo), i32, i32, vp]),
+            "forge_b200_embed": (i32, [vp, i32, vp, vp]),
+            "forge_b200_qkv_rope": (i32, [vp, i32, i32, vp, vp]),
+            "forge_b200_attention": (i32, [vp, i32, i32, vp, vp]),
+            "forge_b200_o_proj": (i32, [vp, i32, i32, vp, vp]),
+            "forge_b200_mlp": (i32, [vp, i32, i32, vp, vp]),
+            "forge_b200_lm_head": (i32, [vp, i32, vp, vp, vp]),
+            "forge_b200_advance": (i32, [vp, i32]),
+            "forge_b200_set_kv": (i32, [vp, i32, i32, vp, vp, i32]),
+            "hexa_farr_bf16_alloc": (C.POINTER(HexaFarrBf16), [i64]),
+            "hexa_farr_bf16_free": (None, [C.POINTER(HexaFarrBf16)]),
+            "hexa_farr_bf16_from_f64": (i32, [vp, C.POINTER(HexaFarrBf16), i64]),
+            "hexa_farr_bf16_to_f64": (i32, [C.POINTER(HexaFarrBf16), vp, i64]),
+            "hexa_farr_bf16_to_device": (i32, [C.POINTER(HexaFarrBf16)]),
+            "hexa_farr_bf16_to_host": (i32, [C.POINTER(HexaFarrBf16)]),
+            "hexa_farr_f32_alloc": (C.POINTER(HexaFarrF32), [i64]),
+            "hexa_farr_f32_free": (None, [C.POINTER(HexaFarrF32)]),
+            "hexa_farr_f32_to_device": (i32, [C.POINTER(HexaFarrF32)]),
+            "hexa_farr_f32_to_host": (i32, [C.POINTER(HexaFarrF32)]),
+            "hexa_farr_i32_alloc": (C.POINTER(HexaFarrI32), [i64]),
+            "hexa_farr_i32_free": (None, [C.POINTER(HexaFarrI32)]),
+            "hexa_farr_i32_to_device": (i32, [C.POINTER(HexaFarrI32)]),
+            "hexa_farr_i32_to_host": (i32, [C.POINTER(HexaFarrI32)]),
+            "hexa_farr_w_alloc": (C.POINTER(HexaFarrW), [i32, i64, i64]),
+            "hexa_farr_q4_alloc": (C.POINTER(HexaFarrW), [i64, i64, i32]),
+            "hexa_farr_w_pack": (i32, [C.POINTER(HexaFarrW), C.POINTER(HexaFarrBf16)]),
+            "hexa_farr_q4_unpack": (i32, [C.POINTER(HexaFarrW), vp, vp]),
+            "hexa_farr_w_free": (None, [C.POINTER(HexaFarrW)]),
+            "hexa_kv_alloc": (C.POINTER(HexaKvCache), [i64, i64, i64, i64, i64]),
+            "hexa_kv_free": (None, [C.POINTER(HexaKvCache)]),
+            "hexa_kv_set_positions": (i32, [C.POINTER(HexaKvCache), vp, i64]),
+            "hexa_kv_write": (i32, [C.POINTER(HexaKvCache), i64, i64, vp, vp, i64]),
             "forge_api_version_v2": (C.c_uint32, []),
         }
         for name, (res, args) in sig.items():
@@ -184,6 +268,35 @@ class ForgeModel:
         v = np.zeros_like(k)
         check(lib().forge_b200_get_kv(self.h, layer, seq, _ptr(k), _ptr(v)), "get_kv")
         return k, v
+
+    def set_kv(self, layer, seq, k, v):
+        """k, v: host bf16 bit patterns [n_kv_head][n_pos][head_dim]."""
+        import numpy as np
+        k = np.ascontiguousarray(k, np.uint16)
+        v = np.ascontiguousarray(v, np.uint16)
+        check(lib().forge_b200_set_kv(self.h, layer, seq, _ptr(k), _ptr(v), k.shape[1]), "set_kv")
+
+    # block-level entries on device arrays (torch CUDA tensors), handle stream
+    def embed(self, batch, tok, x):
+        check(lib().forge_b200_embed(self.h, batch, _ptr(tok), _ptr(x)), "embed")
+
+    def qkv_rope(self, layer, batch, x, q):
+        check(lib().forge_b200_qkv_rope(self.h, layer, batch, _ptr(x), _ptr(q)), "qkv_rope")
+
+    def attention(self, layer, batch, q, ctx):
+        check(lib().forge_b200_attention(self.h, layer, batch, _ptr(q), _ptr(ctx)), "attention")
+
+    def o_proj(self, layer, batch, ctx, x):
+        check(lib().forge_b200_o_proj(self.h, layer, batch, _ptr(ctx), _ptr(x)), "o_proj")
+
+    def mlp(self, layer, batch, x, y):
+        check(lib().forge_b200_mlp(self.h, layer, batch, _ptr(x), _ptr(y)), "mlp")
+
+    def lm_head(self, batch, x, tok, logits=None):
+        check(lib().forge_b200_lm_head(self.h, batch, _ptr(x), _ptr(tok), _ptr(logits)), "lm_head")
+
+    def advance(self, batch):
+        check(lib().forge_b200_advance(self.h, batch), "advance")
 
     def step(self, tokens, want_logits=False):
         import numpy as np

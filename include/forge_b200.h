@@ -24,6 +24,7 @@
 #define FORGE_B200_H
 #include <stdint.h>
 #include "forge_tier_v1.h"
+#include "forge_farr.h"
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -42,13 +43,45 @@ uint32_t forge_api_version_v2(void);
 #define FORGE_KERNEL_DECODE_STEP      23
 #define FORGE_PREC_W4A16_G128_BF16    3
 
+/* Dispatch of the v2 families; same arguments and return codes as
+ * forge_tier_dispatch_v1 (v1 families are forwarded to it unchanged).
+ * Slots hold descriptor pointers cast through intptr_t, or plain integers
+ * where marked. Device work runs on the legacy default stream (handle
+ * families: on the handle's stream) and is not waited for, except
+ * DECODE_STEP, which is synchronous.
+ *   GEMV_W4A16_G128 (precision FORGE_PREC_W4A16_G128_BF16), GEMV_BF16
+ *   (FORGE_PREC_PURE_BF16): in = [HexaFarrW* W, HexaFarrF32* X [M][K]],
+ *     out = [HexaFarrF32* Y [M][N]]; shape N = rows of W, K, M = sequences.
+ *   FLASH_DECODE (PURE_BF16): in = [HexaFarrF32* Q [M][N*hd],
+ *     HexaKvCache*, layer (integer)], out = [HexaFarrF32* O [M][N*hd]];
+ *     shape M = sequences, N = query heads; attends to positions 0..pos.
+ *   QKV_ROPE_FUSED, SWIGLU_FUSED, LMHEAD_ARGMAX, DECODE_STEP (either
+ *   precision; the handle's weights decide): in[0] = ForgeB200*, shape
+ *   batch (or M) = sequences.
+ *     QKV_ROPE_FUSED: in = [h, layer, HexaFarrF32* X [B][d]],
+ *       out = [HexaFarrF32* Q [B][H*hd]]; K/V appended at the positions.
+ *     SWIGLU_FUSED: in = [h, layer, X [B][d]], out = [Y [B][d]],
+ *       Y = X + Wd (silu(Wg n) * Wu n), n = RMSNorm(X).
+ *     LMHEAD_ARGMAX: in = [h, X [B][d]], out = [HexaFarrI32* TOK [B],
+ *       optional HexaFarrF32* LOGITS [B][V]].
+ *     DECODE_STEP: in = [h, HexaFarrI32* TOK [B] (host copy)],
+ *       out = [HexaFarrI32* NEXT [B], optional HexaFarrF32* LOGITS] (host).
+ *   FLASH_PREFILL (PURE_BF16): in = [HexaFarrBf16* Q, K, V [M][N][S][K]],
+ *     out = [HexaFarrBf16* O [M][N][S][K]]; shape M = batch, N = heads,
+ *     K = head_dim (128), batch = S; causal. */
+int forge_tier_dispatch_v2(int kernel_family, const ForgeShapeInfo* shape, int regime_hint,
+                           int precision_policy, int det_mode, const ForgeArgs* in, const ForgeArgs* out);
+
+/* Reads and clears the error word of the per-op kernels (synchronises). */
+int forge_ops_check(void);
+
 /* ---- model ------------------------------------------------------------- */
 #define FORGE_WEIGHT_BF16     0
 #define FORGE_WEIGHT_Q4_G128  1
 
 typedef struct ForgeModelDesc {
     int32_t n_layer, d_model, n_head, n_kv_head, head_dim, ffn, vocab;
-    float   rms_eps, rope_theta;
+    float   rms_eps, rope_theta;  /* rope_theta <= 0: no rotary embedding */
     int32_t weight_kind;   /* FORGE_WEIGHT_*                                      */
     int32_t tied_head;     /* 1: LM head = embedding table (flame ties them)      */
     int32_t max_batch;     /* sequences decoded together                          */
@@ -87,6 +120,9 @@ int forge_b200_reset(ForgeB200* h);
 int forge_b200_fill_kv_synthetic(ForgeB200* h, uint64_t seed, int ctx_len, float std);
 int forge_b200_set_positions(ForgeB200* h, const int32_t* pos, int batch);
 int forge_b200_get_kv(ForgeB200* h, int layer, int seq, uint16_t* k_out, uint16_t* v_out);
+/* Writes positions [0, n_pos) of one sequence's K/V cache from host
+ * [n_kv_head][n_pos][head_dim] bf16 arrays (synchronous). */
+int forge_b200_set_kv(ForgeB200* h, int layer, int seq, const uint16_t* k, const uint16_t* v, int n_pos);
 
 /* One decode step from host buffers (H2D tokens, graph launch, D2H next
  * tokens and optional logits [batch][vocab]); synchronous. */
@@ -113,6 +149,26 @@ int forge_b200_step_trace(ForgeB200* h, unsigned long long* out, int cap);
 int forge_b200_uses_fused_step(ForgeB200* h, int batch);
 /* Kernel launches per decode step (for the bench's launch count). */
 int forge_b200_launches_per_step(ForgeB200* h, int batch);
+
+/* Block-level entries: one block of one layer on the handle's stream, on
+ * device fp32 arrays the caller owns, at the handle's current positions
+ * (the pieces forge_b200_decode_step chains, with the same kernels).
+ *   embed:     x[b] = emb[tok[b]]                      (tok: device int32)
+ *   qkv_rope:  q = RoPE(Wq n), K/V = (RoPE(Wk n), Wv n) appended at pos,
+ *              n = RMSNorm(x) * g1
+ *   attention: ctx = softmax(q K^T / sqrt(hd)) V over positions 0..pos
+ *   o_proj:    x += Wo ctx
+ *   mlp:       y = x + Wd (silu(Wg n) * Wu n), n = RMSNorm(x) * g2 (x may be y)
+ *   lm_head:   tok = argmax(head RMSNorm(x) * gF), lowest index on ties;
+ *              logits [batch][vocab] when not NULL
+ *   advance:   pos += 1 for the first `batch` sequences */
+int forge_b200_embed(ForgeB200* h, int batch, const int32_t* tok, float* x);
+int forge_b200_qkv_rope(ForgeB200* h, int layer, int batch, const float* x, float* q);
+int forge_b200_attention(ForgeB200* h, int layer, int batch, const float* q, float* ctx);
+int forge_b200_o_proj(ForgeB200* h, int layer, int batch, const float* ctx, float* x);
+int forge_b200_mlp(ForgeB200* h, int layer, int batch, const float* x, float* y);
+int forge_b200_lm_head(ForgeB200* h, int batch, const float* x, int32_t* tok, float* logits);
+int forge_b200_advance(ForgeB200* h, int batch);
 
 /* ---- per-op entries on caller-owned device memory ------------------------ */
 /* y[b][n] = sum_k W[n][k] x[b][k]: W packed int4 (forge_q4_pack_tiles) or

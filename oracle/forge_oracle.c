@@ -579,3 +579,12 @@ void or_matmul_f64(const double* A, const double* B, double* C, int M, int K, in
             C[(size_t)i * N + j] = acc;
         }
 }
+
+void or_ref_lcg_f32(uint32_t* state, float* out, int64_t n) {
+    uint32_t st = *state;
+    for (int64_t i = 0; i < n; ++i) {
+        st = st * 1664525u + 1013904223u;
+        out[i] = ((float)(st >> 8) / (float)(1u << 24)) - 0.5f;
+    }
+    *state = st;
+}

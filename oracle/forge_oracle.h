@@ -112,6 +112,12 @@ void or_flash_decode_single(const float* q, const float* K, const float* V,
 void or_matmul_f64(const double* A, const double* B, double* C, int M, int K, int N);
 
 int  or_num_threads(void);
+
+/* Input generator of the reference's single-layer decode check
+ * (tool/decode_eager_baseline.cu:53-54): state = state*1664525 + 1013904223
+ * (mod 2^32), value = (state >> 8) / 2^24 - 0.5 in float. Writes n values
+ * and advances *state. */
+void or_ref_lcg_f32(uint32_t* state, float* out, int64_t n);
 #ifdef __cplusplus
 }
 #endif

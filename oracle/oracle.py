@@ -68,6 +68,7 @@ def lib() -> C.CDLL:
             "or_flash_decode_single": (None, [vp, vp, vp, i32, i32, i32, vp]),
             "or_matmul_f64": (None, [vp, vp, vp, i32, i32, i32]),
             "or_num_threads": (i32, []),
+            "or_ref_lcg_f32": (None, [vp, vp, i64]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -176,6 +177,9 @@ class OracleModel:
 
     def _mat(self, w_bf16, q4):
         rows, cols = w_bf16.shape
+        if w_bf16.dtype == np.float32:  # fp32 weights (the reference's own check inputs)
+            w = self._k(np.ascontiguousarray(w_bf16))
+            return OrMat(OR_MAT_F32, 0, rows, cols, P(w), None)
         if q4:
             codes, scales = q4g_quantize(w_bf16)
             self._k(codes), self._k(scales)
@@ -216,6 +220,53 @@ class OracleModel:
 
 
 # ---- the reference's own single-layer decode (tool/decode_eager_baseline.cu) ---
+REF_D, REF_NH, REF_HD, REF_FF = 768, 12, 64, 3072  # its fixed #defines (:42-45)
+
+
+def ref_inputs(L):
+    """The inputs of the reference's single-layer decode check at cache length
+    L, drawn from its LCG in the order of its main()
+    (tool/decode_eager_baseline.cu:209-219); fp32 arrays."""
+    D, FF = REF_D, REF_FF
+    st = np.array([0x12345678], np.uint32)
+
+    def draw(n):
+        out = np.empty(n, np.float32)
+        lib().or_ref_lcg_f32(P(st), P(out), n)
+        return out
+    wq = np.float32(0.036)
+    a = draw(3 * D).reshape(D, 3)
+    x = a[:, 0].copy()
+    g1 = np.float32(1) + np.float32(0.1) * a[:, 1]
+    g2 = np.float32(1) + np.float32(0.1) * a[:, 2]
+    b = draw(4 * D * D).reshape(D * D, 4) * wq
+    Wq, Wk, Wv, Wo = (b[:, i].reshape(D, D).copy() for i in range(4))
+    c = draw(2 * FF * D).reshape(FF * D, 2) * wq
+    Wg, Wu = (c[:, i].reshape(FF, D).copy() for i in range(2))
+    Wd = (draw(D * FF) * np.float32(0.018)).reshape(D, FF)
+    kv = draw(2 * L * D).reshape(L * D, 2)
+    Kc = (kv[:, 0] * wq * np.float32(0.5)).reshape(L, D)
+    Vc = kv[:, 1].reshape(L, D).copy()
+    return dict(x=x, g1=g1, g2=g2, Wq=Wq, Wk=Wk, Wv=Wv, Wo=Wo, Wg=Wg, Wu=Wu, Wd=Wd, Kc=Kc, Vc=Vc)
+
+
+def ref_layer_via_oracle(inp, L, flags=OR_NO_ROPE):
+    """The oracle's decode step at the reference check's shape: one MHA layer
+    (12 heads x 64), fp32 weights, fp32 cache with L rows, no RoPE, eps 1e-5;
+    the input row is supplied as a one-row embedding table. Returns the
+    layer's output hidden state (f64, [768])."""
+    D, NH, HD, FF = REF_D, REF_NH, REF_HD, REF_FF
+    w = {(0, "wq"): inp["Wq"], (0, "wk"): inp["Wk"], (0, "wv"): inp["Wv"], (0, "wo"): inp["Wo"],
+         (0, "wg"): inp["Wg"], (0, "wu"): inp["Wu"], (0, "wd"): inp["Wd"],
+         "emb": inp["x"].reshape(1, D).astype(np.float32)}
+    gains = {(0, "g1"): inp["g1"].astype(np.float32), (0, "g2"): inp["g2"].astype(np.float32),
+             "gF": np.ones(D, np.float32)}
+    m = OracleModel(1, D, NH, NH, HD, FF, 1, tied=True, eps=1e-5, weights=(w, gains))
+    kc, vc = m.new_cache(1, L + 1)
+    kc[0, 0, :, :L, :] = inp["Kc"].reshape(L, NH, HD).transpose(1, 0, 2)
+    vc[0, 0, :, :L, :] = inp["Vc"].reshape(L, NH, HD).transpose(1, 0, 2)
+    _, _, hid = m.decode_step(kc, vc, [0], [L], flags=flags, want_hidden=True)
+    return hid[0]
 def ref_lib():
     """libcpu_ref.so built by oracle/Makefile from the reference source, or None."""
     if not os.path.exists(REF_LIB):
