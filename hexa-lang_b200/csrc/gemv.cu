@@ -41,6 +41,9 @@ namespace {
 #ifndef FORGE_GEMV_STAGES
 #define FORGE_GEMV_STAGES 4
 #endif
+#ifndef FORGE_GEMV_MIN_BLOCKS
+#define FORGE_GEMV_MIN_BLOCKS 1
+#endif
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStages = FORGE_GEMV_STAGES;
@@ -53,7 +56,7 @@ constexpr int kFixedSmem = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats 
 constexpr int kMaxSmem = 227 * 1024;
 
 template <int WK, int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) k_gemv(const ForgeGemvArgs a) {
+__global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const ForgeGemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stages = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);

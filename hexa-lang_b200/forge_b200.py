@@ -16,7 +16,7 @@ import os
 import subprocess
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libforge_b200.so")
+LIB_PATH = os.environ.get("FORGE_B200_LIB") or os.path.join(HERE, "libforge_b200.so")
 
 FORGE_WEIGHT_BF16 = 0
 FORGE_WEIGHT_Q4_G128 = 1
