@@ -35,6 +35,17 @@ CTX = 2048
 GEMV_TRAFFIC = None
 
 
+def _tc_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
+TC_PEAK = _tc_peak()
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -143,6 +154,33 @@ def time_dominant_gemv(fb, torch, dev, K=4096, N=2 * 11008, copies=4, reps=20):
     ms = e0.elapsed_time(e1) / reps
     nbytes = lib.forge_q4_tile_bytes(N, K) + lib.forge_q4_scale_tile_bytes(N, K, 128) + 4 * K + 4 * N
     return ms, nbytes
+
+
+def time_prefill(fb, torch, dev, B=8, H=32, S=4096, reps=10):
+    """Causal flash-attention prefill on the tcgen05 kernel: bf16 Q/K/V
+    ~N(0,1) [B][H][S][128] (805 MB, larger than L2). Algorithmic FLOPs:
+    4 * B * H * S^2 * hd / 2 (causal half)."""
+    q, k, v = (torch.randn(B, H, S, 128, device=dev).to(torch.bfloat16) for _ in range(3))
+    o = torch.empty_like(q)
+    lib = fb.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    run = lambda: lib.forge_flash_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S, 128, 1,
+                                          stream)
+    for _ in range(3):
+        fb.check(run(), "prefill")
+    torch.cuda.synchronize()
+    fb.check(lib.forge_ops_check(), "prefill error word")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = 4.0 * B * H * S * S * 128 / 2
+    return {"workload": f"flash prefill B{B} H{H} S{S} hd128 causal bf16", "ms": ms, "tflops": flops / ms / 1e9,
+            "peak_tflops": TC_PEAK, "frac": flops / ms / 1e9 / TC_PEAK, "peak_kind": "measured bf16 burst",
+            "launches": reps}
 
 
 def cpu_sample(batch, ctx, reps=2):
@@ -256,6 +294,8 @@ def main():
     ap.add_argument("--also-batch", type=int, nargs="*", default=[32],
                     help="further batch sizes measured after the main one (reported under batch_sweep)")
     ap.add_argument("--only-gemv", action="store_true", help="run only the dominant GEMV (for profiling)")
+    ap.add_argument("--only-prefill", action="store_true", help="run only the flash prefill (for profiling)")
+    ap.add_argument("--no-prefill", action="store_true")
     args = ap.parse_args()
     world, rank, local, pg = dist_setup()
     if args.impl == "reference":
@@ -271,6 +311,9 @@ def main():
         ms, nbytes = time_dominant_gemv(fb, torch, dev, reps=3)
         print(json.dumps({"kernel": "k_gemv int4 22016x4096 bs1", "ms": ms, "bytes": nbytes}))
         return
+    if args.only_prefill:
+        print(json.dumps(time_prefill(fb, torch, dev, B=2, H=8, S=4096, reps=2)))
+        return
     B, K, W = args.batch, args.steps, max(3, args.warmup)
     r = run_decode(fb, torch, pg, local, world, rank, B, K, W)
     extra = []
@@ -281,6 +324,7 @@ def main():
     peak, peak_kind = peaks()
     gemv_ms, gemv_bytes = time_dominant_gemv(fb, torch, dev)
     achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
+    prefill = None if args.no_prefill else time_prefill(fb, torch, dev)
     if rank != 0:
         return
     cpu = None if args.no_cpu else cpu_sample(B, CTX)
@@ -303,6 +347,7 @@ def main():
         "gpu_launches": r["gpu_launches"],
         "clocks": r["clocks"],
         "batch_sweep": extra,
+        "prefill": prefill,
         "cpu_baseline": cpu,
     }
     print(json.dumps(out))

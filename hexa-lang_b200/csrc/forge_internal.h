@@ -128,5 +128,7 @@ struct ForgeArgs;
 // Row widths of a handle's activations: 0 model dim, 1 query width H*hd,
 // 2 vocabulary; 0 for a null handle.
 extern "C" int64_t forge_b200_width(const ForgeB200* h, int which);
+// Per-device error word of the per-op entries (created on first use).
+uint32_t* forge_ops_err_word();
 // v2 FLASH_PREFILL family.
 int forge_prefill_dispatch(const ForgeShapeInfo* s, const ForgeArgs* in, const ForgeArgs* out);

@@ -24,6 +24,11 @@ uint32_t* err_word() {
     return g_err[dev];
 }
 
+}  // namespace
+
+uint32_t* forge_ops_err_word() { return err_word(); }
+
+namespace {
 int gemv_entry(int wkind, const void* tiles, const void* stiles, int64_t N, int64_t K, const float* x, int batch,
                float* y, int exact, void* stream) {
     if (!tiles || !x || !y || batch <= 0 || N <= 0 || K <= 0 || N > (1ll << 30) || K > (1ll << 30))

@@ -1,10 +1,364 @@
-// prefill.cu — causal flash-attention prefill (v2 FLASH_PREFILL family).
+// prefill.cu — causal flash-attention prefill on the 5th-generation tensor
+// cores (tcgen05 + TMEM, TMA-fed), head_dim 128, bf16 in / bf16 out, fp32
+// accumulation.
+//
+// Semantics follow nn_attn_core_fwd (stdlib/flame/nn_lib.hexa:221-278):
+// O = softmax(Q K^T / sqrt(hd) + causal mask) V per (batch, head), the mask
+// hiding keys after the query. The reference's own fused prefill kernel
+// (tool/r14_walls/flash_attn_bm32_bk32_v0.cu:75) is fp16 wmma at d = 64
+// and non-causal only; this is a new kernel for hd = 128 with the mask.
+//
+// One CTA owns 128 query rows of one (batch, head) and walks the key blocks
+// of 128 up to the diagonal:
+//   warp 4 (one lane)  TMA: the Q tile once, K/V tiles through a 2-stage ring
+//                      (128-byte swizzled boxes of 64 columns x 128 rows);
+//   warp 5 (one lane)  tensor-core issue: S = Q K^T into TMEM columns 0-127
+//                      (8 x K16 steps), then O += P V into columns 128-255;
+//   warps 0-3          softmax, one thread per query row: S row out of TMEM,
+//                      online max / sum in fp32 (exp2 with the scale folded
+//                      in), O rescaled in TMEM when the row max moved, P
+//                      written as bf16 into shared memory in the same
+//                      swizzled K-major layout TMA gives Q and K, then the
+//                      final O / l written to global memory.
+// Every wait is bounded (error word, then the CTA drains its copies and
+// tensor-core work and frees its TMEM).
+#include <mutex>
+#include "tcgen05.cuh"
 #include "forge_internal.h"
 #include "../../include/forge_b200.h"
 #include "../../include/forge_farr.h"
 
+namespace {
+constexpr int kHD = 128;                  // head dim (the K of S = Q K^T)
+constexpr int kBM = 128;                  // query rows per CTA
+constexpr int kBN = 128;                  // keys per block
+constexpr int kTile = kBM * kHD * 2;      // 32 KB: one Q / K / V / P tile
+constexpr int kHalf = kTile / 2;          // 16 KB: 64 columns x 128 rows, swizzled
+constexpr int kThreads = 192;
+constexpr int kOffQ = 0, kOffK0 = kTile, kOffV0 = 2 * kTile, kOffK1 = 3 * kTile, kOffV1 = 4 * kTile,
+              kOffP = 5 * kTile, kOffBar = 6 * kTile;
+constexpr int kSmem = kOffBar + 256 + 1024;  // + barriers / TMEM slot + alignment slack
+constexpr uint32_t kTmemCols = 256;       // S: 0-127, O: 128-255
+constexpr uint32_t kIdescS = umma_idesc_bf16_f32(kBM, kBN, false);  // B = K rows, K-major
+constexpr uint32_t kIdescO = umma_idesc_bf16_f32(kBM, kHD, true);   // B = V rows, MN-major
+
+struct PrefillArgs {
+    uint16_t* o;
+    int B, H, S, causal;
+    float scale_log2;  // log2(e) / sqrt(hd)
+    uint32_t* err;
+};
+
+// Byte offset of the 16-byte chunk c (columns 8c..8c+7) of row r inside a
+// 128x128 bf16 tile stored as two 128-byte-swizzled halves (the layout a
+// TMA box of 64 x 128 with 128-byte swizzle writes).
+__device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
+    return (uint32_t)((c >> 3) * kHalf + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_flash_prefill(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, const PrefillArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzle atoms
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    const uint32_t sbase = smem_u32(base);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
+    uint64_t* q_full = bars + 0;
+    uint64_t* kv_full = bars + 1;   // [2]
+    uint64_t* kv_empty = bars + 3;  // [2]
+    uint64_t* s_full = bars + 5;
+    uint64_t* p_full = bars + 6;
+    uint64_t* o_done = bars + 7;
+    uint64_t* drain = bars + 8;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 9);
+
+    const int ntile = a.S / kBM;
+    const int qt = ntile - 1 - (int)blockIdx.x;  // longest causal rows first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int nblk = a.causal ? qt + 1 : ntile;
+    const int row0 = (b * a.H + h) * a.S;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // after an earlier CTA's wait ran out, the rest of the grid skips its
+    // work instead of timing out one by one
+    __shared__ uint32_t s_abort;
+    if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile uint32_t*>(a.err);
+    __syncthreads();
+    if (s_abort) return;
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        mbar_init(&kv_full[0], 1);
+        mbar_init(&kv_full[1], 1);
+        mbar_init(&kv_empty[0], 1);
+        mbar_init(&kv_empty[1], 1);
+        mbar_init(s_full, 1);
+        mbar_init(p_full, 128);
+        mbar_init(o_done, 1);
+        mbar_init(drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == 5) tmem_alloc(tslot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint32_t tS = tmem, tO = tmem + 128;
+
+    if (warp == 4) {
+        // ------------------------------------------------------------ TMA
+        if (lane == 0) {
+            int issued = 0;
+            mbar_arrive_expect_tx(q_full, kTile);
+            tma_load_2d(base + kOffQ, &tq, 0, row0 + qt * kBM, q_full);
+            tma_load_2d(base + kOffQ + kHalf, &tq, 64, row0 + qt * kBM, q_full);
+            for (int j = 0; j < nblk; ++j) {
+                const int st = j & 1;
+                if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, a.err)) break;
+                uint8_t* kd = base + (st ? kOffK1 : kOffK0);
+                uint8_t* vd = base + (st ? kOffV1 : kOffV0);
+                mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+                tma_load_2d(kd, &tk, 0, row0 + j * kBN, &kv_full[st]);
+                tma_load_2d(kd + kHalf, &tk, 64, row0 + j * kBN, &kv_full[st]);
+                tma_load_2d(vd, &tv, 0, row0 + j * kBN, &kv_full[st]);
+                tma_load_2d(vd + kHalf, &tv, 64, row0 + j * kBN, &kv_full[st]);
+                issued = j + 1;
+            }
+            // every copy issued lands before the CTA exits
+            mbar_wait(q_full, 0, a.err);
+            for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
+                mbar_wait(&kv_full[j & 1], (j >> 1) & 1, a.err);
+        }
+    } else if (warp == 5) {
+        // ---------------------------------------------------- tensor cores
+        if (lane == 0) {
+            bool ok = mbar_wait(q_full, 0, a.err);
+            auto issue_s = [&](int j) {
+                const uint32_t kb = sbase + (uint32_t)((j & 1) ? kOffK1 : kOffK0);
+                const uint32_t qb = sbase + kOffQ;
+#pragma unroll
+                for (int s = 0; s < kHD / 16; ++s) {
+                    const uint32_t off = (uint32_t)((s >> 2) * kHalf + (s & 3) * 32);
+                    umma_bf16(tS, umma_desc_sw128(qb + off, 16, 1024), umma_desc_sw128(kb + off, 16, 1024), kIdescS,
+                              s > 0 ? 1u : 0u);
+                }
+                umma_commit(s_full);
+            };
+            if (ok && mbar_wait(&kv_full[0], 0, a.err)) {
+                tc_fence_after();
+                issue_s(0);
+            } else {
+                ok = false;
+            }
+            for (int j = 0; j < nblk && ok; ++j) {
+                if (!mbar_wait(p_full, j & 1, a.err)) break;
+                tc_fence_after();
+                const uint32_t vb = sbase + (uint32_t)((j & 1) ? kOffV1 : kOffV0);
+                const uint32_t pb = sbase + kOffP;
+#pragma unroll
+                for (int s = 0; s < kBN / 16; ++s) {
+                    const uint32_t aoff = (uint32_t)((s >> 2) * kHalf + (s & 3) * 32);
+                    umma_bf16(tO, umma_desc_sw128(pb + aoff, 16, 1024),
+                              umma_desc_sw128(vb + (uint32_t)s * 2048u, kHalf, 1024), kIdescO,
+                              (j > 0 || s > 0) ? 1u : 0u);
+                }
+                umma_commit(&kv_empty[j & 1]);
+                umma_commit(o_done);
+                if (j + 1 < nblk) {
+                    if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, a.err)) break;
+                    tc_fence_after();
+                    issue_s(j + 1);
+                }
+            }
+            // all tensor-core work of this CTA completes before TMEM is freed
+            umma_commit(drain);
+            mbar_wait(drain, 0, a.err);
+        }
+    } else {
+        // ---------------------------------------------------------- softmax
+        const int r = threadIdx.x;  // query row within the tile
+        const uint32_t lrow = (uint32_t)(warp * 32) << 16;
+        const float c = a.scale_log2;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        uint8_t* P = base + kOffP;
+        // tcgen05.ld / st are warp-collective: a warp leaves the loop as a whole
+        for (int j = 0; j < nblk; ++j) {
+            if (!__all_sync(0xffffffffu, mbar_wait(s_full, j & 1, a.err))) { ok = false; break; }
+            tc_fence_after();
+            uint32_t sv[4][32];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) tmem_ld32(tS + lrow + 32 * q, sv[q]);
+            tmem_wait_ld();
+            const bool diag = a.causal && j == qt;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float x = __uint_as_float(sv[q][i]);
+                    if (diag && 32 * q + i > r) x = -INFINITY;
+                    sv[q][i] = __float_as_uint(x);
+                    mx = fmaxf(mx, x);
+                }
+            const float m_new = fmaxf(m, mx);  // finite: key 0 of a block is never masked for row r >= 0
+            const float alpha = exp2f((m - m_new) * c);
+            if (j > 0) {
+                if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, a.err))) { ok = false; break; }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint32_t ov[32];
+                        tmem_ld32(tO + lrow + 32 * q, ov);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                        tmem_st32(tO + lrow + 32 * q, ov);
+                    }
+                }
+            }
+            const float mc = m_new * c;
+            float sum = 0.f;
+#pragma unroll
+            for (int ch = 0; ch < 16; ++ch) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int col = ch * 8 + 2 * e;
+                    const float p0 = exp2f(fmaf(__uint_as_float(sv[col >> 5][col & 31]), c, -mc));
+                    const float p1 = exp2f(fmaf(__uint_as_float(sv[(col + 1) >> 5][(col + 1) & 31]), c, -mc));
+                    sum += p0 + p1;
+                    pk[e] = (uint32_t)f32_to_bf16_bits(p0) | ((uint32_t)f32_to_bf16_bits(p1) << 16);
+                }
+                *reinterpret_cast<uint4*>(P + sw128_chunk(r, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+            l = l * alpha + sum;
+            m = m_new;
+            tmem_wait_st();
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && __all_sync(0xffffffffu, mbar_wait(o_done, (nblk - 1) & 1, a.err))) {
+            tc_fence_after();
+            const float inv = 1.0f / l;
+            uint16_t* orow = a.o + ((size_t)row0 + (size_t)qt * kBM + r) * kHD;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint32_t ov[32];
+                tmem_ld32(tO + lrow + 32 * q, ov);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i += 8) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        w[e] = (uint32_t)f32_to_bf16_bits(__uint_as_float(ov[i + 2 * e]) * inv) |
+                               ((uint32_t)f32_to_bf16_bits(__uint_as_float(ov[i + 2 * e + 1]) * inv) << 16);
+                    *reinterpret_cast<uint4*>(orow + 32 * q + i) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---- host ------------------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// [rows][128] bf16 viewed as 64-column x 128-row boxes, 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* ptr, int64_t rows) {
+    EncodeTiled enc = encode_fn();
+    if (!enc) return forge_fail(-1, "flash prefill: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {(cuuint64_t)kHD, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kHD * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0
+                             : forge_fail(-1, "flash prefill: tensor map encode failed (%d): ptr %p rows %lld map%%64 %d",
+                                          (int)r, ptr, (long long)rows, (int)((uintptr_t)m % 64));
+}
+
+int configure() {
+    static bool done[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return forge_fail(-1, "flash prefill: no device");
+    if (done[dev]) return 0;
+    cudaError_t e = cudaFuncSetAttribute(k_flash_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return forge_fail(-1, "flash prefill: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    done[dev] = true;
+    return 0;
+}
+}  // namespace
+
+extern "C" FORGE_API int forge_flash_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
+                                             int B, int H, int S, int hd, int causal, void* stream) {
+    if (!q || !k || !v || !o || B <= 0 || H <= 0 || S <= 0)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_flash_prefill: bad args");
+    if (hd != kHD) return forge_fail(FORGE_KERNEL_UNSUPPORTED, "forge_flash_prefill: head_dim %d (only 128)", hd);
+    if (S % kBM) return forge_fail(FORGE_KERNEL_UNSUPPORTED, "forge_flash_prefill: seq_len %d not a multiple of 128", S);
+    if ((int64_t)B * H * S > (1ll << 31) - 1 || H > 65535 || B > 65535)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_flash_prefill: shape too large");
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) & 15)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_flash_prefill: arrays must be 16-byte aligned");
+    if (configure()) return -1;
+    uint32_t* err = forge_ops_err_word();
+    if (!err) return forge_fail(-1, "forge_flash_prefill: no device");
+    const int64_t rows = (int64_t)B * H * S;
+    CUtensorMap mq, mk, mv;
+    if (make_map(&mq, q, rows) || make_map(&mk, k, rows) || make_map(&mv, v, rows)) return -1;
+    PrefillArgs a{o, B, H, S, causal ? 1 : 0, (float)(1.4426950408889634 / 11.313708498984761), err};
+    dim3 grid((unsigned)(S / kBM), (unsigned)H, (unsigned)B);
+    k_flash_prefill<<<grid, kThreads, kSmem, (cudaStream_t)stream>>>(mq, mk, mv, a);
+    return forge_check_launch("forge_flash_prefill");
+}
+
+// FLASH_PREFILL family: in = [Q, K, V (HexaFarrBf16, [B][H][S][hd]), causal],
+// out = [O]; shape M = B, N = H, K = hd, batch = S.
 int forge_prefill_dispatch(const ForgeShapeInfo* s, const ForgeArgs* in, const ForgeArgs* out) {
-    (void)s; (void)in; (void)out;
-    forge_fail(FORGE_KERNEL_UNSUPPORTED, "FLASH_PREFILL: not built");
-    return FORGE_KERNEL_UNSUPPORTED;
+    if (in->count < 3 || out->count < 1 || s->M <= 0 || s->N <= 0 || s->K <= 0 || s->batch <= 0)
+        return FORGE_INVALID_ARGS;
+    const int64_t n = s->M * s->N * s->batch * s->K;
+    HexaFarrBf16* F[4] = {(HexaFarrBf16*)(intptr_t)in->farr_ids[0], (HexaFarrBf16*)(intptr_t)in->farr_ids[1],
+                          (HexaFarrBf16*)(intptr_t)in->farr_ids[2], (HexaFarrBf16*)(intptr_t)out->farr_ids[0]};
+    for (int i = 0; i < 4; ++i)
+        if (!F[i] || F[i]->len < n) return FORGE_INVALID_ARGS;
+    for (int i = 0; i < 3; ++i)
+        if (hexa_farr_bf16_to_device(F[i])) return FORGE_INVALID_ARGS;
+    if (!F[3]->d_buf && cudaMalloc(&F[3]->d_buf, (size_t)F[3]->len * 2) != cudaSuccess) {
+        cudaGetLastError();
+        F[3]->d_buf = nullptr;
+        return FORGE_INVALID_ARGS;
+    }
+    F[3]->loc = FARR_BF16_LOC_DEVICE;
+    const int causal = in->count > 3 ? (int)in->farr_ids[3] : 1;
+    const int rc = forge_flash_prefill((const uint16_t*)F[0]->d_buf, (const uint16_t*)F[1]->d_buf,
+                                       (const uint16_t*)F[2]->d_buf, (uint16_t*)F[3]->d_buf, (int)s->M, (int)s->N,
+                                       (int)s->batch, (int)s->K, causal, nullptr);
+    return rc == 0 ? FORGE_OK : (rc == FORGE_INVALID_ARGS ? FORGE_INVALID_ARGS : FORGE_KERNEL_UNSUPPORTED);
 }

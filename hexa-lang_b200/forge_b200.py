@@ -149,6 +149,7 @@ def lib() -> C.CDLL:
             "forge_q4_tile_bytes": (i64, [i64, i64]),
             "forge_q4_scale_tile_bytes": (i64, [i64, i64, i32]),
             "forge_ops_check": (i32, []),
+            "forge_flash_prefill": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
             "forge_api_version_v1": (C.c_uint32, []),
             "forge_tier_dispatch_v1": (i32, [i32, C.POINTER(ForgeShapeInfo), i32, i32, i32,
                                              C.POINTER(ForgeArgs), C.POINTER(ForgeArgs)]),

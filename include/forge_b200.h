@@ -204,6 +204,14 @@ int forge_flash_decode_noalloc(const float* q, const uint16_t* kc, const uint16_
                                int B, int H, int Hkv, int hd, int lmax, float* out, void* stream);
 int forge_flash_decode_noalloc_status(void);
 
+/* Causal (or full) flash-attention prefill on the tcgen05 tensor cores:
+ * q, k, v, o [B][H][S][hd] bf16 device arrays (16-byte aligned), hd = 128,
+ * S a multiple of 128; O = softmax(Q K^T / sqrt(hd) + mask) V with fp32
+ * accumulation. Asynchronous on `stream`; kernel errors (a wait that ran
+ * out) show in forge_ops_check(). */
+int forge_flash_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o, int B, int H, int S,
+                        int hd, int causal, void* stream);
+
 /* Weight preparation (device memory). */
 int forge_fill_normal_bf16(uint16_t* out, int64_t n, uint64_t seed, uint64_t offset, float std,
                            void* stream);

@@ -165,3 +165,11 @@ def test_compute_fails_loudly_without_gpu(forge):
     d = forge.ForgeModelDesc(n_layer=1, d_model=64, n_head=2, n_kv_head=2, head_dim=64, ffn=64, vocab=64,
                              rms_eps=1e-5, rope_theta=1e4, max_batch=1, max_ctx=16, tp_size=1)
     assert L.forge_b200_create(C.byref(d), 0, C.byref(h)) != 0
+
+
+def test_python_binding_types_every_header_function(forge):
+    """Every C entry has explicit ctypes argument types in the binding (an
+    untyped call would pass 64-bit pointers as 32-bit ints)."""
+    L = forge.lib()
+    untyped = [n for n in sorted(header_functions()) if getattr(L, n).argtypes is None]
+    assert not untyped, untyped

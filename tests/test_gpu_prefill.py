@@ -1,0 +1,75 @@
+"""Flash-attention prefill on the tcgen05 tensor cores against a PyTorch
+fp32 reference of the same op: O = softmax(Q K^T / sqrt(128) + causal mask) V
+(nn_attn_core_fwd, stdlib/flame/nn_lib.hexa:221-278), bf16 inputs ~ N(0, 1).
+
+Tolerance: the kernel rounds P to bf16 before P V and O to bf16 on output,
+so against the fp32 reference the bar is max |err| <= 2e-2 and mean |err| <=
+2e-3. The first case is a single CTA, so a broken kernel fails in one short
+launch before the larger grids run."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(torch, q, k, v, causal):
+    qf, kf, vf = q.float(), k.float(), v.float()
+    s = qf @ kf.transpose(-1, -2) / np.sqrt(q.shape[-1])
+    if causal:
+        S = q.shape[-2]
+        mask = torch.triu(torch.ones(S, S, dtype=torch.bool, device=q.device), 1)
+        s = s.masked_fill(mask, float("-inf"))
+    return torch.softmax(s, -1) @ vf
+
+
+@pytest.mark.parametrize("B,H,S,causal", [
+    (1, 1, 128, True),
+    (1, 1, 128, False),
+    (1, 2, 256, True),
+    (1, 2, 512, False),
+    (2, 3, 1024, True),
+])
+def test_flash_prefill(forge, cuda, B, H, S, causal):
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(B * 100 + H * 10 + S + causal)
+    q, k, v = (torch.randn(B, H, S, 128, generator=g, device=cuda).to(torch.bfloat16) for _ in range(3))
+    o = torch.full_like(q, float("nan"))
+    torch.cuda.synchronize()
+    forge.check(forge.lib().forge_flash_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S, 128,
+                                                int(causal), torch.cuda.current_stream().cuda_stream), "prefill")
+    torch.cuda.synchronize()
+    forge.check(forge.lib().forge_ops_check(), "prefill error word")
+    ref = _ref(torch, q, k, v, causal)
+    err = (o.float() - ref).abs()
+    assert torch.isfinite(o.float()).all()
+    assert err.max().item() <= 2e-2, err.max().item()
+    assert err.mean().item() <= 2e-3, err.mean().item()
+
+
+def test_flash_prefill_dispatch_family(forge, cuda):
+    """FLASH_PREFILL through forge_tier_dispatch_v2 on HexaFarrBf16 slots."""
+    import ctypes as C
+    import torch
+    F = forge
+    L = F.lib()
+    B, H, S = 1, 2, 256
+    g = torch.Generator().manual_seed(5)
+    arrs = [torch.randn(B, H, S, 128, generator=g).to(torch.bfloat16) for _ in range(3)]
+    descs = []
+    for a in arrs:
+        d = L.hexa_farr_bf16_alloc(a.numel())
+        C.memmove(d.contents.h_buf, a.view(torch.int16).numpy().ctypes.data, a.numel() * 2)
+        descs.append(d)
+    out = L.hexa_farr_bf16_alloc(B * H * S * 128)
+    shape = F.ForgeShapeInfo(B, H, 128, S)
+    ins, outs = F.forge_args(*descs, 1), F.forge_args(out)
+    rc = L.forge_tier_dispatch_v2(F.FORGE_KERNEL_FLASH_PREFILL, C.byref(shape), 0, F.FORGE_PREC_PURE_BF16, 0,
+                                  C.byref(ins), C.byref(outs))
+    assert rc == F.FORGE_OK
+    F.check(L.hexa_farr_bf16_to_host(out), "to_host")
+    got = np.ctypeslib.as_array(C.cast(out.contents.h_buf, C.POINTER(C.c_uint16)), shape=(B * H * S * 128,))
+    o = torch.from_numpy(got.astype(np.int32) << 16).view(torch.float32).reshape(B, H, S, 128)
+    ref = _ref(torch, *[a.to(cuda) for a in arrs], True).cpu()
+    assert (o - ref).abs().max().item() <= 2e-2
+    for d in descs + [out]:
+        L.hexa_farr_bf16_free(d)
