@@ -59,6 +59,7 @@ struct ForgeGemvArgs {
     // LOGITS epilogue
     unsigned long long* argmax_key;  // [Btot]
     int32_t nvalid;        // rows >= nvalid (zero padding) never win the argmax
+    int32_t row_off;       // global index of row 0 in the argmax key (vocabulary shard)
     uint32_t* err;         // device error word
 };
 
@@ -128,6 +129,17 @@ struct ForgeArgs;
 // Row widths of a handle's activations: 0 model dim, 1 query width H*hd,
 // 2 vocabulary; 0 for a null handle.
 extern "C" int64_t forge_b200_width(const ForgeB200* h, int which);
+// Synthetic weights: block [nr][nc] of a matrix with `stride` columns.
+int forge_fill_normal_bf16_2d(uint16_t* out, int64_t nr, int64_t nc, uint64_t seed, uint64_t offset, int64_t stride,
+                              float std, cudaStream_t stream);
+
+// Tensor parallel (tp.cu): NCCL opened at run time.
+int forge_tp_comm_init(void** comm, const void* unique_id, int rank, int size);
+void forge_tp_comm_destroy(void* comm);
+int forge_tp_allreduce_sum_f32(void* comm, float* buf, size_t count, cudaStream_t stream);
+int forge_tp_allreduce_max_u64(void* comm, unsigned long long* buf, size_t count, cudaStream_t stream);
+int forge_tp_allgather_f32(void* comm, const float* send, float* recv, size_t count, cudaStream_t stream);
+
 // Per-device error word of the per-op entries (created on first use).
 uint32_t* forge_ops_err_word();
 // v2 FLASH_PREFILL family.

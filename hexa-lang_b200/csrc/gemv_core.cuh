@@ -112,8 +112,14 @@ __device__ __forceinline__ void epilogue(const ForgeGemvArgs& a, int u, int p, i
     } else if (EPI == FORGE_EPI_LOGITS) {
         a.y[(size_t)b * a.y_stride + row0 + p] = ylo;
         a.y[(size_t)b * a.y_stride + row0 + p + 8] = yhi;
-        if (row0 + p < a.nvalid) { unsigned long long k = argmax_key(ylo, row0 + p); best = k > best ? k : best; }
-        if (row0 + p + 8 < a.nvalid) { unsigned long long k = argmax_key(yhi, row0 + p + 8); best = k > best ? k : best; }
+        if (row0 + p < a.nvalid) {
+            const unsigned long long k = argmax_key(ylo, a.row_off + row0 + p);
+            best = k > best ? k : best;
+        }
+        if (row0 + p + 8 < a.nvalid) {
+            const unsigned long long k = argmax_key(yhi, a.row_off + row0 + p + 8);
+            best = k > best ? k : best;
+        }
     } else if (EPI == FORGE_EPI_SWIGLU) {
         // physical tile u = gate rows 8u..8u+7 (rows 0-7), up rows 8u..8u+7 (rows 8-15)
         const float gte = ylo, upv = yhi;

@@ -125,6 +125,13 @@ struct ForgeB200 {
     int trace_n = 0;
     std::vector<void*> allocs;
     bool weights_ready = false;
+    // tensor parallel shard (tp_size 1: the whole model). H, Hkv, F, V and
+    // Vpad above are this rank's; the *full fields are the model's.
+    int tp_rank = 0, tp_size = 1;
+    int Hfull = 0, Hkvfull = 0, Ffull = 0, Vfull = 0;
+    int h0 = 0, kv0 = 0, f0 = 0, v0 = 0;  // first head / kv head / FFN row / vocabulary row of this rank
+    void* comm = nullptr;                 // NCCL communicator
+    float* logits_all = nullptr;          // [tp][Bmax][Vpad] all-gathered logits
 
     void* alloc(size_t bytes) {
         void* p = nullptr;
@@ -188,26 +195,50 @@ int fill_rows(ForgeB200* h, uint16_t* dst, int64_t rows, int64_t K, const Src& s
     }
     return forge_fill_normal_bf16(dst, rows * K, s.seed, s.offset, s.std, h->stream);
 }
+// dst [nr][nc] = rows r0.., columns c0.. of the logical matrix with `cols`
+// columns (a tensor-parallel shard; the whole matrix when r0 = c0 = 0).
+int fill_block(ForgeB200* h, uint16_t* dst, int64_t cols, int64_t r0, int64_t nr, int64_t c0, int64_t nc,
+               const Src& s) {
+    if (c0 == 0 && nc == cols) {
+        Src t = s;
+        if (t.host) t.host += r0 * cols;
+        else t.offset += (uint64_t)(r0 * cols);
+        return fill_rows(h, dst, nr, nc, t);
+    }
+    if (s.host) {
+        cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)nc * 2, s.host + r0 * cols + c0, (size_t)cols * 2,
+                                          (size_t)nc * 2, (size_t)nr, cudaMemcpyHostToDevice, h->stream);
+        return e == cudaSuccess ? 0 : forge_fail(-1, "forge_b200: H2D weights: %s", cudaGetErrorString(e));
+    }
+    return forge_fill_normal_bf16_2d(dst, nr, nc, s.seed, s.offset + (uint64_t)(r0 * cols + c0), cols, s.std,
+                                     h->stream);
+}
 
 int load_layer_impl(ForgeB200* h, int l, const Src src[7], const float* g1, const float* g2, bool gains_one) {
     LayerDev& Ld = h->layers[l];
-    const int d = h->d, qd = h->qd, kvd = h->kvd, F = h->F;
+    const int d = h->d, qd = h->qd, kvd = h->kvd, F = h->F, hd = h->hd;
+    const int64_t qfull = (int64_t)h->Hfull * hd;
     int rc = 0;
-    // QKV: [Wq; Wk; Wv] logical rows -> RoPE-pair permutation -> pack
-    rc |= fill_rows(h, h->stA, qd, d, src[0]);
-    rc |= fill_rows(h, h->stA + (size_t)qd * d, kvd, d, src[1]);
-    rc |= fill_rows(h, h->stA + (size_t)(qd + kvd) * d, kvd, d, src[2]);
+    // QKV: this rank's heads of [Wq; Wk; Wv] -> RoPE-pair permutation -> pack
+    rc |= fill_block(h, h->stA, d, (int64_t)h->h0 * hd, qd, 0, d, src[0]);
+    rc |= fill_block(h, h->stA + (size_t)qd * d, d, (int64_t)h->kv0 * hd, kvd, 0, d, src[1]);
+    rc |= fill_block(h, h->stA + (size_t)(qd + kvd) * d, d, (int64_t)h->kv0 * hd, kvd, 0, d, src[2]);
     if (rc) return -1;
-    if (forge_permute_rows_bf16(h->stA, h->stB, h->nqkv, d, FORGE_PERM_QKV, h->hd, h->stream)) return -1;
+    if (forge_permute_rows_bf16(h->stA, h->stB, h->nqkv, d, FORGE_PERM_QKV, hd, h->stream)) return -1;
     if (pack_matrix(h, h->nqkv, d, Ld.qkv_w, Ld.qkv_s, h->q4)) return -1;
-    // O
-    if (fill_rows(h, h->stB, d, qd, src[3]) || pack_matrix(h, d, qd, Ld.o_w, Ld.o_s, h->q4)) return -1;
-    // gate/up interleave
-    if (fill_rows(h, h->stA, F, d, src[4]) || fill_rows(h, h->stA + (size_t)F * d, F, d, src[5])) return -1;
+    // O: the columns of this rank's heads (row-split along K)
+    if (fill_block(h, h->stB, qfull, 0, d, (int64_t)h->h0 * hd, qd, src[3]) ||
+        pack_matrix(h, d, qd, Ld.o_w, Ld.o_s, h->q4))
+        return -1;
+    // gate/up: this rank's FFN rows, interleaved
+    if (fill_block(h, h->stA, d, h->f0, F, 0, d, src[4]) ||
+        fill_block(h, h->stA + (size_t)F * d, d, h->f0, F, 0, d, src[5]))
+        return -1;
     if (forge_permute_rows_bf16(h->stA, h->stB, 2 * F, d, FORGE_PERM_GATEUP, F, h->stream)) return -1;
     if (pack_matrix(h, 2 * F, d, Ld.gu_w, Ld.gu_s, h->q4)) return -1;
-    // down
-    if (fill_rows(h, h->stB, d, F, src[6]) || pack_matrix(h, d, F, Ld.dn_w, Ld.dn_s, h->q4)) return -1;
+    // down: the columns of this rank's FFN rows
+    if (fill_block(h, h->stB, h->Ffull, 0, d, h->f0, F, src[6]) || pack_matrix(h, d, F, Ld.dn_w, Ld.dn_s, h->q4))
+        return -1;
     // gains
     if (gains_one) {
         if (forge_fill_f32(Ld.g1, d, 1.0f, h->stream) || forge_fill_f32(Ld.g2, d, 1.0f, h->stream)) return -1;
@@ -222,13 +253,16 @@ int load_layer_impl(ForgeB200* h, int l, const Src src[7], const float* g1, cons
 
 int load_embed_impl(ForgeB200* h, const Src& emb, const Src* head, const float* gF, bool gains_one) {
     const int64_t V = h->V, Vp = h->Vpad, d = h->d;
-    if (fill_rows(h, h->emb, V, d, emb)) return -1;
-    // head tiles from a zero-padded [Vpad][d] copy
+    if (fill_rows(h, h->emb, h->Vfull, d, emb)) return -1;  // replicated on every rank
+    // head tiles (this rank's vocabulary rows) from a zero-padded [Vpad][d] copy
     if (cudaMemsetAsync(h->stB, 0, (size_t)Vp * d * 2, h->stream) != cudaSuccess) return forge_fail(-1, "memset");
-    if (head) {
-        if (fill_rows(h, h->stB, V, d, *head)) return -1;
-    } else if (cudaMemcpyAsync(h->stB, h->emb, (size_t)V * d * 2, cudaMemcpyDeviceToDevice, h->stream) != cudaSuccess) {
-        return forge_fail(-1, "forge_b200: head copy failed");
+    if (V > 0) {
+        if (head) {
+            if (fill_block(h, h->stB, d, h->v0, V, 0, d, *head)) return -1;
+        } else if (cudaMemcpyAsync(h->stB, h->emb + (size_t)h->v0 * d, (size_t)V * d * 2, cudaMemcpyDeviceToDevice,
+                                   h->stream) != cudaSuccess) {
+            return forge_fail(-1, "forge_b200: head copy failed");
+        }
     }
     if (forge_bf16_pack_tiles(h->stB, Vp, d, h->head_w, h->stream)) return -1;
     if (gains_one) {
@@ -248,6 +282,14 @@ ForgeGemvArgs gemv_base(const ForgeB200* h, int B) {
     a.split = h->split_for(B);
     a.err = h->err;
     return a;
+}
+
+// Row-split projections under tensor parallelism: rank 0 adds its partial
+// product to the residual stream, the other ranks store theirs, and one
+// all-reduce (sum) leaves x + sum of all partials on every rank.
+int resid_epi(const ForgeB200* h) { return h->tp_rank == 0 ? FORGE_EPI_RESID : FORGE_EPI_STORE; }
+int tp_sum(ForgeB200* h, float* x, int B) {
+    return h->comm ? forge_tp_allreduce_sum_f32(h->comm, x, (size_t)B * h->d, h->stream) : 0;
 }
 
 // RMSNorm + QKV + RoPE, K/V appended at each sequence's position.
@@ -277,8 +319,9 @@ int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool p
     const LayerDev& Ld = h->layers[l];
     ForgeGemvArgs g = gemv_base(h, B);
     g.w = Ld.o_w; g.s = Ld.o_s; g.N = h->d; g.K = h->qd; g.x = ctx; g.x_stride = h->qd;
-    g.pro = FORGE_PRO_PLAIN; g.epi = FORGE_EPI_RESID; g.y = x; g.y_stride = h->d;
-    return forge_gemv_launch(g, h->stream, pdl);
+    g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
+    if (forge_gemv_launch(g, h->stream, pdl)) return -1;
+    return tp_sum(h, x, B);
 }
 
 // x += Wd (silu(Wg n) * (Wu n)), n = RMSNorm(x) * g2
@@ -291,8 +334,9 @@ int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl) {
     if (forge_gemv_launch(g, h->stream, pdl)) return -1;
     g = gemv_base(h, B);
     g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = h->s; g.x_stride = h->F;
-    g.pro = FORGE_PRO_PLAIN; g.epi = FORGE_EPI_RESID; g.y = x; g.y_stride = h->d;
-    return forge_gemv_launch(g, h->stream, pdl);
+    g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
+    if (forge_gemv_launch(g, h->stream, pdl)) return -1;
+    return tp_sum(h, x, B);
 }
 
 // final RMSNorm + LM head into the handle's logits, argmax keys updated
@@ -302,12 +346,14 @@ int enqueue_head(ForgeB200* h, int B, const float* x, bool pdl) {
     g.w = h->head_w; g.s = nullptr; g.N = h->Vpad; g.K = h->d; g.x = x; g.x_stride = h->d;
     g.pro = FORGE_PRO_RMSNORM; g.gain = h->gF; g.eps = h->desc.rms_eps;
     g.epi = FORGE_EPI_LOGITS; g.y = h->logits; g.y_stride = h->Vpad; g.argmax_key = h->amax; g.nvalid = h->V;
-    return forge_gemv_launch(g, h->stream, pdl);
+    g.row_off = h->v0;
+    if (forge_gemv_launch(g, h->stream, pdl)) return -1;
+    return h->comm ? forge_tp_allreduce_max_u64(h->comm, h->amax, (size_t)B, h->stream) : 0;
 }
 
 int enqueue_step(ForgeB200* h, int B) {
     cudaStream_t st = h->stream;
-    if (forge_embed_launch(h->emb, h->d, h->V, h->tok, B, h->x, h->err, st, false)) return -1;
+    if (forge_embed_launch(h->emb, h->d, h->Vfull, h->tok, B, h->x, h->err, st, false)) return -1;
     for (int l = 0; l < h->L; ++l) {
         if (enqueue_qkv(h, l, B, h->x, h->q, true) || enqueue_attn(h, l, B, h->q, h->ctx, true) ||
             enqueue_oproj(h, l, B, h->ctx, h->x, true) || enqueue_mlp(h, l, B, h->x, true))
@@ -340,7 +386,7 @@ int fused_splits(const ForgeB200* h, int B) {
 // Builds (once per batch size) the phase list of the fused step and checks
 // that it fits one CTA per SM. Returns the args or nullptr.
 const ForgeStepArgs* fused_for(ForgeB200* h, int B) {
-    if (h->force_graph) return nullptr;
+    if (h->force_graph || h->tp_size > 1) return nullptr;
     // one mma column block per GEMV: int4 (hi/lo int8) and exact bf16 use two
     // columns per sequence, plain bf16 one
     if ((h->q4 || h->split_for(B)) ? B > 4 : B > 8) return nullptr;
@@ -514,7 +560,8 @@ int forge_argmax_finalize_launch(unsigned long long* keys, int B, int32_t* tok_o
 }
 
 extern "C" {
-FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB200** out) {
+namespace {
+int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, ForgeB200** out) {
     if (!desc || !out) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: null argument");
     *out = nullptr;
     const ForgeModelDesc& m = *desc;
@@ -529,7 +576,16 @@ FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB20
         return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: int4 group-128 needs every K %% 128 == 0");
     if (m.weight_kind != FORGE_WEIGHT_BF16 && m.weight_kind != FORGE_WEIGHT_Q4_G128)
         return forge_fail(FORGE_PRECISION_UNSUPPORTED, "forge_b200_create: unknown weight kind %d", m.weight_kind);
-    if (m.tp_size > 1) return forge_fail(FORGE_REGIME_UNSUPPORTED, "forge_b200_create: tensor parallel handles use forge_b200_create_tp");
+    const int T = m.tp_size > 0 ? m.tp_size : 1, R = m.tp_size > 0 ? m.tp_rank : 0;
+    if (R < 0 || R >= T) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: tp_rank %d outside 0..%d", R, T - 1);
+    if (m.n_head % T || m.n_kv_head % T)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: %d / %d heads do not split over %d ranks", m.n_head,
+                          m.n_kv_head, T);
+    if ((int64_t)m.n_head / T * m.head_dim % 128 && m.weight_kind == FORGE_WEIGHT_Q4_G128)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: a rank's O-projection K must be a multiple of 128");
+    int64_t f_off = 0, f_len = m.ffn;
+    if (T > 1 && forge_tp_split(m.ffn, m.weight_kind == FORGE_WEIGHT_Q4_G128 ? 128 : 16, R, T, &f_off, &f_len))
+        return FORGE_INVALID_ARGS;
     if (m.max_batch > 1024) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create: max_batch <= 1024");
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
@@ -544,8 +600,18 @@ FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB20
     ForgeB200* h = new ForgeB200();
     h->desc = m;
     h->device = device;
-    h->L = m.n_layer; h->d = m.d_model; h->H = m.n_head; h->Hkv = m.n_kv_head; h->hd = m.head_dim;
-    h->F = m.ffn; h->V = m.vocab; h->Vpad = (int)round_up(m.vocab, 16);
+    h->L = m.n_layer; h->d = m.d_model; h->hd = m.head_dim;
+    h->tp_rank = R; h->tp_size = T;
+    h->Hfull = m.n_head; h->Hkvfull = m.n_kv_head; h->Ffull = m.ffn; h->Vfull = m.vocab;
+    h->H = m.n_head / T; h->Hkv = m.n_kv_head / T; h->h0 = R * h->H; h->kv0 = R * h->Hkv;
+    h->F = (int)f_len; h->f0 = (int)f_off;
+    {
+        // equal vocabulary slices of whole 16-row tiles (all-gather needs equal counts)
+        const int vs = (int)round_up((m.vocab + T - 1) / T, 16);
+        h->Vpad = vs;
+        h->v0 = R * vs;
+        h->V = std::max(0, std::min(vs, m.vocab - h->v0));
+    }
     h->qd = h->H * h->hd; h->kvd = h->Hkv * h->hd; h->nqkv = h->qd + 2 * h->kvd;
     h->Bmax = m.max_batch; h->lmax = m.max_ctx; h->q4 = m.weight_kind == FORGE_WEIGHT_Q4_G128;
     if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -556,7 +622,8 @@ FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB20
     int rc = 0;
     for (auto& Ld : h->layers) rc |= alloc_layer(h, Ld);
     const size_t d = h->d;
-    h->emb = (uint16_t*)h->alloc((size_t)h->V * d * 2);
+    h->emb = (uint16_t*)h->alloc((size_t)h->Vfull * d * 2);
+    if (T > 1) h->logits_all = (float*)h->alloc(sizeof(float) * (size_t)T * h->Bmax * h->Vpad);
     h->head_w = h->alloc((size_t)h->Vpad * d * 2);
     h->gF = (float*)h->alloc(sizeof(float) * d);
     h->kv_layer = (size_t)h->Bmax * h->Hkv * h->lmax * h->hd;
@@ -644,8 +711,26 @@ FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB20
         forge_b200_destroy(h);
         return forge_fail(-1, "forge_b200_create: device initialisation failed");
     }
+    if (T > 1 && (!h->logits_all || forge_tp_comm_init(&h->comm, nccl_id, R, T))) {
+        forge_b200_destroy(h);
+        return -1;
+    }
     *out = h;
     return 0;
+}
+}  // namespace
+
+FORGE_API int forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB200** out) {
+    if (desc && desc->tp_size > 1)
+        return forge_fail(FORGE_REGIME_UNSUPPORTED, "forge_b200_create: tensor parallel handles use forge_b200_create_tp");
+    return create_impl(desc, device, nullptr, out);
+}
+
+FORGE_API int forge_b200_create_tp(const ForgeModelDesc* desc, int device, const void* nccl_unique_id,
+                                   ForgeB200** out) {
+    if (!desc || !nccl_unique_id || desc->tp_size < 1)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create_tp: bad args");
+    return create_impl(desc, device, nccl_unique_id, out);
 }
 
 FORGE_API void forge_b200_destroy(ForgeB200* h) {
@@ -653,6 +738,8 @@ FORGE_API void forge_b200_destroy(ForgeB200* h) {
     cudaSetDevice(h->device);
     if (h->stream) cudaStreamSynchronize(h->stream);
     for (auto& kv : h->graphs) cudaGraphExecDestroy(kv.second);
+    h->graphs.clear();
+    if (h->comm) forge_tp_comm_destroy(h->comm);  // after the graphs that hold its collectives
     for (void* p : h->allocs) cudaFree(p);
     if (h->h_tok) cudaFreeHost(h->h_tok);
     if (h->stream) cudaStreamDestroy(h->stream);
@@ -776,9 +863,20 @@ FORGE_API int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tok
     cudaMemcpyAsync(h->tok, stage, 4 * batch, cudaMemcpyHostToDevice, h->stream);
     if (enqueue_one(h, batch)) return -1;
     if (next_tokens) cudaMemcpyAsync(stage, h->tok, 4 * batch, cudaMemcpyDeviceToHost, h->stream);
-    if (logits)
+    if (logits && !h->comm) {
         cudaMemcpy2DAsync(logits, sizeof(float) * h->V, h->logits, sizeof(float) * h->Vpad, sizeof(float) * h->V,
                           batch, cudaMemcpyDeviceToHost, h->stream);
+    } else if (logits) {
+        // every rank holds one vocabulary slice: gather them (all ranks call this)
+        const size_t per = (size_t)batch * h->Vpad;
+        if (forge_tp_allgather_f32(h->comm, h->logits, h->logits_all, per, h->stream)) return -1;
+        for (int r = 0; r < h->tp_size; ++r) {
+            const int nv = std::max(0, std::min(h->Vpad, h->Vfull - r * h->Vpad));
+            if (nv)
+                cudaMemcpy2DAsync(logits + (size_t)r * h->Vpad, sizeof(float) * h->Vfull, h->logits_all + r * per,
+                                  sizeof(float) * h->Vpad, sizeof(float) * nv, batch, cudaMemcpyDeviceToHost, h->stream);
+        }
+    }
     if (cudaStreamSynchronize(h->stream) != cudaSuccess)
         return forge_fail(-1, "forge_b200_decode_step: %s", cudaGetErrorString(cudaGetLastError()));
     if (next_tokens) memcpy(next_tokens, stage, 4 * batch);
@@ -869,7 +967,7 @@ FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
 }
 int64_t forge_b200_width(const ForgeB200* h, int which) {
     if (!h) return 0;
-    return which == 0 ? h->d : which == 1 ? h->qd : h->V;
+    return which == 0 ? h->d : which == 1 ? h->qd : h->V;  // under tensor parallelism: this rank's slice
 }
 
 // ---- block-level entries (the v2 fused families) ------------------------------
@@ -929,7 +1027,7 @@ FORGE_API int forge_b200_lm_head(ForgeB200* h, int batch, const float* x, int32_
 FORGE_API int forge_b200_embed(ForgeB200* h, int batch, const int32_t* tok, float* x) {
     if (int rc = check_ready(h, batch)) return rc;
     if (!tok || !x) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_embed: null array");
-    return forge_embed_launch(h->emb, h->d, h->V, tok, batch, x, h->err, h->stream, false);
+    return forge_embed_launch(h->emb, h->d, h->Vfull, tok, batch, x, h->err, h->stream, false);
 }
 
 FORGE_API int forge_b200_advance(ForgeB200* h, int batch) {

@@ -101,6 +101,20 @@ __global__ void k_fill_normal_bf16(uint16_t* out, int64_t n, uint64_t seed, uint
     }
 }
 
+// Block [nr][nc] of a row-major matrix with `stride` columns whose element
+// (r, c) is stream position offset + r * stride + c: the same values the 1-D
+// fill gives the whole matrix, so a tensor-parallel shard of a synthetic
+// weight equals the slice of the single-GPU weight.
+__global__ void k_fill_normal_bf16_2d(uint16_t* out, int64_t nr, int64_t nc, uint64_t seed, uint64_t offset,
+                                      int64_t stride, double sd) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nr * nc;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / nc, c = i - r * nc;
+        float v = __double2float_rn(__dmul_rn(sd, normal_at(seed, offset + (uint64_t)(r * stride + c))));
+        out[i] = f32_to_bf16_bits(v);
+    }
+}
+
 __global__ void k_fill_f32(float* out, int64_t n, float v) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x)
@@ -253,6 +267,17 @@ FORGE_API int forge_fill_normal_bf16(uint16_t* out, int64_t n, uint64_t seed, ui
     k_fill_normal_bf16<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(out, n, seed, offset, (double)std);
     return forge_check_launch("forge_fill_normal_bf16");
 }
+}  // extern "C"
+
+int forge_fill_normal_bf16_2d(uint16_t* out, int64_t nr, int64_t nc, uint64_t seed, uint64_t offset, int64_t stride,
+                              float std, cudaStream_t stream) {
+    if (!out || nr < 0 || nc < 0 || stride < nc) return forge_fail(-1, "forge_fill_normal_bf16_2d: bad args");
+    if (nr * nc == 0) return 0;
+    k_fill_normal_bf16_2d<<<grid_for(nr * nc, 256), 256, 0, stream>>>(out, nr, nc, seed, offset, stride, (double)std);
+    return forge_check_launch("forge_fill_normal_bf16_2d");
+}
+
+extern "C" {
 FORGE_API int forge_fill_f32(float* out, int64_t n, float v, void* stream) {
     if (!out || n < 0) return forge_fail(-1, "forge_fill_f32: bad args");
     if (n == 0) return 0;

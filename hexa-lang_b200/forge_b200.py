@@ -115,6 +115,9 @@ def lib() -> C.CDLL:
         sig = {
             "forge_b200_create": (i32, [C.POINTER(ForgeModelDesc), i32, C.POINTER(vp)]),
             "forge_b200_destroy": (None, [vp]),
+            "forge_b200_create_tp": (i32, [C.POINTER(ForgeModelDesc), i32, vp, C.POINTER(vp)]),
+            "forge_b200_tp_unique_id": (i32, [vp]),
+            "forge_tp_split": (i32, [i64, i64, i32, i32, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
             "forge_b200_last_error": (C.c_char_p, []),
             "forge_b200_stream": (vp, [vp]),
             "forge_b200_load_layer": (i32, [vp, i32, C.POINTER(ForgeLayerWeights)]),
@@ -222,12 +225,16 @@ class ForgeModel:
 
     def __init__(self, n_layer, d_model, n_head, n_kv_head, head_dim, ffn, vocab, *,
                  weight_kind=FORGE_WEIGHT_BF16, tied_head=False, max_batch=1, max_ctx=256,
-                 rms_eps=1e-5, rope_theta=10000.0, act_mode=0, device=0):
+                 rms_eps=1e-5, rope_theta=10000.0, act_mode=0, device=0, tp_rank=0, tp_size=1, nccl_id=None):
         self.desc = ForgeModelDesc(n_layer, d_model, n_head, n_kv_head, head_dim, ffn, vocab,
                                    rms_eps, rope_theta, weight_kind, int(tied_head), max_batch,
-                                   max_ctx, 0, 1, act_mode)
+                                   max_ctx, tp_rank, tp_size, act_mode)
         h = C.c_void_p()
-        check(lib().forge_b200_create(C.byref(self.desc), device, C.byref(h)), "forge_b200_create")
+        if tp_size > 1:
+            idb = C.create_string_buffer(bytes(nccl_id), 128)
+            check(lib().forge_b200_create_tp(C.byref(self.desc), device, idb, C.byref(h)), "forge_b200_create_tp")
+        else:
+            check(lib().forge_b200_create(C.byref(self.desc), device, C.byref(h)), "forge_b200_create")
         self.h = h
         self.vocab = vocab
 
@@ -335,6 +342,19 @@ class ForgeModel:
     @property
     def stream(self):
         return lib().forge_b200_stream(self.h)
+
+
+def tp_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id for forge_b200_create_tp."""
+    buf = C.create_string_buffer(128)
+    check(lib().forge_b200_tp_unique_id(buf), "forge_b200_tp_unique_id")
+    return buf.raw
+
+
+def tp_split(n, gran, rank, size):
+    off, ln = C.c_int64(), C.c_int64()
+    check(lib().forge_tp_split(n, gran, rank, size, C.byref(off), C.byref(ln)), "forge_tp_split")
+    return off.value, ln.value
 
 
 # ---- per-op helpers on torch CUDA tensors -----------------------------------

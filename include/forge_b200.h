@@ -102,6 +102,24 @@ typedef struct ForgeLayerWeights {
 typedef struct ForgeB200 ForgeB200;
 
 int         forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB200** out);
+/* Tensor-parallel handle: rank desc->tp_rank of desc->tp_size, one process
+ * (or thread) per GPU. Every rank passes the same 128-byte NCCL unique id
+ * (made once by forge_b200_tp_unique_id and shared out of band) and calls
+ * this at the same time (it blocks until all ranks joined). Heads are split
+ * evenly (n_head and n_kv_head divisible by tp_size), the FFN in whole
+ * 128-row groups (int4) or 16-row tiles (bf16) with the first ranks taking one
+ * more when they do not divide, the vocabulary in equal 16-row slices. Each
+ * decode step then runs one NCCL fp32 all-reduce after the O and after the
+ * down projection and one max all-reduce of the argmax keys; tokens, positions
+ * and the residual stream are identical on every rank. Entries that return
+ * logits gather them from all ranks: call them on all ranks alike. NCCL is
+ * opened at run time (libnccl.so.2, or the path in FORGE_NCCL_LIB). */
+int         forge_b200_create_tp(const ForgeModelDesc* desc, int device, const void* nccl_unique_id,
+                                 ForgeB200** out);
+int         forge_b200_tp_unique_id(void* out128);
+/* Shard of n items in units of gran for rank of size (the split the TP
+ * handle uses for the FFN): first rank offset and length. */
+int         forge_tp_split(int64_t n, int64_t gran, int rank, int size, int64_t* off, int64_t* len);
 void        forge_b200_destroy(ForgeB200* h);
 const char* forge_b200_last_error(void);
 void*       forge_b200_stream(ForgeB200* h);
