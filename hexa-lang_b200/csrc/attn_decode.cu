@@ -313,10 +313,12 @@ int forge_attn_configure() {
 }
 
 int forge_attn_pick_splits(int B, int Hkv, int lmax) {
-    // ~12 CTAs per SM of a 148-SM B200 (3 resident x ~4 waves); fixed so
-    // workspace sizes do not depend on which device is current.
-    const int target = 12 * 148;
-    int ns = (target + B * Hkv - 1) / (B * Hkv);
+    // As many splits as still fit one wave of resident CTAs (3 per SM of a
+    // 148-SM B200 at ~65 KB of shared memory each): a second wave would wait
+    // for the first and double the latency of the short decode attention.
+    // Fixed so workspace sizes do not depend on which device is current.
+    const int resident = 3 * 148;
+    int ns = resident / (B * Hkv);
     const int cap = (lmax + 127) / 128;  // at least ~128 keys per split at full context
     if (ns > cap) ns = cap;
     if (ns < 1) ns = 1;

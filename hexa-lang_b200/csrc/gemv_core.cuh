@@ -183,49 +183,56 @@ __device__ __forceinline__ int xq_index(int k, int col, int ncols) {
 // maximum. Columns 2b / 2b+1 hold hi / lo. Per group it records s (sxf[g][b])
 // and the column sums of hi and lo (ssum[g][2b], ssum[g][2b+1]) that remove
 // the +7 code bias of the weights after the integer dot product.
-template <int PRO, int NT, int MAXV = 12, int MAXG = 4>
+template <int PRO, int NT, int MAXP = 3>
 __device__ __noinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, float* sxf, int* ssum,
                                         float* red) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.K;
     const int ncols = 2 * a.batch;
-    // The global reads of a chunk of CH = NT*4*MAXV elements (and, for the
-    // RMSNorm prologue, the first NT*4*MAXG gains) are all issued before the
-    // first use, so a row up to CH long costs one memory round trip instead
-    // of one per 128-group pass. Longer rows are read in further chunks (and
-    // twice under RMSNorm: once for the norm, once to quantise).
-    constexpr int CH = NT * 4 * MAXV;
+    // Each thread owns 16 consecutive k (four float4), so 8 lanes cover one
+    // 128-group and the group reductions take 3 shuffle steps instead of 5;
+    // one pass covers PK = NT * 16 k. The reads of the first MAXP passes (and
+    // the first pass of RMSNorm gains) are all issued before the first use,
+    // so a row up to MAXP * PK long costs one memory round trip; later passes
+    // read in the pass.
+    constexpr int PK = NT * 16;
+    const int passes = (K + PK - 1) / PK;
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int kt = tid * 16;  // this thread's first k within a pass
     for (int b = 0; b < a.batch; ++b) {
         const float* xb = a.x + (size_t)b * a.x_stride;
-        float4 xv[MAXV];
-        float4 gv[MAXG];
+        float4 xv[MAXP][4];
+        float4 gv[4];
 #pragma unroll
-        for (int i = 0; i < MAXV; ++i) {
-            const int k = tid * 4 + i * NT * 4;
-            xv[i] = k < K ? load_x4<PRO>(a, b, xb, k) : z4;
-        }
+        for (int p = 0; p < MAXP; ++p)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int k = p * PK + kt + 4 * c;
+                xv[p][c] = k < K ? load_x4<PRO>(a, b, xb, k) : z4;
+            }
         if (PRO != FORGE_PRO_PLAIN) {
 #pragma unroll
-            for (int i = 0; i < MAXG; ++i) {
-                const int k = tid * 4 + i * NT * 4;
-                gv[i] = k < K ? __ldg(reinterpret_cast<const float4*>(a.gain + k)) : z4;
+            for (int c = 0; c < 4; ++c) {
+                const int k = kt + 4 * c;
+                gv[c] = k < K ? __ldg(reinterpret_cast<const float4*>(a.gain + k)) : z4;
             }
         }
         float inv = 1.0f;
         if (PRO != FORGE_PRO_PLAIN) {
             float ss = 0.0f;
 #pragma unroll
-            for (int i = 0; i < MAXV; ++i)
-                ss += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
-            for (int c = CH; c < K; c += CH) {
+            for (int p = 0; p < MAXP; ++p)
 #pragma unroll
-                for (int i = 0; i < MAXV; ++i) {
-                    const int k = c + tid * 4 + i * NT * 4;
+                for (int c = 0; c < 4; ++c)
+                    ss += xv[p][c].x * xv[p][c].x + xv[p][c].y * xv[p][c].y + xv[p][c].z * xv[p][c].z +
+                          xv[p][c].w * xv[p][c].w;
+            for (int p = MAXP; p < passes; ++p)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int k = p * PK + kt + 4 * c;
                     const float4 v = k < K ? load_x4<PRO>(a, b, xb, k) : z4;
                     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
                 }
-            }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
             // two halves of red alternate between sequences, so one barrier
@@ -238,60 +245,77 @@ __device__ __noinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, flo
             for (int w = 0; w < NT / 32; ++w) tot += rb[w];
             inv = 1.0f / sqrtf(tot / (float)K + a.eps);
         }
-        for (int c = 0; c < K; c += CH) {
-            if (c > 0) {
+        auto quantise = [&](int p, const float4 (&v)[4]) {
+            const int k0 = p * PK + kt;
+            // lanes past K hold zeros and take part in the shuffles; only
+            // whole 8-lane groups are ever past K (K % 128 == 0)
+            float e[16];
 #pragma unroll
-                for (int i = 0; i < MAXV; ++i) {
-                    const int k = c + tid * 4 + i * NT * 4;
-                    xv[i] = k < K ? load_x4<PRO>(a, b, xb, k) : z4;
+            for (int c = 0; c < 4; ++c) {
+                e[4 * c] = v[c].x; e[4 * c + 1] = v[c].y; e[4 * c + 2] = v[c].z; e[4 * c + 3] = v[c].w;
+            }
+            if (PRO != FORGE_PRO_PLAIN) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const float4 g4 = p == 0 ? gv[c]
+                                             : (k0 + 4 * c < K ? __ldg(reinterpret_cast<const float4*>(a.gain + k0 + 4 * c))
+                                                               : z4);
+                    e[4 * c] = g4.x * (e[4 * c] * inv); e[4 * c + 1] = g4.y * (e[4 * c + 1] * inv);
+                    e[4 * c + 2] = g4.z * (e[4 * c + 2] * inv); e[4 * c + 3] = g4.w * (e[4 * c + 3] * inv);
                 }
             }
-            // a warp covers one 128-group per pass (NT * 4 is a multiple of 128)
+            float amax = 0.f;
 #pragma unroll
-            for (int i = 0; i < MAXV; ++i) {
-                const int k = c + tid * 4 + i * NT * 4;
-                if (k < K) {  // whole warps take the same branch (K % 128 == 0)
-                    float e[4] = {xv[i].x, xv[i].y, xv[i].z, xv[i].w};
-                    if (PRO != FORGE_PRO_PLAIN) {
-                        const float4 g4 = (c == 0 && i < MAXG) ? gv[i < MAXG ? i : 0]
-                                                                : __ldg(reinterpret_cast<const float4*>(a.gain + k));
-                        e[0] = g4.x * (e[0] * inv); e[1] = g4.y * (e[1] * inv);
-                        e[2] = g4.z * (e[2] * inv); e[3] = g4.w * (e[3] * inv);
-                    }
-                    float amax = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
+            for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(e[j]));
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-                    const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
-                    const float is = amax > 0.f ? 127.0f / amax : 0.0f;
-                    uint32_t hw = 0, lw = 0;
-                    int shi = 0, slo = 0;
+            for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
+            const float is = amax > 0.f ? 127.0f / amax : 0.0f;
+            int shi = 0, slo = 0;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float hq = fminf(fmaxf(rintf(e[j] * is), -127.f), 127.f);
-                        const float lq = fminf(fmaxf(rintf((e[j] - sc * hq) * (256.0f * is)), -127.f), 127.f);
-                        const int hi = (int)hq, lo = (int)lq;
-                        shi += hi;
-                        slo += lo;
-                        hw |= (uint32_t)(hi & 0xFF) << (8 * j);
-                        lw |= (uint32_t)(lo & 0xFF) << (8 * j);
-                    }
-                    *reinterpret_cast<uint32_t*>(xq + xq_index(k, 2 * b, ncols)) = hw;
-                    *reinterpret_cast<uint32_t*>(xq + xq_index(k, 2 * b + 1, ncols)) = lw;
-                    // both column sums in one reduction: hi * 2^16 + lo
-                    // (|sum| <= 128 * 127 < 2^15 for each)
-                    int packed = shi * 65536 + slo;
+            for (int c = 0; c < 4; ++c) {
+                uint32_t hw = 0, lw = 0;
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) packed += __shfl_xor_sync(0xffffffffu, packed, o);
-                    if (lane == 0) {
-                        const int lo_sum = (int)(short)(packed & 0xFFFF);
-                        const int hi_sum = (packed - lo_sum) / 65536;
-                        const int g = k >> 7;
-                        sxf[g * 4 + b] = sc;
-                        ssum[g * 8 + 2 * b] = hi_sum;
-                        ssum[g * 8 + 2 * b + 1] = lo_sum;
-                    }
+                for (int j = 0; j < 4; ++j) {
+                    const float x = e[4 * c + j];
+                    const float hq = fminf(fmaxf(rintf(x * is), -127.f), 127.f);
+                    const float lq = fminf(fmaxf(rintf((x - sc * hq) * (256.0f * is)), -127.f), 127.f);
+                    const int hi = (int)hq, lo = (int)lq;
+                    shi += hi;
+                    slo += lo;
+                    hw |= (uint32_t)(hi & 0xFF) << (8 * j);
+                    lw |= (uint32_t)(lo & 0xFF) << (8 * j);
+                }
+                if (k0 < K) {
+                    *reinterpret_cast<uint32_t*>(xq + xq_index(k0 + 4 * c, 2 * b, ncols)) = hw;
+                    *reinterpret_cast<uint32_t*>(xq + xq_index(k0 + 4 * c, 2 * b + 1, ncols)) = lw;
                 }
             }
+            // both column sums in one reduction: hi * 2^16 + lo
+            // (|sum| <= 128 * 127 < 2^15 for each)
+            int packed = shi * 65536 + slo;
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) packed += __shfl_xor_sync(0xffffffffu, packed, o);
+            if ((lane & 7) == 0 && k0 < K) {
+                const int lo_sum = (int)(short)(packed & 0xFFFF);
+                const int hi_sum = (packed - lo_sum) / 65536;
+                const int g = k0 >> 7;
+                sxf[g * 4 + b] = sc;
+                ssum[g * 8 + 2 * b] = hi_sum;
+                ssum[g * 8 + 2 * b + 1] = lo_sum;
+            }
+        };
+#pragma unroll
+        for (int p = 0; p < MAXP; ++p)
+            if (p * PK < K) quantise(p, xv[p]);
+        for (int p = MAXP; p < passes; ++p) {
+            float4 v[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int k = p * PK + kt + 4 * c;
+                v[c] = k < K ? load_x4<PRO>(a, b, xb, k) : z4;
+            }
+            quantise(p, v);
         }
     }
 }
