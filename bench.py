@@ -31,8 +31,8 @@ MODEL = dict(n_layer=32, d=4096, n_head=32, n_kv=32, hd=128, ffn=11008, vocab=32
 CTX = 2048
 # dram__bytes_read.sum + dram__bytes_write.sum of one k_gemv launch (int4
 # gate/up 22016 x 4096, batch 1) from the ncu capture summarised in
-# profiles/; None until that capture exists.
-GEMV_TRAFFIC = None
+# profiles/k_gemv_int4_gateup_22016x4096_bs1.md (46.56 MB + 0.05 MB).
+GEMV_TRAFFIC = 46558720 + 51968
 
 
 def _tc_peak():
@@ -322,7 +322,7 @@ def main():
         print(json.dumps({"kernel": "k_gemv int4 22016x4096 bs1", "ms": ms, "bytes": nbytes}))
         return
     if args.only_prefill:
-        print(json.dumps(time_prefill(fb, torch, dev, B=2, H=8, S=4096, reps=2)))
+        print(json.dumps(time_prefill(fb, torch, dev, B=4, H=16, S=4096, reps=2)))
         return
     B, K, W = args.batch, args.steps, max(3, args.warmup)
     r = run_decode(fb, torch, pg, local, world, rank, B, K, W)
