@@ -8,20 +8,23 @@
 // (tool/r14_walls/flash_attn_bm32_bk32_v0.cu:75) is fp16 wmma at d = 64
 // and non-causal only; this is a new kernel for hd = 128 with the mask.
 //
-// One CTA owns 128 query rows of one (batch, head) and walks the key blocks
-// of 128 up to the diagonal:
-//   warp 4 (one lane)  TMA: the Q tile once, K/V tiles through a 2-stage ring
-//                      (128-byte swizzled boxes of 64 columns x 128 rows);
-//   warp 5 (one lane)  tensor-core issue: S = Q K^T into TMEM columns 0-127
-//                      (8 x K16 steps), then O += P V into columns 128-255;
-//   warps 0-3          softmax, one thread per query row: S row out of TMEM,
-//                      online max / sum in fp32 (exp2 with the scale folded
-//                      in), O rescaled in TMEM when the row max moved, P
-//                      written as bf16 into shared memory in the same
-//                      swizzled K-major layout TMA gives Q and K, then the
-//                      final O / l written to global memory.
+// One CTA owns two tiles of 128 query rows of one (batch, head) and walks the
+// key blocks of 128 up to the diagonal (k_flash_prefill_pp below):
+//   warp 8             TMA: Q of both tiles once, K through a 2-stage ring, V
+//                      through one buffer (128-byte swizzled 64 x 128 boxes);
+//   warp 9 (one lane)  tensor-core issue: S = Q K^T and O += P V per tile
+//                      (tcgen05.mma kind::f16, M 128, N 128, 8 x K16 steps),
+//                      alternating tiles so one tile's MMAs overlap the other
+//                      tile's softmax;
+//   warps 0-3 / 4-7    softmax of tile A / B, one thread per query row: S out
+//                      of TMEM (tcgen05.ld), online max / sum in fp32 with
+//                      exp2 (the scale folded in), O rescaled in TMEM only
+//                      when the row max grows by more than 2^8, P written as
+//                      bf16 into shared memory in the swizzled K-major layout
+//                      TMA gives Q and K, and finally O / l to global memory.
 // Every wait is bounded (error word, then the CTA drains its copies and
 // tensor-core work and frees its TMEM).
+#include <cstring>
 #include <mutex>
 #include "tcgen05.cuh"
 #include "forge_internal.h"
@@ -34,11 +37,6 @@ constexpr int kBM = 128;                  // query rows per CTA
 constexpr int kBN = 128;                  // keys per block
 constexpr int kTile = kBM * kHD * 2;      // 32 KB: one Q / K / V / P tile
 constexpr int kHalf = kTile / 2;          // 16 KB: 64 columns x 128 rows, swizzled
-constexpr int kThreads = 192;
-constexpr int kOffQ = 0, kOffK0 = kTile, kOffV0 = 2 * kTile, kOffK1 = 3 * kTile, kOffV1 = 4 * kTile,
-              kOffP = 5 * kTile, kOffBar = 6 * kTile;
-constexpr int kSmem = kOffBar + 256 + 1024;  // + barriers / TMEM slot + alignment slack
-constexpr uint32_t kTmemCols = 256;       // S: 0-127, O: 128-255
 constexpr uint32_t kIdescS = umma_idesc_bf16_f32(kBM, kBN, false);  // B = K rows, K-major
 constexpr uint32_t kIdescO = umma_idesc_bf16_f32(kBM, kHD, true);   // B = V rows, MN-major
 
@@ -49,6 +47,20 @@ struct PrefillArgs {
     uint32_t* err;
 };
 
+// 2^x with the hardware approximation (ex2.approx, relative error ~2^-22;
+// 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// Two floats to packed bf16x2 (round to nearest even), first in the low half.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
 // Byte offset of the 16-byte chunk c (columns 8c..8c+7) of row r inside a
 // 128x128 bf16 tile stored as two 128-byte-swizzled halves (the layout a
 // TMA box of 64 x 128 with 128-byte swizzle writes).
@@ -56,199 +68,272 @@ __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
     return (uint32_t)((c >> 3) * kHalf + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    k_flash_prefill(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                    const __grid_constant__ CUtensorMap tv, const PrefillArgs a) {
+// ---- two query tiles per CTA -------------------------------------------------------
+// Tiles A (rows 256p .. +127) and B (rows 256p+128 .. +255) share every K/V
+// block (loaded once) and alternate on the tensor core: while the softmax
+// warpgroup of one tile works on its S, the MMA warp runs the other tile's
+// S = QK^T or O += PV. TMEM holds S_A, O_A, S_B, O_B (512 columns); the softmax
+// reads each S row twice (max, then exp) so no thread holds a whole row.
+// Shared memory: Q_A Q_B | K ring of 2 | V (one buffer) | P_A P_B.
+constexpr int kPThreads = 320;            // warps 0-3 softmax A, 4-7 softmax B, 8 TMA, 9 MMA
+constexpr int kPOffQ = 0, kPOffK = 2 * kTile, kPOffV = 4 * kTile, kPOffP = 5 * kTile, kPOffBar = 7 * kTile;
+constexpr int kPSmem = kPOffBar + 256 + 1024;
+constexpr uint32_t kPTmemCols = 512;
+
+__global__ void __launch_bounds__(kPThreads, 1)
+    k_flash_prefill_pp(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                       const __grid_constant__ CUtensorMap tv, const PrefillArgs a) {
     extern __shared__ uint8_t smem_raw[];
-    // 1024-byte alignment for the swizzle atoms
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
     const uint32_t sbase = smem_u32(base);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kPOffBar);
     uint64_t* q_full = bars + 0;
-    uint64_t* kv_full = bars + 1;   // [2]
-    uint64_t* kv_empty = bars + 3;  // [2]
-    uint64_t* s_full = bars + 5;
-    uint64_t* p_full = bars + 6;
-    uint64_t* o_done = bars + 7;
-    uint64_t* drain = bars + 8;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 9);
+    uint64_t* k_full = bars + 1;    // [2]
+    uint64_t* k_empty = bars + 3;   // [2]
+    uint64_t* v_full = bars + 5;
+    uint64_t* v_empty = bars + 6;
+    uint64_t* s_full = bars + 7;    // [2] per tile
+    uint64_t* p_full = bars + 9;    // [2]
+    uint64_t* o_done = bars + 11;   // [2]
+    uint64_t* drain = bars + 13;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 14);
 
-    const int ntile = a.S / kBM;
-    const int qt = ntile - 1 - (int)blockIdx.x;  // longest causal rows first
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int nblk = a.causal ? qt + 1 : ntile;
-    const int row0 = (b * a.H + h) * a.S;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    // after an earlier CTA's wait ran out, the rest of the grid skips its
-    // work instead of timing out one by one
     __shared__ uint32_t s_abort;
     if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile uint32_t*>(a.err);
     __syncthreads();
     if (s_abort) return;
+
+    const int ntile = a.S / kBM;
+    const int npair = (ntile + 1) / 2;
+    const int qp = npair - 1 - (int)blockIdx.x;  // longest causal rows first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int tA = 2 * qp, tB = 2 * qp + 1;      // query tile indices
+    const bool hasB = tB < ntile;
+    // key blocks each tile needs (causal: up to its diagonal)
+    const int nA = a.causal ? tA + 1 : ntile;
+    const int nB = hasB ? (a.causal ? tB + 1 : ntile) : 0;
+    const int nblk = nA > nB ? nA : nB;
+    const int row0 = (b * a.H + h) * a.S;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        mbar_init(&kv_full[0], 1);
-        mbar_init(&kv_full[1], 1);
-        mbar_init(&kv_empty[0], 1);
-        mbar_init(&kv_empty[1], 1);
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 128);
-        mbar_init(o_done, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 128);
+            mbar_init(&o_done[i], 1);
+        }
+        mbar_init(v_full, 1);
+        mbar_init(v_empty, 1);
         mbar_init(drain, 1);
         fence_mbar_init();
     }
-    if (warp == 5) tmem_alloc(tslot, kTmemCols);
+    if (warp == 9) tmem_alloc(tslot, kPTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    const uint32_t tS = tmem, tO = tmem + 128;
+    // TMEM columns: S_A 0-127, O_A 128-255, S_B 256-383, O_B 384-511
+    const uint32_t tS[2] = {tmem, tmem + 256}, tO[2] = {tmem + 128, tmem + 384};
 
-    if (warp == 4) {
-        // ------------------------------------------------------------ TMA
+    if (warp == 8) {
+        // --------------------------------------------------------------- TMA
         if (lane == 0) {
+            // Q of both tiles, then the K ring
+            mbar_arrive_expect_tx(q_full, hasB ? 2 * kTile : kTile);
+            tma_load_2d(base + kPOffQ, &tq, 0, row0 + tA * kBM, q_full);
+            tma_load_2d(base + kPOffQ + kHalf, &tq, 64, row0 + tA * kBM, q_full);
+            if (hasB) {
+                tma_load_2d(base + kPOffQ + kTile, &tq, 0, row0 + tB * kBM, q_full);
+                tma_load_2d(base + kPOffQ + kTile + kHalf, &tq, 64, row0 + tB * kBM, q_full);
+            }
             int issued = 0;
-            mbar_arrive_expect_tx(q_full, kTile);
-            tma_load_2d(base + kOffQ, &tq, 0, row0 + qt * kBM, q_full);
-            tma_load_2d(base + kOffQ + kHalf, &tq, 64, row0 + qt * kBM, q_full);
             for (int j = 0; j < nblk; ++j) {
                 const int st = j & 1;
-                if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, a.err)) break;
-                uint8_t* kd = base + (st ? kOffK1 : kOffK0);
-                uint8_t* vd = base + (st ? kOffV1 : kOffV0);
-                mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
-                tma_load_2d(kd, &tk, 0, row0 + j * kBN, &kv_full[st]);
-                tma_load_2d(kd + kHalf, &tk, 64, row0 + j * kBN, &kv_full[st]);
-                tma_load_2d(vd, &tv, 0, row0 + j * kBN, &kv_full[st]);
-                tma_load_2d(vd + kHalf, &tv, 64, row0 + j * kBN, &kv_full[st]);
+                if (!mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1, a.err)) break;
+                uint8_t* kd = base + kPOffK + st * kTile;
+                mbar_arrive_expect_tx(&k_full[st], kTile);
+                tma_load_2d(kd, &tk, 0, row0 + j * kBN, &k_full[st]);
+                tma_load_2d(kd + kHalf, &tk, 64, row0 + j * kBN, &k_full[st]);
                 issued = j + 1;
             }
-            // every copy issued lands before the CTA exits
             mbar_wait(q_full, 0, a.err);
-            for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
-                mbar_wait(&kv_full[j & 1], (j >> 1) & 1, a.err);
+            for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.err);
+        } else if (lane == 1) {
+            // the single V buffer: block j once both tiles' PV of block j-1 are done
+            int issued = 0;
+            for (int j = 0; j < nblk; ++j) {
+                if (!mbar_wait(v_empty, (j & 1) ^ 1, a.err)) break;
+                mbar_arrive_expect_tx(v_full, kTile);
+                tma_load_2d(base + kPOffV, &tv, 0, row0 + j * kBN, v_full);
+                tma_load_2d(base + kPOffV + kHalf, &tv, 64, row0 + j * kBN, v_full);
+                issued = j + 1;
+            }
+            if (issued) mbar_wait(v_full, (issued - 1) & 1, a.err);
         }
-    } else if (warp == 5) {
-        // ---------------------------------------------------- tensor cores
+    } else if (warp == 9) {
+        // ------------------------------------------------------ tensor cores
         if (lane == 0) {
             bool ok = mbar_wait(q_full, 0, a.err);
-            auto issue_s = [&](int j) {
-                const uint32_t kb = sbase + (uint32_t)((j & 1) ? kOffK1 : kOffK0);
-                const uint32_t qb = sbase + kOffQ;
+            auto issue_s = [&](int t, int j) {
+                const uint32_t kb = sbase + (uint32_t)(kPOffK + (j & 1) * kTile);
+                const uint32_t qb = sbase + (uint32_t)(kPOffQ + t * kTile);
 #pragma unroll
                 for (int s = 0; s < kHD / 16; ++s) {
                     const uint32_t off = (uint32_t)((s >> 2) * kHalf + (s & 3) * 32);
-                    umma_bf16(tS, umma_desc_sw128(qb + off, 16, 1024), umma_desc_sw128(kb + off, 16, 1024), kIdescS,
-                              s > 0 ? 1u : 0u);
+                    umma_bf16(tS[t], umma_desc_sw128(qb + off, 16, 1024), umma_desc_sw128(kb + off, 16, 1024),
+                              kIdescS, s > 0 ? 1u : 0u);
                 }
-                umma_commit(s_full);
+                umma_commit(&s_full[t]);
             };
-            if (ok && mbar_wait(&kv_full[0], 0, a.err)) {
+            auto issue_pv = [&](int t, int j) {
+                const uint32_t vb = sbase + kPOffV;
+                const uint32_t pb = sbase + (uint32_t)(kPOffP + t * kTile);
+#pragma unroll
+                for (int s = 0; s < kBN / 16; ++s) {
+                    const uint32_t aoff = (uint32_t)((s >> 2) * kHalf + (s & 3) * 32);
+                    umma_bf16(tO[t], umma_desc_sw128(pb + aoff, 16, 1024),
+                              umma_desc_sw128(vb + (uint32_t)s * 2048u, kHalf, 1024), kIdescO,
+                              (j > 0 || s > 0) ? 1u : 0u);
+                }
+                umma_commit(&o_done[t]);
+            };
+            // block 0: S of both tiles
+            if (ok && mbar_wait(&k_full[0], 0, a.err)) {
                 tc_fence_after();
-                issue_s(0);
+                issue_s(0, 0);
+                if (nB > 0) issue_s(1, 0);
+                umma_commit(&k_empty[0]);
             } else {
                 ok = false;
             }
             for (int j = 0; j < nblk && ok; ++j) {
-                if (!mbar_wait(p_full, j & 1, a.err)) break;
-                tc_fence_after();
-                const uint32_t vb = sbase + (uint32_t)((j & 1) ? kOffV1 : kOffV0);
-                const uint32_t pb = sbase + kOffP;
-#pragma unroll
-                for (int s = 0; s < kBN / 16; ++s) {
-                    const uint32_t aoff = (uint32_t)((s >> 2) * kHalf + (s & 3) * 32);
-                    umma_bf16(tO, umma_desc_sw128(pb + aoff, 16, 1024),
-                              umma_desc_sw128(vb + (uint32_t)s * 2048u, kHalf, 1024), kIdescO,
-                              (j > 0 || s > 0) ? 1u : 0u);
-                }
-                umma_commit(&kv_empty[j & 1]);
-                umma_commit(o_done);
-                if (j + 1 < nblk) {
-                    if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, a.err)) break;
+                const bool useA = j < nA, useB = j < nB;
+                if (!mbar_wait(v_full, j & 1, a.err)) break;
+                if (useA) {
+                    if (!mbar_wait(&p_full[0], j & 1, a.err)) break;
                     tc_fence_after();
-                    issue_s(j + 1);
+                    issue_pv(0, j);
                 }
+                // tile A's next S overlaps tile B's softmax of this block
+                const bool nextA = j + 1 < nA, nextB = j + 1 < nB;
+                if (nextA || nextB) {
+                    if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, a.err)) break;
+                    tc_fence_after();
+                    if (nextA) issue_s(0, j + 1);
+                }
+                if (useB) {
+                    if (!mbar_wait(&p_full[1], j & 1, a.err)) break;
+                    tc_fence_after();
+                    issue_pv(1, j);
+                }
+                umma_commit(v_empty);
+                if (nextB) issue_s(1, j + 1);
+                if (nextA || nextB) umma_commit(&k_empty[(j + 1) & 1]);
             }
-            // all tensor-core work of this CTA completes before TMEM is freed
             umma_commit(drain);
             mbar_wait(drain, 0, a.err);
         }
     } else {
-        // ---------------------------------------------------------- softmax
-        const int r = threadIdx.x;  // query row within the tile
-        const uint32_t lrow = (uint32_t)(warp * 32) << 16;
+        // ------------------------------------------------------------ softmax
+        const int t = warp >> 2;                // tile 0 (A) or 1 (B)
+        const int r = threadIdx.x & 127;        // query row within the tile
+        const int qt = t ? tB : tA;
+        const int nmine = t ? nB : nA;
+        const uint32_t lrow = (uint32_t)((warp & 3) * 32) << 16;
         const float c = a.scale_log2;
+        // Running max in log2 units (m = max * c). It is raised only when a
+        // new score exceeds it by more than 8 (P values stay below 2^8, exact
+        // enough in bf16 and fp32), so O in TMEM is rescaled rarely; l and O
+        // always refer to the same m, so the result does not change.
         float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        uint8_t* P = base + kOffP;
-        // tcgen05.ld / st are warp-collective: a warp leaves the loop as a whole
-        for (int j = 0; j < nblk; ++j) {
-            if (!__all_sync(0xffffffffu, mbar_wait(s_full, j & 1, a.err))) { ok = false; break; }
+        bool ok = nmine > 0;
+        uint8_t* P = base + kPOffP + t * kTile;
+        for (int j = 0; j < nmine; ++j) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, a.err))) { ok = false; break; }
             tc_fence_after();
-            uint32_t sv[4][32];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) tmem_ld32(tS + lrow + 32 * q, sv[q]);
-            tmem_wait_ld();
             const bool diag = a.causal && j == qt;
+            // pass 1: row max (two TMEM loads in flight per wait)
             float mx = -INFINITY;
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
+            for (int q = 0; q < 4; q += 2) {
+                uint32_t sv[2][32];
+                tmem_ld32(tS[t] + lrow + 32 * q, sv[0]);
+                tmem_ld32(tS[t] + lrow + 32 * (q + 1), sv[1]);
+                tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    float x = __uint_as_float(sv[q][i]);
-                    if (diag && 32 * q + i > r) x = -INFINITY;
-                    sv[q][i] = __float_as_uint(x);
-                    mx = fmaxf(mx, x);
-                }
-            const float m_new = fmaxf(m, mx);  // finite: key 0 of a block is never masked for row r >= 0
-            const float alpha = exp2f((m - m_new) * c);
+                for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float x = (diag && 32 * (q + h2) + i > r) ? -INFINITY : __uint_as_float(sv[h2][i]);
+                        mx = fmaxf(mx, x);
+                    }
+            }
+            const float mxc = mx * c;
+            const bool raise = mxc > m + 8.0f;
+            const float m_new = raise ? mxc : m;
+            const float alpha = raise ? ex2_approx(m - m_new) : 1.0f;
             if (j > 0) {
-                if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, a.err))) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, a.err))) { ok = false; break; }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                if (__any_sync(0xffffffffu, raise)) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         uint32_t ov[32];
-                        tmem_ld32(tO + lrow + 32 * q, ov);
+                        tmem_ld32(tO[t] + lrow + 32 * q, ov);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                        tmem_st32(tO + lrow + 32 * q, ov);
+                        tmem_st32(tO[t] + lrow + 32 * q, ov);
                     }
                 }
             }
-            const float mc = m_new * c;
+            // pass 2: P = exp2(S * c - m) as bf16 into shared memory
             float sum = 0.f;
 #pragma unroll
-            for (int ch = 0; ch < 16; ++ch) {
-                uint32_t pk[4];
+            for (int q = 0; q < 4; q += 2) {
+                uint32_t sv[2][32];
+                tmem_ld32(tS[t] + lrow + 32 * q, sv[0]);
+                tmem_ld32(tS[t] + lrow + 32 * (q + 1), sv[1]);
+                tmem_wait_ld();
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int col = ch * 8 + 2 * e;
-                    const float p0 = exp2f(fmaf(__uint_as_float(sv[col >> 5][col & 31]), c, -mc));
-                    const float p1 = exp2f(fmaf(__uint_as_float(sv[(col + 1) >> 5][(col + 1) & 31]), c, -mc));
-                    sum += p0 + p1;
-                    pk[e] = (uint32_t)f32_to_bf16_bits(p0) | ((uint32_t)f32_to_bf16_bits(p1) << 16);
-                }
-                *reinterpret_cast<uint4*>(P + sw128_chunk(r, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+                    for (int ch = 0; ch < 4; ++ch) {
+                        uint32_t pk[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int i = ch * 8 + 2 * e, col = 32 * (q + h2) + i;
+                            const float p0 =
+                                (diag && col > r) ? 0.f : ex2_approx(fmaf(__uint_as_float(sv[h2][i]), c, -m_new));
+                            const float p1 = (diag && col + 1 > r)
+                                                 ? 0.f
+                                                 : ex2_approx(fmaf(__uint_as_float(sv[h2][i + 1]), c, -m_new));
+                            sum += p0 + p1;
+                            pk[e] = pack_bf16x2(p0, p1);
+                        }
+                        *reinterpret_cast<uint4*>(P + sw128_chunk(r, 4 * (q + h2) + ch)) =
+                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    }
             }
             l = l * alpha + sum;
             m = m_new;
             tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[t]);
         }
-        if (ok && __all_sync(0xffffffffu, mbar_wait(o_done, (nblk - 1) & 1, a.err))) {
+        if (ok && __all_sync(0xffffffffu, mbar_wait(&o_done[t], (nmine - 1) & 1, a.err))) {
             tc_fence_after();
             const float inv = 1.0f / l;
             uint16_t* orow = a.o + ((size_t)row0 + (size_t)qt * kBM + r) * kHD;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 uint32_t ov[32];
-                tmem_ld32(tO + lrow + 32 * q, ov);
+                tmem_ld32(tO[t] + lrow + 32 * q, ov);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i += 8) {
@@ -264,9 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        tmem_dealloc(tmem, kPTmemCols);
     }
 }
 
@@ -309,7 +394,7 @@ int configure() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return forge_fail(-1, "flash prefill: no device");
     if (done[dev]) return 0;
-    cudaError_t e = cudaFuncSetAttribute(k_flash_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e = cudaFuncSetAttribute(k_flash_prefill_pp, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
     if (e != cudaSuccess) return forge_fail(-1, "flash prefill: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done[dev] = true;
     return 0;
@@ -333,8 +418,8 @@ extern "C" FORGE_API int forge_flash_prefill(const uint16_t* q, const uint16_t* 
     CUtensorMap mq, mk, mv;
     if (make_map(&mq, q, rows) || make_map(&mk, k, rows) || make_map(&mv, v, rows)) return -1;
     PrefillArgs a{o, B, H, S, causal ? 1 : 0, (float)(1.4426950408889634 / 11.313708498984761), err};
-    dim3 grid((unsigned)(S / kBM), (unsigned)H, (unsigned)B);
-    k_flash_prefill<<<grid, kThreads, kSmem, (cudaStream_t)stream>>>(mq, mk, mv, a);
+    dim3 grid((unsigned)((S / kBM + 1) / 2), (unsigned)H, (unsigned)B);
+    k_flash_prefill_pp<<<grid, kPThreads, kPSmem, (cudaStream_t)stream>>>(mq, mk, mv, a);
     return forge_check_launch("forge_flash_prefill");
 }
 
