@@ -60,6 +60,7 @@ struct ForgeGemvArgs {
     unsigned long long* argmax_key;  // [Btot]
     int32_t nvalid;        // rows >= nvalid (zero padding) never win the argmax
     int32_t row_off;       // global index of row 0 in the argmax key (vocabulary shard)
+    void* bscratch;        // int4, batch > 4: forge_gemv_b_scratch_bytes(K) bytes for the batched path
     uint32_t* err;         // device error word
 };
 
@@ -67,7 +68,13 @@ struct ForgeGemvArgs {
 // mma column block). pdl: launch with programmatic stream serialization.
 int forge_gemv_launch(const ForgeGemvArgs& a, cudaStream_t stream, bool pdl);
 int forge_gemv_configure();
-int forge_gemv_launch_count(int K, int batch, bool split, bool q4);
+int forge_gemv_launch_count(int K, int batch, bool split, bool q4, bool batched);
+// Batched int4 path (gemv_batched.cu): up to forge_gemv_b_max_seq()
+// sequences per weight stream.
+int forge_gemv_b_max_seq();
+int64_t forge_gemv_b_scratch_bytes(int K);
+int forge_gemv_b_configure();
+int forge_gemv_b_launch(const ForgeGemvArgs& a, void* scratch, cudaStream_t stream, bool pdl);
 
 // ------------------------------------------------------ flash-decode launch
 struct ForgeAttnArgs {

@@ -323,12 +323,14 @@ int forge_gemv_configure() {
     return rc ? -1 : 0;
 }
 
-// Number of launches forge_gemv_launch issues for one call.
-int forge_gemv_launch_count(int K, int batch, bool split, bool q4) {
+// Number of launches forge_gemv_launch issues for one call (int4 with a
+// batched scratch: two per forge_gemv_b_max_seq() sequences).
+int forge_gemv_launch_count(int K, int batch, bool split, bool q4, bool batched) {
     const int row = q4 ? K : ((K + 31) / 32) * 64;
     int max_cols = (kMaxSmem - kFixedSmem - (q4 ? (K / 128) * 48 : 0)) / row;
     if (max_cols > 8) max_cols = 8;
     const int per = max_cols / ((split || q4) ? 2 : 1);
+    if (q4 && batched && batch > per) return 2 * ((batch + forge_gemv_b_max_seq() - 1) / forge_gemv_b_max_seq());
     return per > 0 ? (batch + per - 1) / per : 0;
 }
 
@@ -352,6 +354,22 @@ int forge_gemv_launch(const ForgeGemvArgs& a0, cudaStream_t stream, bool pdl) {
     if (max_cols > 8) max_cols = 8;
     const int per_launch = max_cols / cols_per_seq;
     if (per_launch < 1) return forge_fail(-1, "gemv: K=%d too large for the staged activation", a0.K);
+    if (q4 && a0.batch > per_launch && a0.bscratch && a0.pro != FORGE_PRO_EMBED_RMSNORM &&
+        a0.epi != FORGE_EPI_LOGITS) {
+        // larger batches: one weight stream per forge_gemv_b_max_seq() sequences
+        const int mx = forge_gemv_b_max_seq();
+        for (int b0 = 0; b0 < a0.batch; b0 += mx) {
+            ForgeGemvArgs a = a0;
+            a.batch = a0.batch - b0 < mx ? a0.batch - b0 : mx;
+            a.b0 = a0.b0 + b0;
+            a.x = a0.x + (size_t)b0 * a0.x_stride;
+            if (a.y) a.y = a0.y + (size_t)b0 * a0.y_stride;
+            if (a.q_out) a.q_out = a0.q_out + (size_t)b0 * a0.H * a0.hd;
+            if (a.s_out) a.s_out = a0.s_out + (size_t)b0 * a0.F;
+            if (int rc = forge_gemv_b_launch(a, a0.bscratch, stream, pdl && b0 == 0)) return rc;
+        }
+        return 0;
+    }
     for (int b0 = 0; b0 < a0.batch; b0 += per_launch) {
         ForgeGemvArgs a = a0;
         a.batch = a0.batch - b0 < per_launch ? a0.batch - b0 : per_launch;

@@ -1,0 +1,303 @@
+// gemv_batched.cu — int4 decode GEMV for larger batches: the weights are
+// streamed once per launch for up to 32 sequences.
+//
+// The small-batch kernel (gemv.cu) keeps every sequence's int8 activations
+// in shared memory, which limits one launch to 4 sequences; a batch of 32
+// would stream the weights 8 times. Here the activations are quantised once
+// per sequence by k_quant_x into a global scratch (the same int8 hi/lo
+// fragment order, per-group scales and column sums; the bytes are exactly
+// those the small-batch staging produces), and k_gemv_b reads them from L2
+// while each 16 KB weight piece in the TMA ring serves every column block of
+// 4 sequences. Per-group arithmetic and the order of every sum match
+// k_gemv, so results are bit-identical to the small-batch path.
+#include "common.cuh"
+#include "layout.cuh"
+#include "forge_internal.h"
+#include "gemv_core.cuh"
+
+namespace {
+constexpr int kCW = 8;                      // consumer warps
+constexpr int kThreads = (kCW + 1) * 32;    // + producer warp
+constexpr int kStages = 4;
+constexpr int kStageW = 16384, kStageS = 512, kStageBytes = kStageW + kStageS;
+constexpr int kMaxSeq = 32;                 // sequences per launch (8 column blocks of 4)
+constexpr int kRedFloats = 2 * kCW * 16 * kMaxSeq;
+
+// One CTA per sequence: the staging of the small-batch kernel into shared
+// memory (batch 1), then copied out to the batched global layout.
+template <int PRO>
+__global__ void __launch_bounds__(256) k_quant_x(const ForgeGemvArgs a, int nseq, uint8_t* xq_g, float* sx_g,
+                                                 int* ss_g) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    float* red = reinterpret_cast<float*>(smem);
+    const int G = a.K / 128;
+    float* sxf = red + 16;
+    int* ssum = reinterpret_cast<int*>(sxf + G * 4);
+    uint8_t* xq = reinterpret_cast<uint8_t*>(ssum + G * 8);
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x;
+    ForgeGemvArgs s = a;
+    s.batch = 1;
+    s.b0 = a.b0 + b;
+    s.x = a.x + (size_t)b * a.x_stride;
+    stage_x_q8<PRO, 256>(s, xq, sxf, ssum, red);
+    __syncthreads();
+    const int ncols = 2 * nseq;
+    for (int i = threadIdx.x; i < a.K / 2; i += 256) {  // words of 4 k, hi and lo columns
+        const int k = (i >> 1) * 4, col = i & 1;
+        *reinterpret_cast<uint32_t*>(xq_g + xq_index(k, 2 * b + col, ncols)) =
+            *reinterpret_cast<const uint32_t*>(xq + xq_index(k, col, 2));
+    }
+    for (int g = threadIdx.x; g < G; g += 256) {
+        sx_g[g * nseq + b] = sxf[g * 4];
+        ss_g[g * 2 * nseq + 2 * b] = ssum[g * 8];
+        ss_g[g * 2 * nseq + 2 * b + 1] = ssum[g * 8 + 1];
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, const uint8_t* __restrict__ xq_g,
+                                                        const float* __restrict__ sx_g,
+                                                        const int* __restrict__ ss_g) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* stages = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    float* red = reinterpret_cast<float*>(empty + kStages);
+    const int B = a.batch, G = a.K / 128;
+    float* sxs = red + kRedFloats;              // [G][B]
+    int* sss = reinterpret_cast<int*>(sxs + G * B);  // [G][2B]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KT = a.K >> 4;
+    constexpr int kItemKT = 128;
+    const int nitems = (KT + kItemKT - 1) / kItemKT;
+    const int units = a.N >> 4;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCW);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+
+    if (warp == kCW) {
+        // ------------------------------------------------------ producer
+        if (lane == 0) {
+            const uint8_t* wbase = static_cast<const uint8_t*>(a.w);
+            const uint8_t* sbase = static_cast<const uint8_t*>(a.s);
+            const int G4 = (KT / 8 + 3) / 4;
+            uint32_t it = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                for (int i = 0; i < nitems; ++i) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) { ok = false; break; }
+                    const int kt0 = i * kItemKT, nkt = min(kItemKT, KT - kt0);
+                    const uint32_t wb = (uint32_t)nkt * 128;
+                    const uint32_t sb = (uint32_t)(((nkt / 8) + 3) / 4) * 128u;
+                    mbar_arrive_expect_tx(&full[s], wb + sb);
+                    bulk_g2s(stages + s * kStageBytes, wbase + ((int64_t)u * KT + kt0) * 128, wb, &full[s]);
+                    bulk_g2s(stages + s * kStageBytes + kStageW, sbase + ((int64_t)u * G4 + kt0 / 32) * 128, sb,
+                             &full[s]);
+                    ++it;
+                }
+            }
+            for (uint32_t j = 0; j < (uint32_t)kStages && j < it; ++j) {
+                const uint32_t idx = it - 1 - j;
+                mbar_wait(&full[idx % kStages], (idx / kStages) & 1u, a.err);
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- consumers
+    pdl_wait();
+    for (int i = threadIdx.x; i < G * B; i += kCW * 32) sxs[i] = sx_g[i];
+    for (int i = threadIdx.x; i < G * 2 * B; i += kCW * 32) sss[i] = ss_g[i];
+    named_bar_sync(1, kCW * 32);
+
+    const int g = lane >> 2, t = lane & 3;
+    const int ncols = 2 * B;
+    const int ncb = (B + 3) / 4;
+    unsigned long long best = 0ull;
+    uint32_t it = 0;
+    int slot = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, slot ^= 1) {
+        float totA[kMaxSeq / 4][2], totB[kMaxSeq / 4][2];
+#pragma unroll
+        for (int c = 0; c < kMaxSeq / 4; ++c) totA[c][0] = totA[c][1] = totB[c][0] = totB[c][1] = 0.f;
+        for (int i = 0; i < nitems; ++i) {
+            const int s = it % kStages;
+            const uint32_t ph = (it / kStages) & 1u;
+            if (!mbar_wait(&full[s], ph, a.err)) { ok = false; break; }
+            const int kt0 = i * kItemKT, nkt = min(kItemKT, KT - kt0);
+            const uint8_t* st = stages + s * kStageBytes;
+            const uint16_t* sst = reinterpret_cast<const uint16_t*>(st + kStageW);
+            const int ng = nkt / 8;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {  // this warp's groups 2w and 2w+1 of the piece
+                const int gl = 2 * warp + h;
+                if (gl < ng) {
+                const int gg = kt0 / 8 + gl;
+                const uint4 w0 = *reinterpret_cast<const uint4*>(st + (4 * warp + 2 * h) * 512 + lane * 16);
+                const uint4 w1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 2 * h + 1) * 512 + lane * 16);
+                const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (gl >> 2) * 64 + g * 8 + (gl & 3) * 2);
+                uint32_t af[4][4];
+                dequant_q4_u8(w0.x, w0.y, af[0]);
+                dequant_q4_u8(w0.z, w0.w, af[1]);
+                dequant_q4_u8(w1.x, w1.y, af[2]);
+                dequant_q4_u8(w1.z, w1.w, af[3]);
+                const uint4* xg = reinterpret_cast<const uint4*>(xq_g) + (size_t)(2 * gg) * ncols * 4;
+#pragma unroll
+                for (int cb = 0; cb < kMaxSeq / 4; ++cb) {
+                    if (cb < ncb) {
+                    int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+                    const int col = min(cb * 8 + g, ncols - 1);
+                    const uint4 b0 = __ldg(xg + (size_t)col * 4 + t);
+                    const uint4 b1 = __ldg(xg + (size_t)(ncols + col) * 4 + t);
+                    mma_u8s8_16832(c0, af[0], b0.x, b0.y);
+                    mma_u8s8_16832(c1, af[1], b0.z, b0.w);
+                    mma_u8s8_16832(c0, af[2], b1.x, b1.y);
+                    mma_u8s8_16832(c1, af[3], b1.z, b1.w);
+                    const int sq = min(cb * 4 + t, B - 1);
+                    const int shi = sss[gg * 2 * B + 2 * sq], slo = sss[gg * 2 * B + 2 * sq + 1];
+                    const float sx = sxs[gg * B + sq];
+                    const float v0 = (float)(c0[0] + c1[0] - 7 * shi) + (float)(c0[1] + c1[1] - 7 * slo) * (1.0f / 256.0f);
+                    const float v1 = (float)(c0[2] + c1[2] - 7 * shi) + (float)(c0[3] + c1[3] - 7 * slo) * (1.0f / 256.0f);
+                    const float y0 = bf16_lo_f32(sc) * sx * v0;
+                    const float y1 = bf16_hi_f32(sc) * sx * v1;
+                    if (h == 0) { totA[cb][0] += y0; totA[cb][1] += y1; }
+                    else { totB[cb][0] += y0; totB[cb][1] += y1; }
+                    }
+                }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            ++it;
+        }
+        if (!ok) break;
+        // cross-warp reduction: lane (g, t) holds rows g / g+8 of sequences 4cb + t
+        float* rw = red + (slot * kCW + warp) * 16 * kMaxSeq;
+#pragma unroll
+        for (int cb = 0; cb < kMaxSeq / 4; ++cb) {
+            const int sq = cb * 4 + t;
+            if (cb < ncb && sq < B) {
+                rw[g * kMaxSeq + sq] = totA[cb][0] + totB[cb][0];
+                rw[(g + 8) * kMaxSeq + sq] = totA[cb][1] + totB[cb][1];
+            }
+        }
+        named_bar_sync(1, kCW * 32);
+        const int tid = threadIdx.x;
+        if (tid < 8 * B) {
+            const int p = tid & 7, b = tid >> 3;
+            const float* rs = red + slot * kCW * 16 * kMaxSeq;
+            float ylo = 0.f, yhi = 0.f;
+#pragma unroll
+            for (int w = 0; w < kCW; ++w) {
+                ylo += rs[(w * 16 + p) * kMaxSeq + b];
+                yhi += rs[(w * 16 + p + 8) * kMaxSeq + b];
+            }
+            epilogue<EPI>(a, u, p, b, ylo, yhi, best);
+        }
+    }
+}
+
+template <int EPI>
+int launch_b(const ForgeGemvArgs& a, const uint8_t* xq, const float* sx, const int* ss, cudaStream_t stream, bool pdl,
+             int smem) {
+    const int units = a.N / 16;
+    int grid = forge_sm_count();
+    if (grid > units) grid = units;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_b<EPI>, a, xq, sx, ss);
+    return e == cudaSuccess ? 0 : forge_fail(-1, "batched gemv launch: %s", cudaGetErrorString(e));
+}
+
+template <int PRO>
+int launch_q(const ForgeGemvArgs& a, int nseq, uint8_t* xq, float* sx, int* ss, cudaStream_t stream, bool pdl) {
+    const int smem = 16 * 4 + (a.K / 128) * 12 * 4 + a.K * 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nseq);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_quant_x<PRO>, a, nseq, xq, sx, ss);
+    return e == cudaSuccess ? 0 : forge_fail(-1, "activation quantise launch: %s", cudaGetErrorString(e));
+}
+
+constexpr int smem_b(int K, int B) {
+    return kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4 + (K / 128) * B * 12;
+}
+}  // namespace
+
+int forge_gemv_b_max_seq() { return kMaxSeq; }
+
+int64_t forge_gemv_b_scratch_bytes(int K) {
+    return (int64_t)K * 2 * kMaxSeq + (int64_t)(K / 128) * kMaxSeq * 12 + 256;
+}
+
+int forge_gemv_b_configure() {
+    static bool done[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return forge_fail(-1, "batched gemv: no device");
+    if (done[dev]) return 0;
+    const int mx = 227 * 1024;
+    cudaError_t e = cudaSuccess;
+    auto set = [&](const void* f) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+    };
+    set((const void*)k_gemv_b<FORGE_EPI_STORE>);
+    set((const void*)k_gemv_b<FORGE_EPI_RESID>);
+    set((const void*)k_gemv_b<FORGE_EPI_QKV>);
+    set((const void*)k_gemv_b<FORGE_EPI_SWIGLU>);
+    set((const void*)k_quant_x<FORGE_PRO_PLAIN>);
+    set((const void*)k_quant_x<FORGE_PRO_RMSNORM>);
+    if (e != cudaSuccess) return forge_fail(-1, "batched gemv: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    done[dev] = true;
+    return 0;
+}
+
+// One chunk of up to kMaxSeq sequences: quantise, then one weight stream.
+// scratch: forge_gemv_b_scratch_bytes(K) bytes of device memory.
+int forge_gemv_b_launch(const ForgeGemvArgs& a, void* scratch, cudaStream_t stream, bool pdl) {
+    if (a.wkind != FORGE_W_Q4 || a.batch <= 0 || a.batch > kMaxSeq || !scratch)
+        return forge_fail(-1, "batched gemv: int4 weights, 1..%d sequences and a scratch buffer", kMaxSeq);
+    if (a.pro == FORGE_PRO_EMBED_RMSNORM || a.epi == FORGE_EPI_LOGITS)
+        return forge_fail(-1, "batched gemv: prologue/epilogue not supported");
+    const int smem = smem_b(a.K, a.batch);
+    if (smem > 227 * 1024) return forge_fail(-1, "batched gemv: K=%d too large", a.K);
+    uint8_t* xq = static_cast<uint8_t*>(scratch);
+    float* sx = reinterpret_cast<float*>(xq + (size_t)a.K * 2 * kMaxSeq);
+    int* ss = reinterpret_cast<int*>(sx + (size_t)(a.K / 128) * kMaxSeq);
+    int rc = a.pro == FORGE_PRO_RMSNORM ? launch_q<FORGE_PRO_RMSNORM>(a, a.batch, xq, sx, ss, stream, pdl)
+                                        : launch_q<FORGE_PRO_PLAIN>(a, a.batch, xq, sx, ss, stream, pdl);
+    if (rc) return rc;
+    switch (a.epi) {
+    case FORGE_EPI_STORE: return launch_b<FORGE_EPI_STORE>(a, xq, sx, ss, stream, true, smem);
+    case FORGE_EPI_RESID: return launch_b<FORGE_EPI_RESID>(a, xq, sx, ss, stream, true, smem);
+    case FORGE_EPI_QKV: return launch_b<FORGE_EPI_QKV>(a, xq, sx, ss, stream, true, smem);
+    case FORGE_EPI_SWIGLU: return launch_b<FORGE_EPI_SWIGLU>(a, xq, sx, ss, stream, true, smem);
+    default: return forge_fail(-1, "batched gemv: unknown epilogue %d", a.epi);
+    }
+}

@@ -131,6 +131,7 @@ struct ForgeB200 {
     int Hfull = 0, Hkvfull = 0, Ffull = 0, Vfull = 0;
     int h0 = 0, kv0 = 0, f0 = 0, v0 = 0;  // first head / kv head / FFN row / vocabulary row of this rank
     void* comm = nullptr;                 // NCCL communicator
+    void* bscratch = nullptr;             // int4 activations of the batched GEMV path
     float* logits_all = nullptr;          // [tp][Bmax][Vpad] all-gathered logits
 
     void* alloc(size_t bytes) {
@@ -277,6 +278,7 @@ int load_embed_impl(ForgeB200* h, const Src& emb, const Src* head, const float* 
 // writes the given device arrays; the step itself passes the handle's own.
 ForgeGemvArgs gemv_base(const ForgeB200* h, int B) {
     ForgeGemvArgs a{};
+    a.bscratch = h->bscratch;
     a.wkind = h->q4 ? FORGE_W_Q4 : FORGE_W_BF16;
     a.batch = B;
     a.split = h->split_for(B);
@@ -595,7 +597,7 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
     cudaGetDeviceProperties(&prop, device);
     if (prop.major != 10) return forge_fail(FORGE_KERNEL_UNSUPPORTED, "forge_b200_create: needs an sm_100 device (got sm_%d%d)", prop.major, prop.minor);
 
-    if (forge_gemv_configure() || forge_attn_configure()) return -1;
+    if (forge_gemv_configure() || forge_gemv_b_configure() || forge_attn_configure()) return -1;
     forge_sm_count();
     ForgeB200* h = new ForgeB200();
     h->desc = m;
@@ -662,6 +664,8 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
     }
     h->counters = (uint32_t*)h->alloc(4 * (size_t)h->Bmax * h->Hkv);
     h->err = (uint32_t*)h->alloc(16);
+    if (h->q4 && h->Bmax > 4)
+        h->bscratch = h->alloc((size_t)forge_gemv_b_scratch_bytes(std::max({h->d, h->qd, h->F})));
     size_t st = std::max({(size_t)h->nqkv * d, (size_t)2 * h->F * d, (size_t)d * h->F, (size_t)d * h->qd,
                           (size_t)h->Vpad * d});
     h->stA = (uint16_t*)h->alloc(st * 2);
@@ -961,9 +965,9 @@ FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
     if (!h || batch <= 0) return -1;
     if (fused_for(h, batch)) return 1;
     const bool split = h->split_for(batch);
-    auto launches = [&](int K) { return forge_gemv_launch_count(K, batch, split, h->q4); };
+    auto launches = [&](int K) { return forge_gemv_launch_count(K, batch, split, h->q4, h->bscratch != nullptr); };
     int per_layer = launches(h->d) * 2 + launches(h->qd) + launches(h->F) + 1;
-    return 1 + h->L * per_layer + forge_gemv_launch_count(h->d, batch, split, false) + 1;
+    return 1 + h->L * per_layer + forge_gemv_launch_count(h->d, batch, split, false, false) + 1;
 }
 int64_t forge_b200_width(const ForgeB200* h, int which) {
     if (!h) return 0;

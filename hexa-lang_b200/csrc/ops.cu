@@ -40,6 +40,32 @@ int gemv_entry(int wkind, const void* tiles, const void* stiles, int64_t N, int6
     a.w = tiles; a.s = stiles; a.N = (int32_t)N; a.K = (int32_t)K; a.wkind = wkind;
     a.batch = batch; a.split = exact ? 1 : 0; a.x = x; a.x_stride = (int32_t)K;
     a.pro = FORGE_PRO_PLAIN; a.epi = FORGE_EPI_STORE; a.y = y; a.y_stride = (int32_t)N; a.err = err;
+    if (wkind == FORGE_W_Q4 && batch > 4) {
+        // batched path: library-owned activation scratch, grown on demand
+        static std::mutex mu;
+        static void* buf[64] = {nullptr};
+        static int64_t cap[64] = {0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (forge_gemv_b_configure()) return -1;
+        std::lock_guard<std::mutex> lk(mu);
+        const int64_t need = forge_gemv_b_scratch_bytes((int)K);
+        if (need > cap[dev]) {
+            if (buf[dev]) {
+                cudaStreamSynchronize((cudaStream_t)stream);
+                cudaFree(buf[dev]);
+            }
+            buf[dev] = nullptr;
+            cap[dev] = 0;
+            if (cudaMalloc(&buf[dev], (size_t)need) != cudaSuccess) {
+                cudaGetLastError();
+                return forge_fail(-1, "forge_gemv: batched scratch of %lld bytes", (long long)need);
+            }
+            cap[dev] = need;
+        }
+        a.bscratch = buf[dev];
+        return forge_gemv_launch(a, (cudaStream_t)stream, false) ? FORGE_INVALID_ARGS : 0;
+    }
     int rc = forge_gemv_launch(a, (cudaStream_t)stream, false);
     return rc ? FORGE_INVALID_ARGS : 0;
 }

@@ -254,7 +254,8 @@ def test_block_entries_chain_equals_decode_step(forge, cuda, q4):
 
     # LMHEAD_ARGMAX family on the chained hidden state
     X = L.hexa_farr_f32_alloc(B * d)
-    C.memmove(X.contents.h_buf, x.cpu().numpy().ctypes.data, B * d * 4)
+    xh = np.ascontiguousarray(x.cpu().numpy())  # kept alive for the copy
+    C.memmove(X.contents.h_buf, xh.ctypes.data, B * d * 4)
     TK = L.hexa_farr_i32_alloc(B)
     assert dispatch(F, F.FORGE_KERNEL_LMHEAD_ARGMAX, prec, (B, 0, 0, B), (h, X), (TK,), v2=True) == 0
     m.sync()

@@ -129,3 +129,29 @@ def test_flash_decode(forge, oracle, cuda, B, H, Hkv, hd, lmax, pos):
         forge.check(forge.lib().forge_ops_check(), "fd error word")
         got = out.cpu().numpy()
         assert np.abs(got - ref).max() < 2e-5 * max(1.0, np.abs(ref).max()), np.abs(got - ref).max()
+
+
+@pytest.mark.parametrize("N,K", [(4096, 4096), (4096, 11008), (22016, 4096)])
+@pytest.mark.parametrize("batch", [5, 8, 32, 37])
+def test_gemv_int4_batched_bit_identical(forge, oracle, cuda, N, K, batch):
+    """Above 4 sequences the int4 GEMV streams the weights once for up to 32
+    sequences (activations quantised once into a global scratch); it must give
+    exactly the bits of the small-batch path run on slices of <= 4 sequences."""
+    import torch
+    rng = np.random.default_rng(N + K + batch)
+    w = oracle.fill_normal_bf16(N * K, 9, N * 3 + K, 0.02).reshape(N, K)
+    X = (rng.standard_normal((batch, K)) * rng.uniform(0.1, 4.0, (batch, 1))).astype(np.float32)
+    _, _, tiles, stiles = forge.q4_pack(_dev_bf16(torch, w, cuda))
+    xd = torch.from_numpy(X).to(cuda)
+    lib = forge.lib()
+    yb = torch.full((batch, N), float("nan"), device=cuda)
+    forge.check(lib.forge_gemv_w4a16_g128(tiles.data_ptr(), stiles.data_ptr(), N, K, xd.data_ptr(), batch,
+                                          yb.data_ptr(), 1, 0), "batched")
+    ys = torch.full((batch, N), float("nan"), device=cuda)
+    for b0 in range(0, batch, 4):
+        nb = min(4, batch - b0)
+        forge.check(lib.forge_gemv_w4a16_g128(tiles.data_ptr(), stiles.data_ptr(), N, K, xd[b0:].data_ptr(), nb,
+                                              ys[b0:].data_ptr(), 1, 0), "grouped")
+    torch.cuda.synchronize()
+    forge.check(lib.forge_ops_check(), "error word")
+    assert torch.equal(yb.view(torch.int32), ys.view(torch.int32))
