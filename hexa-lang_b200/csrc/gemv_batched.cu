@@ -56,7 +56,9 @@ __global__ void __launch_bounds__(256) k_quant_x(const ForgeGemvArgs a, int nseq
     }
 }
 
-template <int EPI>
+// NCB: column blocks of 4 sequences per launch (2, 4 or 8), so the B-fragment
+// loads of a group are all issued before its MMAs.
+template <int EPI, int NCB>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, const uint8_t* __restrict__ xq_g,
                                                         const float* __restrict__ sx_g,
                                                         const int* __restrict__ ss_g) {
@@ -123,15 +125,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
 
     const int g = lane >> 2, t = lane & 3;
     const int ncols = 2 * B;
-    const int ncb = (B + 3) / 4;
     unsigned long long best = 0ull;
     uint32_t it = 0;
     int slot = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, slot ^= 1) {
-        float totA[kMaxSeq / 4][2], totB[kMaxSeq / 4][2];
+        float totA[NCB][2], totB[NCB][2];
 #pragma unroll
-        for (int c = 0; c < kMaxSeq / 4; ++c) totA[c][0] = totA[c][1] = totB[c][0] = totB[c][1] = 0.f;
+        for (int c = 0; c < NCB; ++c) totA[c][0] = totA[c][1] = totB[c][0] = totB[c][1] = 0.f;
         for (int i = 0; i < nitems; ++i) {
             const int s = it % kStages;
             const uint32_t ph = (it / kStages) & 1u;
@@ -154,17 +155,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
                 dequant_q4_u8(w1.x, w1.y, af[2]);
                 dequant_q4_u8(w1.z, w1.w, af[3]);
                 const uint4* xg = reinterpret_cast<const uint4*>(xq_g) + (size_t)(2 * gg) * ncols * 4;
+                uint4 bf[NCB][2];
 #pragma unroll
-                for (int cb = 0; cb < kMaxSeq / 4; ++cb) {
-                    if (cb < ncb) {
-                    int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+                for (int cb = 0; cb < NCB; ++cb) {
                     const int col = min(cb * 8 + g, ncols - 1);
-                    const uint4 b0 = __ldg(xg + (size_t)col * 4 + t);
-                    const uint4 b1 = __ldg(xg + (size_t)(ncols + col) * 4 + t);
-                    mma_u8s8_16832(c0, af[0], b0.x, b0.y);
-                    mma_u8s8_16832(c1, af[1], b0.z, b0.w);
-                    mma_u8s8_16832(c0, af[2], b1.x, b1.y);
-                    mma_u8s8_16832(c1, af[3], b1.z, b1.w);
+                    bf[cb][0] = __ldg(xg + (size_t)col * 4 + t);
+                    bf[cb][1] = __ldg(xg + (size_t)(ncols + col) * 4 + t);
+                }
+#pragma unroll
+                for (int cb = 0; cb < NCB; ++cb) {
+                    int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+                    mma_u8s8_16832(c0, af[0], bf[cb][0].x, bf[cb][0].y);
+                    mma_u8s8_16832(c1, af[1], bf[cb][0].z, bf[cb][0].w);
+                    mma_u8s8_16832(c0, af[2], bf[cb][1].x, bf[cb][1].y);
+                    mma_u8s8_16832(c1, af[3], bf[cb][1].z, bf[cb][1].w);
                     const int sq = min(cb * 4 + t, B - 1);
                     const int shi = sss[gg * 2 * B + 2 * sq], slo = sss[gg * 2 * B + 2 * sq + 1];
                     const float sx = sxs[gg * B + sq];
@@ -174,7 +178,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
                     const float y1 = bf16_hi_f32(sc) * sx * v1;
                     if (h == 0) { totA[cb][0] += y0; totA[cb][1] += y1; }
                     else { totB[cb][0] += y0; totB[cb][1] += y1; }
-                    }
                 }
                 }
             }
@@ -186,9 +189,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
         // cross-warp reduction: lane (g, t) holds rows g / g+8 of sequences 4cb + t
         float* rw = red + (slot * kCW + warp) * 16 * kMaxSeq;
 #pragma unroll
-        for (int cb = 0; cb < kMaxSeq / 4; ++cb) {
+        for (int cb = 0; cb < NCB; ++cb) {
             const int sq = cb * 4 + t;
-            if (cb < ncb && sq < B) {
+            if (sq < B) {
                 rw[g * kMaxSeq + sq] = totA[cb][0] + totB[cb][0];
                 rw[(g + 8) * kMaxSeq + sq] = totA[cb][1] + totB[cb][1];
             }
@@ -209,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
     }
 }
 
-template <int EPI>
+template <int EPI, int NCB>
 int launch_b(const ForgeGemvArgs& a, const uint8_t* xq, const float* sx, const int* ss, cudaStream_t stream, bool pdl,
              int smem) {
     const int units = a.N / 16;
@@ -225,8 +228,16 @@ int launch_b(const ForgeGemvArgs& a, const uint8_t* xq, const float* sx, const i
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_b<EPI>, a, xq, sx, ss);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_b<EPI, NCB>, a, xq, sx, ss);
     return e == cudaSuccess ? 0 : forge_fail(-1, "batched gemv launch: %s", cudaGetErrorString(e));
+}
+
+template <int EPI>
+int launch_bn(const ForgeGemvArgs& a, const uint8_t* xq, const float* sx, const int* ss, cudaStream_t stream,
+              bool pdl, int smem) {
+    if (a.batch <= 8) return launch_b<EPI, 2>(a, xq, sx, ss, stream, pdl, smem);
+    if (a.batch <= 16) return launch_b<EPI, 4>(a, xq, sx, ss, stream, pdl, smem);
+    return launch_b<EPI, 8>(a, xq, sx, ss, stream, pdl, smem);
 }
 
 template <int PRO>
@@ -267,10 +278,13 @@ int forge_gemv_b_configure() {
     auto set = [&](const void* f) {
         if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
     };
-    set((const void*)k_gemv_b<FORGE_EPI_STORE>);
-    set((const void*)k_gemv_b<FORGE_EPI_RESID>);
-    set((const void*)k_gemv_b<FORGE_EPI_QKV>);
-    set((const void*)k_gemv_b<FORGE_EPI_SWIGLU>);
+#define FORGE_SET_B(E) \
+    set((const void*)k_gemv_b<E, 2>); set((const void*)k_gemv_b<E, 4>); set((const void*)k_gemv_b<E, 8>)
+    FORGE_SET_B(FORGE_EPI_STORE);
+    FORGE_SET_B(FORGE_EPI_RESID);
+    FORGE_SET_B(FORGE_EPI_QKV);
+    FORGE_SET_B(FORGE_EPI_SWIGLU);
+#undef FORGE_SET_B
     set((const void*)k_quant_x<FORGE_PRO_PLAIN>);
     set((const void*)k_quant_x<FORGE_PRO_RMSNORM>);
     if (e != cudaSuccess) return forge_fail(-1, "batched gemv: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -294,10 +308,10 @@ int forge_gemv_b_launch(const ForgeGemvArgs& a, void* scratch, cudaStream_t stre
                                         : launch_q<FORGE_PRO_PLAIN>(a, a.batch, xq, sx, ss, stream, pdl);
     if (rc) return rc;
     switch (a.epi) {
-    case FORGE_EPI_STORE: return launch_b<FORGE_EPI_STORE>(a, xq, sx, ss, stream, true, smem);
-    case FORGE_EPI_RESID: return launch_b<FORGE_EPI_RESID>(a, xq, sx, ss, stream, true, smem);
-    case FORGE_EPI_QKV: return launch_b<FORGE_EPI_QKV>(a, xq, sx, ss, stream, true, smem);
-    case FORGE_EPI_SWIGLU: return launch_b<FORGE_EPI_SWIGLU>(a, xq, sx, ss, stream, true, smem);
+    case FORGE_EPI_STORE: return launch_bn<FORGE_EPI_STORE>(a, xq, sx, ss, stream, true, smem);
+    case FORGE_EPI_RESID: return launch_bn<FORGE_EPI_RESID>(a, xq, sx, ss, stream, true, smem);
+    case FORGE_EPI_QKV: return launch_bn<FORGE_EPI_QKV>(a, xq, sx, ss, stream, true, smem);
+    case FORGE_EPI_SWIGLU: return launch_bn<FORGE_EPI_SWIGLU>(a, xq, sx, ss, stream, true, smem);
     default: return forge_fail(-1, "batched gemv: unknown epilogue %d", a.epi);
     }
 }
