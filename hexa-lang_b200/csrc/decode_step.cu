@@ -280,26 +280,31 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
                 // warp w: groups 2w and 2w+1 of the piece (int8 tensor-core path)
                 const int ng = nkt / 8;
                 const int gA = 2 * warp;
-                if (gA < ng) {
-                    const uint16_t* sst = reinterpret_cast<const uint16_t*>(st + kPiece);
+                const uint16_t* sst = reinterpret_cast<const uint16_t*>(st + kPiece);
+                if (gA + 1 < ng) {
+                    // both groups in one block so their loads and MMAs interleave
+                    const uint4 wA0 = *reinterpret_cast<const uint4*>(st + (4 * warp) * 512 + lane * 16);
+                    const uint4 wA1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 1) * 512 + lane * 16);
+                    const uint4 wB0 = *reinterpret_cast<const uint4*>(st + (4 * warp + 2) * 512 + lane * 16);
+                    const uint4 wB1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 3) * 512 + lane * 16);
+                    const uint32_t scA = *reinterpret_cast<const uint32_t*>(sst + (gA >> 2) * 64 + g * 8 + (gA & 3) * 2);
+                    const int gB = gA + 1;
+                    const uint32_t scB = *reinterpret_cast<const uint32_t*>(sst + (gB >> 2) * 64 + g * 8 + (gB & 3) * 2);
+                    float yA0, yA1, yB0, yB1;
+                    q4_group(wA0, wA1, xq, kt0 / 8 + gA, ncols, col, t, scA, sxf, ssum, a.batch, yA0, yA1);
+                    q4_group(wB0, wB1, xq, kt0 / 8 + gB, ncols, col, t, scB, sxf, ssum, a.batch, yB0, yB1);
+                    tot[0] += yA0;
+                    tot[1] += yA1;
+                    tot2[0] += yB0;
+                    tot2[1] += yB1;
+                } else if (gA < ng) {
+                    const uint4 w0 = *reinterpret_cast<const uint4*>(st + (4 * warp) * 512 + lane * 16);
+                    const uint4 w1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 1) * 512 + lane * 16);
+                    const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (gA >> 2) * 64 + g * 8 + (gA & 3) * 2);
                     float y0, y1;
-                    {
-                        const uint4 w0 = *reinterpret_cast<const uint4*>(st + (4 * warp) * 512 + lane * 16);
-                        const uint4 w1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 1) * 512 + lane * 16);
-                        const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (gA >> 2) * 64 + g * 8 + (gA & 3) * 2);
-                        q4_group(w0, w1, xq, kt0 / 8 + gA, ncols, col, t, sc, sxf, ssum, a.batch, y0, y1);
-                        tot[0] += y0;
-                        tot[1] += y1;
-                    }
-                    if (gA + 1 < ng) {
-                        const int gB = gA + 1;
-                        const uint4 w0 = *reinterpret_cast<const uint4*>(st + (4 * warp + 2) * 512 + lane * 16);
-                        const uint4 w1 = *reinterpret_cast<const uint4*>(st + (4 * warp + 3) * 512 + lane * 16);
-                        const uint32_t sc = *reinterpret_cast<const uint32_t*>(sst + (gB >> 2) * 64 + g * 8 + (gB & 3) * 2);
-                        q4_group(w0, w1, xq, kt0 / 8 + gB, ncols, col, t, sc, sxf, ssum, a.batch, y0, y1);
-                        tot2[0] += y0;
-                        tot2[1] += y1;
-                    }
+                    q4_group(w0, w1, xq, kt0 / 8 + gA, ncols, col, t, sc, sxf, ssum, a.batch, y0, y1);
+                    tot[0] += y0;
+                    tot[1] += y1;
                 }
             } else {
                 const int ktw = 4 * warp;  // warp w: k-tiles 4w .. 4w+3 (two pairs)
