@@ -147,6 +147,13 @@ int forge_tp_allreduce_sum_f32(void* comm, float* buf, size_t count, cudaStream_
 int forge_tp_allreduce_max_u64(void* comm, unsigned long long* buf, size_t count, cudaStream_t stream);
 int forge_tp_allgather_f32(void* comm, const float* send, float* recv, size_t count, cudaStream_t stream);
 
+// One-shot all-reduce over NVLink peer memory (tp_allreduce.cu).
+struct ForgeTpAr;
+int forge_tp_ar_init(void* comm, int rank, int T, int cap, cudaStream_t stream, ForgeTpAr** out);
+void forge_tp_ar_destroy(ForgeTpAr* ar);
+int forge_tp_ar_capacity(const ForgeTpAr* ar);
+int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStream_t stream);
+
 // Per-device error word of the per-op entries (created on first use).
 uint32_t* forge_ops_err_word();
 // v2 FLASH_PREFILL family.

@@ -132,6 +132,7 @@ struct ForgeB200 {
     int h0 = 0, kv0 = 0, f0 = 0, v0 = 0;  // first head / kv head / FFN row / vocabulary row of this rank
     void* comm = nullptr;                 // NCCL communicator
     void* bscratch = nullptr;             // int4 activations of the batched GEMV path
+    ForgeTpAr* ar = nullptr;              // peer-memory all-reduce (tensor parallel)
     float* logits_all = nullptr;          // [tp][Bmax][Vpad] all-gathered logits
 
     void* alloc(size_t bytes) {
@@ -291,7 +292,12 @@ ForgeGemvArgs gemv_base(const ForgeB200* h, int B) {
 // all-reduce (sum) leaves x + sum of all partials on every rank.
 int resid_epi(const ForgeB200* h) { return h->tp_rank == 0 ? FORGE_EPI_RESID : FORGE_EPI_STORE; }
 int tp_sum(ForgeB200* h, float* x, int B) {
-    return h->comm ? forge_tp_allreduce_sum_f32(h->comm, x, (size_t)B * h->d, h->stream) : 0;
+    if (!h->comm) return 0;
+    // small vectors (up to 32K floats, 8 sequences of 4096): one-shot through
+    // peer memory; larger ones: NCCL's bandwidth-efficient protocols
+    if (h->ar && B * h->d <= 32768 && B * h->d <= forge_tp_ar_capacity(h->ar))
+        return forge_tp_ar_sum_f32(h->ar, x, B * h->d, h->err, h->stream);
+    return forge_tp_allreduce_sum_f32(h->comm, x, (size_t)B * h->d, h->stream);
 }
 
 // RMSNorm + QKV + RoPE, K/V appended at each sequence's position.
@@ -719,6 +725,14 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
         forge_b200_destroy(h);
         return -1;
     }
+    if (T > 1) {
+        // residual all-reduces through peer memory unless FORGE_TP_ALLREDUCE=nccl
+        const char* e = getenv("FORGE_TP_ALLREDUCE");
+        if (!(e && strcmp(e, "nccl") == 0) && forge_tp_ar_init(h->comm, R, T, h->Bmax * h->d, h->stream, &h->ar)) {
+            forge_b200_destroy(h);
+            return -1;
+        }
+    }
     *out = h;
     return 0;
 }
@@ -743,6 +757,7 @@ FORGE_API void forge_b200_destroy(ForgeB200* h) {
     if (h->stream) cudaStreamSynchronize(h->stream);
     for (auto& kv : h->graphs) cudaGraphExecDestroy(kv.second);
     h->graphs.clear();
+    if (h->ar) forge_tp_ar_destroy(h->ar);
     if (h->comm) forge_tp_comm_destroy(h->comm);  // after the graphs that hold its collectives
     for (void* p : h->allocs) cudaFree(p);
     if (h->h_tok) cudaFreeHost(h->h_tok);

@@ -1,0 +1,182 @@
+// tp_allreduce.cu — one-shot all-reduce (fp32 sum) over NVLink peer memory
+// for the tensor-parallel decode step.
+//
+// At decode sizes the residual all-reduce is a few KB to a few hundred KB,
+// where a collective library's protocol overhead is most of its cost. Each
+// rank here owns a receive buffer with one slot per source rank, mapped into
+// every peer through CUDA IPC. The kernel writes this rank's vector straight
+// into its slot on every peer (plain stores over NVLink), raises one flag per
+// (source rank, slice) on every peer, waits for the peers' flags in its own
+// memory, then sums the slots in rank order, so every rank ends with the same
+// bits. Two buffer generations alternate, so a rank that runs ahead writes
+// into the generation its peers finished reading.
+//
+// Every wait is bounded (%globaltimer, 2 s): on expiry the kernel sets the
+// handle's error word and returns.
+#include <cstring>
+#include <vector>
+#include "common.cuh"
+#include "forge_internal.h"
+
+namespace {
+constexpr int kSlices = 16;      // CTAs per all-reduce; each owns a contiguous slice
+constexpr int kThreads = 256;
+constexpr int kMaxRanks = 8;
+
+struct ArDev {
+    float* peer_buf[kMaxRanks];     // rank r's receive buffer [2][T][cap]
+    uint32_t* peer_flag[kMaxRanks]; // rank r's flags [2][T][kSlices]
+    uint32_t* epoch;                // this rank's [kSlices] counters
+    int T, rank, cap;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(kThreads) k_tp_allreduce(float* x, int n, const ArDev d, uint32_t* err) {
+    __shared__ uint32_t s_ep;
+    __shared__ int s_ok;
+    const int sl = blockIdx.x;
+    const int per = ((n + kSlices - 1) / kSlices + 3) & ~3;  // whole float4s per slice
+    const int s0 = sl * per, s1 = min(n, s0 + per);
+    if (threadIdx.x == 0) {
+        s_ep = d.epoch[sl] + 1;
+        d.epoch[sl] = s_ep;
+        s_ok = 1;
+    }
+    __syncthreads();
+    const uint32_t ep = s_ep;
+    const int gen = ep & 1;
+    const size_t slot = ((size_t)gen * d.T + d.rank) * d.cap;
+    // 1. this rank's slice into its slot on every rank (peer stores over NVLink)
+    for (int r = 0; r < d.T; ++r) {
+        float* dst = d.peer_buf[r] + slot;
+        for (int i = s0 + 4 * (int)threadIdx.x; i < s1; i += 4 * kThreads) {
+            if (i + 4 <= s1) {
+                *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(x + i);
+            } else {
+                for (int k = i; k < s1; ++k) dst[k] = x[k];
+            }
+        }
+    }
+    __syncthreads();
+    // 2. flags: "slice sl of rank `rank`, generation ep, has landed" (the
+    // release orders the CTA's data stores, made visible by the barrier,
+    // before the flag)
+    if (threadIdx.x < d.T)
+        st_release_sys(d.peer_flag[threadIdx.x] + ((size_t)gen * d.T + d.rank) * kSlices + sl, ep);
+    // 3. wait for every rank's flag of this slice in this rank's memory
+    if (threadIdx.x < d.T) {
+        const volatile uint32_t* f = d.peer_flag[d.rank] + ((size_t)gen * d.T + threadIdx.x) * kSlices + sl;
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t spins = 0;
+        while (*f != ep) {
+            if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > FORGE_WAIT_NS) {
+                atomicOr(err, FORGE_DEVERR_COUNTER_TIMEOUT);
+                s_ok = 0;
+                break;
+            }
+        }
+        (void)ld_acquire_sys(const_cast<const uint32_t*>(f));  // orders the data reads after the flag
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    // 4. sum the slots in rank order (the same bits on every rank)
+    const float* base = d.peer_buf[d.rank] + (size_t)gen * d.T * d.cap;
+    for (int i = s0 + (int)threadIdx.x; i < s1; i += kThreads) {
+        float acc = base[i];
+        for (int r = 1; r < d.T; ++r) acc += __ldcv(base + (size_t)r * d.cap + i);
+        x[i] = acc;
+    }
+}
+}  // namespace
+
+struct ForgeTpAr {
+    ArDev dev{};
+    void* local = nullptr;   // receive buffer + flags (one allocation)
+    uint32_t* epoch = nullptr;
+    std::vector<void*> opened;
+};
+
+// Allocates this rank's receive buffer (capacity `cap` floats per source
+// rank) and maps every peer's through CUDA IPC, exchanging the handles over
+// the NCCL communicator. All ranks call it together.
+int forge_tp_ar_init(void* comm, int rank, int T, int cap, cudaStream_t stream, ForgeTpAr** out) {
+    if (T < 2 || T > kMaxRanks || cap <= 0) return forge_fail(-1, "tp all-reduce: %d ranks (2..%d)", T, kMaxRanks);
+    ForgeTpAr* ar = new ForgeTpAr();
+    cap = (cap + 3) & ~3;
+    const size_t buf_bytes = (size_t)2 * T * cap * 4, flag_bytes = (size_t)2 * T * kSlices * 4;
+    if (cudaMalloc(&ar->local, buf_bytes + flag_bytes) != cudaSuccess ||
+        cudaMemset(ar->local, 0, buf_bytes + flag_bytes) != cudaSuccess ||
+        cudaMalloc(&ar->epoch, kSlices * 4) != cudaSuccess || cudaMemset(ar->epoch, 0, kSlices * 4) != cudaSuccess) {
+        cudaGetLastError();
+        forge_tp_ar_destroy(ar);
+        return forge_fail(-1, "tp all-reduce: device allocation failed");
+    }
+    cudaIpcMemHandle_t mine;
+    if (cudaIpcGetMemHandle(&mine, ar->local) != cudaSuccess) {
+        cudaGetLastError();
+        forge_tp_ar_destroy(ar);
+        return forge_fail(-1, "tp all-reduce: cudaIpcGetMemHandle failed");
+    }
+    // all-gather the 64-byte handles through device memory
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    void* dh = nullptr;
+    std::vector<char> all(hb * T);
+    int rc = 0;
+    if (cudaMalloc(&dh, hb * (T + 1)) != cudaSuccess) rc = forge_fail(-1, "tp all-reduce: handle buffer");
+    if (!rc && cudaMemcpy((char*)dh + hb * T, &mine, hb, cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = forge_fail(-1, "tp all-reduce: handle upload");
+    if (!rc) rc = forge_tp_allgather_f32(comm, (const float*)((char*)dh + hb * T), (float*)dh, hb / 4, stream);
+    if (!rc && (cudaStreamSynchronize(stream) != cudaSuccess ||
+                cudaMemcpy(all.data(), dh, hb * T, cudaMemcpyDeviceToHost) != cudaSuccess))
+        rc = forge_fail(-1, "tp all-reduce: handle exchange");
+    if (dh) cudaFree(dh);
+    for (int r = 0; r < T && !rc; ++r) {
+        void* p = ar->local;
+        if (r != rank) {
+            cudaIpcMemHandle_t h;
+            memcpy(&h, all.data() + hb * r, hb);
+            if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                rc = forge_fail(-1, "tp all-reduce: cudaIpcOpenMemHandle of rank %d failed", r);
+                break;
+            }
+            ar->opened.push_back(p);
+        }
+        ar->dev.peer_buf[r] = (float*)p;
+        ar->dev.peer_flag[r] = (uint32_t*)((char*)p + buf_bytes);
+    }
+    if (rc) {
+        forge_tp_ar_destroy(ar);
+        return rc;
+    }
+    ar->dev.epoch = ar->epoch;
+    ar->dev.T = T;
+    ar->dev.rank = rank;
+    ar->dev.cap = cap;
+    *out = ar;
+    return 0;
+}
+
+void forge_tp_ar_destroy(ForgeTpAr* ar) {
+    if (!ar) return;
+    for (void* p : ar->opened) cudaIpcCloseMemHandle(p);
+    if (ar->local) cudaFree(ar->local);
+    if (ar->epoch) cudaFree(ar->epoch);
+    delete ar;
+}
+
+int forge_tp_ar_capacity(const ForgeTpAr* ar) { return ar ? ar->dev.cap : 0; }
+
+int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStream_t stream) {
+    if (!ar || n <= 0 || n > ar->dev.cap) return forge_fail(-1, "tp all-reduce: %d floats above capacity", n);
+    k_tp_allreduce<<<kSlices, kThreads, 0, stream>>>(x, n, ar->dev, err);
+    return forge_check_launch("tp all-reduce");
+}

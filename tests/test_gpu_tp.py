@@ -2,7 +2,9 @@
 the sharded model (heads, FFN groups and vocabulary split, NCCL all-reduce
 after the O and down projections, max all-reduce of the argmax keys) must give
 the single-GPU logits up to summation order and the same greedy tokens.
-Runs as two spawned rank processes; skipped with fewer than two GPUs."""
+Runs as two spawned rank processes, with the residual all-reduce through
+peer memory (the default) and through NCCL; skipped with fewer than two
+GPUs."""
 import os
 import socket
 
@@ -38,7 +40,7 @@ def _run(fb, model_kw, tp_kw, device):
     return gen, np.stack(lgs)
 
 
-def _rank_main(rank, world, port, name, q):
+def _rank_main(rank, world, port, name, ar, q):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "hexa-lang_b200"))
@@ -46,7 +48,7 @@ def _rank_main(rank, world, port, name, q):
     import torch
     import torch.distributed as dist
     import forge_b200 as fb
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), FORGE_TP_ALLREDUCE=ar)
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
@@ -60,8 +62,9 @@ def _rank_main(rank, world, port, name, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("ar", ["peer", "nccl"])
 @pytest.mark.parametrize("name", list(CONFIGS))
-def test_tp2_matches_single_gpu(forge, cuda, name):
+def test_tp2_matches_single_gpu(forge, cuda, name, ar):
     import multiprocessing as mp
     import torch
     if torch.cuda.device_count() < 2:
@@ -70,7 +73,7 @@ def test_tp2_matches_single_gpu(forge, cuda, name):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, name, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, name, ar, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
