@@ -11,25 +11,24 @@
 //             LOGITS: LM head logits + first-max argmax (decoder_lib.hexa:485-500)
 //
 // Structure (one CTA per SM, persistent over 16-row units):
-//   warp 8 (producer)  streams each unit's weight tiles in 8 KB pieces with
-//                      cp.async.bulk into a 6-stage mbarrier ring; it never
-//                      waits on the previous kernel, so under programmatic
-//                      dependent launch the next layer's weights are already
-//                      in flight while the previous kernel drains.
-//   warps 0-7          build the bf16 B operand (hi/lo split of the fp32
-//                      activations) in shared memory once per CTA, then for
-//                      every piece dequantise int4 words straight into
-//                      mma.sync A-fragment registers (lop3 + bf16 sub, no
-//                      shared-memory round trip for weights beyond the TMA
-//                      landing zone), accumulate one 128-group in fp32 and
-//                      fold the group's bf16 scale in with one FMA per row.
-//   The eight warps split each piece along K; a shared-memory reduction and
-//   the fused epilogue finish every unit.
-// Why mma.sync: at bs1 each SM must retire ~46 int4 weights per clock to keep
-// up with HBM; FFMA dequant (~3-4 issue slots per weight) cannot, while the
-// fragment path costs ~1.1 slots per weight and keeps A in registers (a
-// tcgen05 A operand would have to round-trip bf16 through shared memory or
-// TMEM, 8 bytes of on-chip traffic per HBM byte).
+//   warp 8 (producer)  streams each unit's weight tiles in 16 KB pieces (plus
+//                      their 512 B of int4 scales) with cp.async.bulk into a
+//                      4-stage mbarrier ring; it never waits on the previous
+//                      kernel, so under programmatic dependent launch the next
+//                      kernel's weights are in flight while the previous one
+//                      drains.
+//   warps 0-7          stage the activations once per CTA (RMSNorm in the same
+//                      pass; int4: int8 hi/lo pairs per 128-group, bf16: hi/lo
+//                      bf16), then for every piece take A fragments straight
+//                      from the packed weights (int4: two LOP3 per register
+//                      into mma.sync.m16n8k32 u8 x s8; bf16: mma.sync.m16n8k16)
+//                      with the activations as B operand.
+//   The eight warps split each piece along K (two 128-groups per warp for
+//   int4); a shared-memory reduction and the fused epilogue finish each unit.
+// Why mma.sync: at batch 1-4 the GEMV has 1-8 columns; a tcgen05 MMA needs
+// M >= 64 rows of A in shared memory or TMEM, so the int4 codes would have to
+// be expanded on chip before every MMA, while the register-fragment path
+// consumes them as they land in the ring.
 #include <cstdio>
 #include <cstdlib>
 #include "common.cuh"
