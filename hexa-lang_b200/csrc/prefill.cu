@@ -264,13 +264,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 tmem_ld32(tS[t] + lrow + 32 * q, sv[0]);
                 tmem_ld32(tS[t] + lrow + 32 * (q + 1), sv[1]);
                 tmem_wait_ld();
+                if (diag) {
 #pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2)
+                    for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float x = (diag && 32 * (q + h2) + i > r) ? -INFINITY : __uint_as_float(sv[h2][i]);
-                        mx = fmaxf(mx, x);
-                    }
+                        for (int i = 0; i < 32; ++i)
+                            if (32 * (q + h2) + i <= r) mx = fmaxf(mx, __uint_as_float(sv[h2][i]));
+                } else {
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sv[h2][i]));
+                }
             }
             const float mxc = mx * c;
             const bool raise = mxc > m + 8.0f;
@@ -291,7 +296,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     }
                 }
             }
-            // pass 2: P = exp2(S * c - m) as bf16 into shared memory
+            // pass 2: P = exp2(S * c - m) as bf16 into shared memory; the
+            // causal mask only matters on the diagonal block
             float sum = 0.f;
 #pragma unroll
             for (int q = 0; q < 4; q += 2) {
@@ -307,11 +313,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             const int i = ch * 8 + 2 * e, col = 32 * (q + h2) + i;
-                            const float p0 =
-                                (diag && col > r) ? 0.f : ex2_approx(fmaf(__uint_as_float(sv[h2][i]), c, -m_new));
-                            const float p1 = (diag && col + 1 > r)
-                                                 ? 0.f
-                                                 : ex2_approx(fmaf(__uint_as_float(sv[h2][i + 1]), c, -m_new));
+                            float p0 = ex2_approx(fmaf(__uint_as_float(sv[h2][i]), c, -m_new));
+                            float p1 = ex2_approx(fmaf(__uint_as_float(sv[h2][i + 1]), c, -m_new));
+                            if (diag) {
+                                p0 = col > r ? 0.f : p0;
+                                p1 = col + 1 > r ? 0.f : p1;
+                            }
                             sum += p0 + p1;
                             pk[e] = pack_bf16x2(p0, p1);
                         }
