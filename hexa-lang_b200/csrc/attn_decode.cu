@@ -313,16 +313,23 @@ int forge_attn_configure() {
 }
 
 int forge_attn_pick_splits(int B, int Hkv, int lmax) {
-    // As many splits as still fit one wave of resident CTAs (3 per SM of a
-    // 148-SM B200 at ~65 KB of shared memory each): a second wave would wait
-    // for the first and double the latency of the short decode attention.
-    // Fixed so workspace sizes do not depend on which device is current.
+    // Splits per (sequence, kv head): the count whose CTAs fill whole waves of
+    // the resident slots (3 per SM of a 148-SM B200 at ~65 KB of shared
+    // memory each) best, each extra wave costing 0.1 of efficiency: short
+    // decode attention loses most to a partly filled last wave. Fixed so
+    // workspace sizes do not depend on which device is current.
     const int resident = 3 * 148;
-    int ns = resident / (B * Hkv);
+    const int pairs = B * Hkv;
     const int cap = (lmax + 127) / 128;  // at least ~128 keys per split at full context
-    if (ns > cap) ns = cap;
-    if (ns < 1) ns = 1;
-    return ns;
+    int best = 1;
+    double best_score = -1e9;
+    for (int ns = 1; ns <= cap; ++ns) {
+        const int items = pairs * ns;
+        const int waves = (items + resident - 1) / resident;
+        const double score = (double)items / ((double)waves * resident) - 0.1 * waves;
+        if (score > best_score + 1e-9) { best_score = score; best = ns; }
+    }
+    return best;
 }
 int64_t forge_attn_partial_floats(int B, int H, int hd, int nsplit) {
     return (int64_t)B * H * nsplit * (hd + 2);

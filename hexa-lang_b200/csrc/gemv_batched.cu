@@ -212,6 +212,189 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
     }
 }
 
+// bf16 weights: the activations as bf16 (no hi/lo split) in the mma.m16n8k16
+// B-fragment order of the small-batch kernel, all sequences of the launch
+// side by side (column = sequence).
+template <int PRO>
+__global__ void __launch_bounds__(256) k_conv_x(const ForgeGemvArgs a, int nseq, uint16_t* xf_g) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    float* red = reinterpret_cast<float*>(smem);
+    uint16_t* xf = reinterpret_cast<uint16_t*>(red + 16);
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x;
+    ForgeGemvArgs s = a;
+    s.batch = 1;
+    s.split = 0;
+    s.b0 = a.b0 + b;
+    s.x = a.x + (size_t)b * a.x_stride;
+    stage_x<PRO, 256>(s, xf, red);
+    zero_x_pad<256>(s, xf);
+    __syncthreads();
+    const int kpad = (a.K + 31) / 32 * 32;
+    for (int k = threadIdx.x; k < kpad; k += 256) xf_g[xf_index(k, b, nseq)] = xf[xf_index(k, 0, 1)];
+}
+
+template <int EPI, int NCB>  // NCB column blocks of 8 sequences
+__global__ void __launch_bounds__(kThreads, 1) k_gemv_bf16_b(const ForgeGemvArgs a, const uint16_t* __restrict__ xf_g) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* stages = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    float* red = reinterpret_cast<float*>(empty + kStages);
+    const int B = a.batch;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KT = a.K >> 4;
+    constexpr int kItemKT = 32;  // 16 KB pieces of 16x16 bf16 tiles
+    const int nitems = (KT + kItemKT - 1) / kItemKT;
+    const int units = a.N >> 4;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCW);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (warp == kCW) {
+        if (lane == 0) {
+            const uint8_t* wbase = static_cast<const uint8_t*>(a.w);
+            uint32_t it = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                for (int i = 0; i < nitems; ++i) {
+                    const int s = it % kStages;
+                    const uint32_t ph = (it / kStages) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, a.err)) { ok = false; break; }
+                    const int kt0 = i * kItemKT, nkt = min(kItemKT, KT - kt0);
+                    const uint32_t wb = (uint32_t)nkt * 512;
+                    mbar_arrive_expect_tx(&full[s], wb);
+                    bulk_g2s(stages + s * kStageBytes, wbase + ((int64_t)u * KT + kt0) * 512, wb, &full[s]);
+                    ++it;
+                }
+            }
+            for (uint32_t j = 0; j < (uint32_t)kStages && j < it; ++j) {
+                const uint32_t idx = it - 1 - j;
+                mbar_wait(&full[idx % kStages], (idx / kStages) & 1u, a.err);
+            }
+        }
+        return;
+    }
+    pdl_wait();
+    const int g = lane >> 2, t = lane & 3;
+    const int ncols = B;
+    unsigned long long best = 0ull;
+    uint32_t it = 0;
+    int slot = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, slot ^= 1) {
+        float tot[NCB][4], tot2[NCB][4];
+#pragma unroll
+        for (int c = 0; c < NCB; ++c)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) tot[c][e] = tot2[c][e] = 0.f;
+        for (int i = 0; i < nitems; ++i) {
+            const int s = it % kStages;
+            const uint32_t ph = (it / kStages) & 1u;
+            if (!mbar_wait(&full[s], ph, a.err)) { ok = false; break; }
+            const int kt0 = i * kItemKT, nkt = min(kItemKT, KT - kt0);
+            const uint8_t* st = stages + s * kStageBytes;
+            const int ktw = 4 * warp;  // warp w: k-tiles 4w .. 4w+3 (two pairs)
+            if (ktw < nkt) {
+                const int kp = (kt0 + ktw) >> 1;
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    if (ktw + 2 * j < nkt) {
+                        const uint4 a0 = *reinterpret_cast<const uint4*>(st + (ktw + 2 * j) * 512 + lane * 16);
+                        const uint4 a1 = (ktw + 2 * j + 1 < nkt)
+                            ? *reinterpret_cast<const uint4*>(st + (ktw + 2 * j + 1) * 512 + lane * 16)
+                            : make_uint4(0, 0, 0, 0);
+                        const uint32_t f0[4] = {a0.x, a0.y, a0.z, a0.w};
+                        const uint32_t f1[4] = {a1.x, a1.y, a1.z, a1.w};
+                        const uint4* xg = reinterpret_cast<const uint4*>(xf_g) + (size_t)(kp + j) * ncols * 4;
+                        uint4 bb[NCB];
+#pragma unroll
+                        for (int cb = 0; cb < NCB; ++cb) bb[cb] = __ldg(xg + (size_t)min(cb * 8 + g, ncols - 1) * 4 + t);
+#pragma unroll
+                        for (int cb = 0; cb < NCB; ++cb) {
+                            mma_bf16_16816(tot[cb], f0, bb[cb].x, bb[cb].y, tot[cb]);
+                            mma_bf16_16816(tot2[cb], f1, bb[cb].z, bb[cb].w, tot2[cb]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            ++it;
+        }
+        if (!ok) break;
+        // lane (g, t) holds rows g / g+8 of sequences 8cb + 2t and 8cb + 2t + 1
+        float* rw = red + (slot * kCW + warp) * 16 * kMaxSeq;
+#pragma unroll
+        for (int cb = 0; cb < NCB; ++cb) {
+            const int sq = cb * 8 + 2 * t;
+            if (sq < B) {
+                rw[g * kMaxSeq + sq] = tot[cb][0] + tot2[cb][0];
+                rw[(g + 8) * kMaxSeq + sq] = tot[cb][2] + tot2[cb][2];
+            }
+            if (sq + 1 < B) {
+                rw[g * kMaxSeq + sq + 1] = tot[cb][1] + tot2[cb][1];
+                rw[(g + 8) * kMaxSeq + sq + 1] = tot[cb][3] + tot2[cb][3];
+            }
+        }
+        named_bar_sync(1, kCW * 32);
+        const int tid = threadIdx.x;
+        if (tid < 8 * B) {
+            const int p = tid & 7, b = tid >> 3;
+            const float* rs = red + slot * kCW * 16 * kMaxSeq;
+            float ylo = 0.f, yhi = 0.f;
+#pragma unroll
+            for (int w = 0; w < kCW; ++w) {
+                ylo += rs[(w * 16 + p) * kMaxSeq + b];
+                yhi += rs[(w * 16 + p + 8) * kMaxSeq + b];
+            }
+            epilogue<EPI>(a, u, p, b, ylo, yhi, best);
+        }
+    }
+    if (EPI == FORGE_EPI_LOGITS) {
+        // thread (p, b) = (tid & 7, tid >> 3): reduce over the 8 row pairs
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+            best = v > best ? v : best;
+        }
+        const int tid = threadIdx.x;
+        if ((tid & 7) == 0 && (tid >> 3) < B && best != 0ull) atomicMax(a.argmax_key + a.b0 + (tid >> 3), best);
+    }
+}
+
+template <int EPI, int NCB>
+int launch_bf(const ForgeGemvArgs& a, const uint16_t* xf, cudaStream_t stream, int smem) {
+    const int units = a.N / 16;
+    int grid = forge_sm_count();
+    if (grid > units) grid = units;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemv_bf16_b<EPI, NCB>, a, xf);
+    return e == cudaSuccess ? 0 : forge_fail(-1, "batched bf16 gemv launch: %s", cudaGetErrorString(e));
+}
+
+template <int EPI>
+int launch_bfn(const ForgeGemvArgs& a, const uint16_t* xf, cudaStream_t stream, int smem) {
+    if (a.batch <= 8) return launch_bf<EPI, 1>(a, xf, stream, smem);
+    if (a.batch <= 16) return launch_bf<EPI, 2>(a, xf, stream, smem);
+    return launch_bf<EPI, 4>(a, xf, stream, smem);
+}
+
 template <int EPI, int NCB>
 int launch_b(const ForgeGemvArgs& a, const uint8_t* xq, const float* sx, const int* ss, cudaStream_t stream, bool pdl,
              int smem) {
@@ -265,7 +448,10 @@ constexpr int smem_b(int K, int B) {
 int forge_gemv_b_max_seq() { return kMaxSeq; }
 
 int64_t forge_gemv_b_scratch_bytes(int K) {
-    return (int64_t)K * 2 * kMaxSeq + (int64_t)(K / 128) * kMaxSeq * 12 + 256;
+    // int4: int8 hi/lo [K][2 x 32] + scales and sums; bf16: [K padded to 32][32] bf16
+    const int64_t q4 = (int64_t)K * 2 * kMaxSeq + (int64_t)(K / 128) * kMaxSeq * 12 + 256;
+    const int64_t bf = (int64_t)((K + 31) / 32 * 32) * 2 * kMaxSeq + 256;
+    return q4 > bf ? q4 : bf;
 }
 
 int forge_gemv_b_configure() {
@@ -287,6 +473,16 @@ int forge_gemv_b_configure() {
 #undef FORGE_SET_B
     set((const void*)k_quant_x<FORGE_PRO_PLAIN>);
     set((const void*)k_quant_x<FORGE_PRO_RMSNORM>);
+    set((const void*)k_conv_x<FORGE_PRO_PLAIN>);
+    set((const void*)k_conv_x<FORGE_PRO_RMSNORM>);
+#define FORGE_SET_BF(E) \
+    set((const void*)k_gemv_bf16_b<E, 1>); set((const void*)k_gemv_bf16_b<E, 2>); set((const void*)k_gemv_bf16_b<E, 4>)
+    FORGE_SET_BF(FORGE_EPI_STORE);
+    FORGE_SET_BF(FORGE_EPI_RESID);
+    FORGE_SET_BF(FORGE_EPI_QKV);
+    FORGE_SET_BF(FORGE_EPI_SWIGLU);
+    FORGE_SET_BF(FORGE_EPI_LOGITS);
+#undef FORGE_SET_BF
     if (e != cudaSuccess) return forge_fail(-1, "batched gemv: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done[dev] = true;
     return 0;
@@ -295,8 +491,38 @@ int forge_gemv_b_configure() {
 // One chunk of up to kMaxSeq sequences: quantise, then one weight stream.
 // scratch: forge_gemv_b_scratch_bytes(K) bytes of device memory.
 int forge_gemv_b_launch(const ForgeGemvArgs& a, void* scratch, cudaStream_t stream, bool pdl) {
-    if (a.wkind != FORGE_W_Q4 || a.batch <= 0 || a.batch > kMaxSeq || !scratch)
-        return forge_fail(-1, "batched gemv: int4 weights, 1..%d sequences and a scratch buffer", kMaxSeq);
+    if (a.batch <= 0 || a.batch > kMaxSeq || !scratch)
+        return forge_fail(-1, "batched gemv: 1..%d sequences and a scratch buffer", kMaxSeq);
+    if (a.wkind == FORGE_W_BF16) {
+        if (a.split || a.pro == FORGE_PRO_EMBED_RMSNORM)
+            return forge_fail(-1, "batched bf16 gemv: bf16 activations and plain/RMSNorm prologue only");
+        uint16_t* xf = static_cast<uint16_t*>(scratch);
+        const int kpad = (a.K + 31) / 32 * 32;
+        const int qsmem = 16 * 4 + kpad * 2;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(a.batch);
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = qsmem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 1 : 0;
+        cudaError_t e = a.pro == FORGE_PRO_RMSNORM ? cudaLaunchKernelEx(&cfg, k_conv_x<FORGE_PRO_RMSNORM>, a, a.batch, xf)
+                                                   : cudaLaunchKernelEx(&cfg, k_conv_x<FORGE_PRO_PLAIN>, a, a.batch, xf);
+        if (e != cudaSuccess) return forge_fail(-1, "activation convert launch: %s", cudaGetErrorString(e));
+        const int smem = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4;
+        switch (a.epi) {
+        case FORGE_EPI_STORE: return launch_bfn<FORGE_EPI_STORE>(a, xf, stream, smem);
+        case FORGE_EPI_RESID: return launch_bfn<FORGE_EPI_RESID>(a, xf, stream, smem);
+        case FORGE_EPI_QKV: return launch_bfn<FORGE_EPI_QKV>(a, xf, stream, smem);
+        case FORGE_EPI_SWIGLU: return launch_bfn<FORGE_EPI_SWIGLU>(a, xf, stream, smem);
+        case FORGE_EPI_LOGITS: return launch_bfn<FORGE_EPI_LOGITS>(a, xf, stream, smem);
+        default: return forge_fail(-1, "batched bf16 gemv: unknown epilogue %d", a.epi);
+        }
+    }
+    if (a.wkind != FORGE_W_Q4) return forge_fail(-1, "batched gemv: unknown weight kind");
     if (a.pro == FORGE_PRO_EMBED_RMSNORM || a.epi == FORGE_EPI_LOGITS)
         return forge_fail(-1, "batched gemv: prologue/epilogue not supported");
     const int smem = smem_b(a.K, a.batch);

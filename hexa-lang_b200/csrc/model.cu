@@ -670,7 +670,7 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
     }
     h->counters = (uint32_t*)h->alloc(4 * (size_t)h->Bmax * h->Hkv);
     h->err = (uint32_t*)h->alloc(16);
-    if (h->q4 && h->Bmax > 4)
+    if (h->Bmax > 4)  // batched GEMV path (int4 above 4 sequences, bf16 above 8)
         h->bscratch = h->alloc((size_t)forge_gemv_b_scratch_bytes(std::max({h->d, h->qd, h->F})));
     size_t st = std::max({(size_t)h->nqkv * d, (size_t)2 * h->F * d, (size_t)d * h->F, (size_t)d * h->qd,
                           (size_t)h->Vpad * d});
@@ -982,7 +982,7 @@ FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
     const bool split = h->split_for(batch);
     auto launches = [&](int K) { return forge_gemv_launch_count(K, batch, split, h->q4, h->bscratch != nullptr); };
     int per_layer = launches(h->d) * 2 + launches(h->qd) + launches(h->F) + 1;
-    return 1 + h->L * per_layer + forge_gemv_launch_count(h->d, batch, split, false, false) + 1;
+    return 1 + h->L * per_layer + forge_gemv_launch_count(h->d, batch, split, false, h->bscratch != nullptr) + 1;
 }
 int64_t forge_b200_width(const ForgeB200* h, int which) {
     if (!h) return 0;

@@ -155,3 +155,29 @@ def test_gemv_int4_batched_bit_identical(forge, oracle, cuda, N, K, batch):
     torch.cuda.synchronize()
     forge.check(lib.forge_ops_check(), "error word")
     assert torch.equal(yb.view(torch.int32), ys.view(torch.int32))
+
+
+@pytest.mark.parametrize("N,K", [(2048, 2048), (32000, 2048), (8192, 688)])
+@pytest.mark.parametrize("batch", [9, 16, 32, 33])
+def test_gemv_bf16_batched_bit_identical(forge, oracle, cuda, N, K, batch):
+    """bf16 weights with bf16 activations above 8 sequences: one weight stream
+    per 32 sequences, the same bits as the small-batch path on slices of 8."""
+    import torch
+    if K % 16:
+        pytest.skip("shape")
+    rng = np.random.default_rng(N + K + batch)
+    w = oracle.fill_normal_bf16(N * K, 4, N + 7 * K, 0.02).reshape(N, K)
+    X = rng.standard_normal((batch, K)).astype(np.float32)
+    tiles = forge.bf16_pack(_dev_bf16(torch, w, cuda))
+    xd = torch.from_numpy(X).to(cuda)
+    lib = forge.lib()
+    yb = torch.full((batch, N), float("nan"), device=cuda)
+    forge.check(lib.forge_gemv_bf16(tiles.data_ptr(), N, K, xd.data_ptr(), batch, yb.data_ptr(), 0, 0), "batched")
+    ys = torch.full((batch, N), float("nan"), device=cuda)
+    for b0 in range(0, batch, 8):
+        nb = min(8, batch - b0)
+        forge.check(lib.forge_gemv_bf16(tiles.data_ptr(), N, K, xd[b0:].data_ptr(), nb, ys[b0:].data_ptr(), 0, 0),
+                    "grouped")
+    torch.cuda.synchronize()
+    forge.check(lib.forge_ops_check(), "error word")
+    assert torch.equal(yb.view(torch.int32), ys.view(torch.int32))
