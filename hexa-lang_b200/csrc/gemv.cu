@@ -334,7 +334,7 @@ int forge_gemv_launch_count(int K, int batch, bool split, bool q4, bool batched)
     int max_cols = (kMaxSmem - kFixedSmem - (q4 ? (K / 128) * 48 : 0)) / row;
     if (max_cols > 8) max_cols = 8;
     const int per = max_cols / ((split || q4) ? 2 : 1);
-    if (batched && batch > per && (q4 || !split)) return 2 * ((batch + forge_gemv_b_max_seq() - 1) / forge_gemv_b_max_seq());
+    if (batched && batch > 4 && (q4 || !split)) return 2 * ((batch + forge_gemv_b_max_seq() - 1) / forge_gemv_b_max_seq());
     return per > 0 ? (batch + per - 1) / per : 0;
 }
 
@@ -359,7 +359,9 @@ int forge_gemv_launch(const ForgeGemvArgs& a0, cudaStream_t stream, bool pdl) {
     const int per_launch = max_cols / cols_per_seq;
     if (per_launch < 1) return forge_fail(-1, "gemv: K=%d too large for the staged activation", a0.K);
     const bool batched_ok = q4 ? (a0.epi != FORGE_EPI_LOGITS) : !a0.split;
-    if (a0.batch > per_launch && a0.bscratch && a0.pro != FORGE_PRO_EMBED_RMSNORM && batched_ok) {
+    // above 4 sequences (int4: more than one launch's worth; bf16: bf16
+    // activations, where one CTA per sequence stages in parallel)
+    if (a0.batch > 4 && a0.bscratch && a0.pro != FORGE_PRO_EMBED_RMSNORM && batched_ok) {
         // larger batches: one weight stream per forge_gemv_b_max_seq() sequences
         const int mx = forge_gemv_b_max_seq();
         for (int b0 = 0; b0 < a0.batch; b0 += mx) {

@@ -40,7 +40,7 @@ int gemv_entry(int wkind, const void* tiles, const void* stiles, int64_t N, int6
     a.w = tiles; a.s = stiles; a.N = (int32_t)N; a.K = (int32_t)K; a.wkind = wkind;
     a.batch = batch; a.split = exact ? 1 : 0; a.x = x; a.x_stride = (int32_t)K;
     a.pro = FORGE_PRO_PLAIN; a.epi = FORGE_EPI_STORE; a.y = y; a.y_stride = (int32_t)N; a.err = err;
-    if ((wkind == FORGE_W_Q4 && batch > 4) || (wkind == FORGE_W_BF16 && !exact && batch > 8)) {
+    if (batch > 4 && (wkind == FORGE_W_Q4 || !exact)) {
         // batched path: library-owned activation scratch, grown on demand
         static std::mutex mu;
         static void* buf[64] = {nullptr};

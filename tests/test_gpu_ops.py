@@ -158,10 +158,10 @@ def test_gemv_int4_batched_bit_identical(forge, oracle, cuda, N, K, batch):
 
 
 @pytest.mark.parametrize("N,K", [(2048, 2048), (32000, 2048), (8192, 688)])
-@pytest.mark.parametrize("batch", [9, 16, 32, 33])
+@pytest.mark.parametrize("batch", [5, 9, 16, 32, 33])
 def test_gemv_bf16_batched_bit_identical(forge, oracle, cuda, N, K, batch):
-    """bf16 weights with bf16 activations above 8 sequences: one weight stream
-    per 32 sequences, the same bits as the small-batch path on slices of 8."""
+    """bf16 weights with bf16 activations above 4 sequences: one weight stream
+    per 32 sequences, the same bits as the small-batch path on slices of 4."""
     import torch
     if K % 16:
         pytest.skip("shape")
@@ -174,8 +174,8 @@ def test_gemv_bf16_batched_bit_identical(forge, oracle, cuda, N, K, batch):
     yb = torch.full((batch, N), float("nan"), device=cuda)
     forge.check(lib.forge_gemv_bf16(tiles.data_ptr(), N, K, xd.data_ptr(), batch, yb.data_ptr(), 0, 0), "batched")
     ys = torch.full((batch, N), float("nan"), device=cuda)
-    for b0 in range(0, batch, 8):
-        nb = min(8, batch - b0)
+    for b0 in range(0, batch, 4):
+        nb = min(4, batch - b0)
         forge.check(lib.forge_gemv_bf16(tiles.data_ptr(), N, K, xd[b0:].data_ptr(), nb, ys[b0:].data_ptr(), 0, 0),
                     "grouped")
     torch.cuda.synchronize()
