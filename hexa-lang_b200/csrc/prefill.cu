@@ -10,8 +10,9 @@
 //
 // One CTA owns two tiles of 128 query rows of one (batch, head) and walks the
 // key blocks of 128 up to the diagonal (k_flash_prefill_pp below):
-//   warp 8             TMA: Q of both tiles once, K through a 2-stage ring, V
-//                      through one buffer (128-byte swizzled 64 x 128 boxes);
+//   warp 8             TMA: Q of both tiles once, then K and V of every key
+//                      block through a 4-slot ring (128-byte swizzled 64 x
+//                      128 boxes);
 //   warp 9 (one lane)  tensor-core issue: S = Q K^T and O += P V per tile
 //                      (tcgen05.mma kind::f16, M 128, N 128, 8 x K16 steps),
 //                      alternating tiles so one tile's MMAs overlap the other
@@ -20,8 +21,8 @@
 //                      of TMEM (tcgen05.ld), online max / sum in fp32 with
 //                      exp2 (the scale folded in), O rescaled in TMEM only
 //                      when the row max grows by more than 2^8, P written as
-//                      bf16 into shared memory in the swizzled K-major layout
-//                      TMA gives Q and K, and finally O / l to global memory.
+//                      bf16 pairs into TMEM over S (the A operand of O += P V),
+//                      and finally O / l to global memory.
 // Every wait is bounded (error word, then the CTA drains its copies and
 // tensor-core work and frees its TMEM).
 #include <cstring>
@@ -54,6 +55,27 @@ __device__ __forceinline__ float ex2_approx(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+// Packed fp32 pairs (low = first) and the sm_100 two-lane fp32 instructions.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
 // Two floats to packed bf16x2 (round to nearest even), first in the low half.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     uint32_t r;
@@ -61,22 +83,25 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return r;
 }
 
-// Byte offset of the 16-byte chunk c (columns 8c..8c+7) of row r inside a
-// 128x128 bf16 tile stored as two 128-byte-swizzled halves (the layout a
-// TMA box of 64 x 128 with 128-byte swizzle writes).
-__device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
-    return (uint32_t)((c >> 3) * kHalf + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
 // ---- two query tiles per CTA -------------------------------------------------------
 // Tiles A (rows 256p .. +127) and B (rows 256p+128 .. +255) share every K/V
 // block (loaded once) and alternate on the tensor core: while the softmax
 // warpgroup of one tile works on its S, the MMA warp runs the other tile's
 // S = QK^T or O += PV. TMEM holds S_A, O_A, S_B, O_B (512 columns); the softmax
-// reads each S row twice (max, then exp) so no thread holds a whole row.
-// Shared memory: Q_A Q_B | K ring of 2 | V (one buffer) | P_A P_B.
+// reads each S row twice (max, then exp) so no thread holds a whole row, and
+// writes P as packed bf16 over the S columns it has read (P of a tile takes
+// 64 columns), where the PV MMA takes it as its A operand. S of the next
+// block overwrites P only after that MMA: tcgen05 MMAs of one thread run in
+// issue order.
+// Shared memory: Q_A Q_B | a ring of kPStages 32 KB slots carrying K0 V0 K1
+// V1 ... in the order the MMAs use them, so the next block's V and K load
+// while the current block is in flight.
 constexpr int kPThreads = 320;            // warps 0-3 softmax A, 4-7 softmax B, 8 TMA, 9 MMA
-constexpr int kPOffQ = 0, kPOffK = 2 * kTile, kPOffV = 4 * kTile, kPOffP = 5 * kTile, kPOffBar = 7 * kTile;
+#ifndef FORGE_PREFILL_STAGES
+#define FORGE_PREFILL_STAGES 4
+#endif
+constexpr int kPStages = FORGE_PREFILL_STAGES;  // K/V ring slots (4 or 5 fit)
+constexpr int kPOffQ = 0, kPOffKV = 2 * kTile, kPOffBar = (2 + kPStages) * kTile;
 constexpr int kPSmem = kPOffBar + 256 + 1024;
 constexpr uint32_t kPTmemCols = 512;
 
@@ -89,15 +114,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const uint32_t sbase = smem_u32(base);
     uint64_t* bars = reinterpret_cast<uint64_t*>(base + kPOffBar);
     uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;    // [2]
-    uint64_t* k_empty = bars + 3;   // [2]
-    uint64_t* v_full = bars + 5;
-    uint64_t* v_empty = bars + 6;
-    uint64_t* s_full = bars + 7;    // [2] per tile
-    uint64_t* p_full = bars + 9;    // [2]
-    uint64_t* o_done = bars + 11;   // [2]
-    uint64_t* drain = bars + 13;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 14);
+    uint64_t* s_full = bars + 1;    // [2] per tile
+    uint64_t* p_full = bars + 3;    // [2]
+    uint64_t* o_done = bars + 5;    // [2]
+    uint64_t* drain = bars + 7;
+    uint64_t* kv_full = bars + 8;   // [kPStages]
+    uint64_t* kv_empty = bars + 8 + kPStages;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 8 + 2 * kPStages);
 
     __shared__ uint32_t s_abort;
     if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile uint32_t*>(a.err);
@@ -120,14 +143,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&k_full[i], 1);
-            mbar_init(&k_empty[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], 128);
             mbar_init(&o_done[i], 1);
         }
-        mbar_init(v_full, 1);
-        mbar_init(v_empty, 1);
+        for (int i = 0; i < kPStages; ++i) {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+        }
         mbar_init(drain, 1);
         fence_mbar_init();
     }
@@ -150,36 +173,35 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 tma_load_2d(base + kPOffQ + kTile, &tq, 0, row0 + tB * kBM, q_full);
                 tma_load_2d(base + kPOffQ + kTile + kHalf, &tq, 64, row0 + tB * kBM, q_full);
             }
+            // item i of the ring: block i / 2, K when i is even, V when odd
+            const int nitem = 2 * nblk;
             int issued = 0;
-            for (int j = 0; j < nblk; ++j) {
-                const int st = j & 1;
-                if (!mbar_wait(&k_empty[st], ((j >> 1) & 1) ^ 1, a.err)) break;
-                uint8_t* kd = base + kPOffK + st * kTile;
-                mbar_arrive_expect_tx(&k_full[st], kTile);
-                tma_load_2d(kd, &tk, 0, row0 + j * kBN, &k_full[st]);
-                tma_load_2d(kd + kHalf, &tk, 64, row0 + j * kBN, &k_full[st]);
-                issued = j + 1;
+            for (int it = 0; it < nitem; ++it) {
+                const int st = it % kPStages;
+                if (!mbar_wait(&kv_empty[st], ((it / kPStages) & 1) ^ 1, a.err)) break;
+                uint8_t* dst = base + kPOffKV + st * kTile;
+                const CUtensorMap* map = (it & 1) ? &tv : &tk;
+                const int y = row0 + (it >> 1) * kBN;
+                mbar_arrive_expect_tx(&kv_full[st], kTile);
+                tma_load_2d(dst, map, 0, y, &kv_full[st]);
+                tma_load_2d(dst + kHalf, map, 64, y, &kv_full[st]);
+                issued = it + 1;
             }
+            // every copy issued has landed before the CTA may exit
             mbar_wait(q_full, 0, a.err);
-            for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.err);
-        } else if (lane == 1) {
-            // the single V buffer: block j once both tiles' PV of block j-1 are done
-            int issued = 0;
-            for (int j = 0; j < nblk; ++j) {
-                if (!mbar_wait(v_empty, (j & 1) ^ 1, a.err)) break;
-                mbar_arrive_expect_tx(v_full, kTile);
-                tma_load_2d(base + kPOffV, &tv, 0, row0 + j * kBN, v_full);
-                tma_load_2d(base + kPOffV + kHalf, &tv, 64, row0 + j * kBN, v_full);
-                issued = j + 1;
-            }
-            if (issued) mbar_wait(v_full, (issued - 1) & 1, a.err);
+            for (int it = issued > kPStages ? issued - kPStages : 0; it < issued; ++it)
+                mbar_wait(&kv_full[it % kPStages], (it / kPStages) & 1, a.err);
         }
     } else if (warp == 9) {
         // ------------------------------------------------------ tensor cores
         if (lane == 0) {
             bool ok = mbar_wait(q_full, 0, a.err);
+            auto slot_addr = [&](int it) { return sbase + (uint32_t)(kPOffKV + (it % kPStages) * kTile); };
+            auto wait_item = [&](int it) {
+                return mbar_wait(&kv_full[it % kPStages], (it / kPStages) & 1, a.err);
+            };
             auto issue_s = [&](int t, int j) {
-                const uint32_t kb = sbase + (uint32_t)(kPOffK + (j & 1) * kTile);
+                const uint32_t kb = slot_addr(2 * j);
                 const uint32_t qb = sbase + (uint32_t)(kPOffQ + t * kTile);
 #pragma unroll
                 for (int s = 0; s < kHD / 16; ++s) {
@@ -189,30 +211,27 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 }
                 umma_commit(&s_full[t]);
             };
+            // O += P V: P (A operand) from TMEM over S, 8 columns per K16 step
             auto issue_pv = [&](int t, int j) {
-                const uint32_t vb = sbase + kPOffV;
-                const uint32_t pb = sbase + (uint32_t)(kPOffP + t * kTile);
+                const uint32_t vb = slot_addr(2 * j + 1);
 #pragma unroll
-                for (int s = 0; s < kBN / 16; ++s) {
-                    const uint32_t aoff = (uint32_t)((s >> 2) * kHalf + (s & 3) * 32);
-                    umma_bf16(tO[t], umma_desc_sw128(pb + aoff, 16, 1024),
-                              umma_desc_sw128(vb + (uint32_t)s * 2048u, kHalf, 1024), kIdescO,
-                              (j > 0 || s > 0) ? 1u : 0u);
-                }
+                for (int s = 0; s < kBN / 16; ++s)
+                    umma_bf16_ta(tO[t], tS[t] + (uint32_t)(8 * s), umma_desc_sw128(vb + (uint32_t)s * 2048u, kHalf, 1024),
+                                 kIdescO, (j > 0 || s > 0) ? 1u : 0u);
                 umma_commit(&o_done[t]);
             };
             // block 0: S of both tiles
-            if (ok && mbar_wait(&k_full[0], 0, a.err)) {
+            if (ok && wait_item(0)) {
                 tc_fence_after();
                 issue_s(0, 0);
                 if (nB > 0) issue_s(1, 0);
-                umma_commit(&k_empty[0]);
+                umma_commit(&kv_empty[0]);
             } else {
                 ok = false;
             }
             for (int j = 0; j < nblk && ok; ++j) {
                 const bool useA = j < nA, useB = j < nB;
-                if (!mbar_wait(v_full, j & 1, a.err)) break;
+                if (!wait_item(2 * j + 1)) break;
                 if (useA) {
                     if (!mbar_wait(&p_full[0], j & 1, a.err)) break;
                     tc_fence_after();
@@ -221,7 +240,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 // tile A's next S overlaps tile B's softmax of this block
                 const bool nextA = j + 1 < nA, nextB = j + 1 < nB;
                 if (nextA || nextB) {
-                    if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, a.err)) break;
+                    if (!wait_item(2 * j + 2)) break;
                     tc_fence_after();
                     if (nextA) issue_s(0, j + 1);
                 }
@@ -230,9 +249,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     tc_fence_after();
                     issue_pv(1, j);
                 }
-                umma_commit(v_empty);
+                umma_commit(&kv_empty[(2 * j + 1) % kPStages]);
                 if (nextB) issue_s(1, j + 1);
-                if (nextA || nextB) umma_commit(&k_empty[(j + 1) & 1]);
+                if (nextA || nextB) umma_commit(&kv_empty[(2 * j + 2) % kPStages]);
             }
             umma_commit(drain);
             mbar_wait(drain, 0, a.err);
@@ -240,6 +259,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     } else {
         // ------------------------------------------------------------ softmax
         const int t = warp >> 2;                // tile 0 (A) or 1 (B)
+        const uint32_t tSm = tmem + (t ? 256u : 0u), tOm = tSm + 128u;  // this tile's S / O columns
         const int r = threadIdx.x & 127;        // query row within the tile
         const int qt = t ? tB : tA;
         const int nmine = t ? nB : nA;
@@ -251,32 +271,35 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // always refer to the same m, so the result does not change.
         float m = -INFINITY, l = 0.f;
         bool ok = nmine > 0;
-        uint8_t* P = base + kPOffP + t * kTile;
         for (int j = 0; j < nmine; ++j) {
             if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, a.err))) { ok = false; break; }
             tc_fence_after();
             const bool diag = a.causal && j == qt;
-            // pass 1: row max (two TMEM loads in flight per wait)
-            float mx = -INFINITY;
+            // pass 1: row max (two TMEM loads in flight per wait; four
+            // independent max chains)
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int q = 0; q < 4; q += 2) {
                 uint32_t sv[2][32];
-                tmem_ld32(tS[t] + lrow + 32 * q, sv[0]);
-                tmem_ld32(tS[t] + lrow + 32 * (q + 1), sv[1]);
+                tmem_ld32(tSm + lrow + 32 * q, sv[0]);
+                tmem_ld32(tSm + lrow + 32 * (q + 1), sv[1]);
                 tmem_wait_ld();
                 if (diag) {
 #pragma unroll
                     for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
-                            if (32 * (q + h2) + i <= r) mx = fmaxf(mx, __uint_as_float(sv[h2][i]));
+                            if (32 * (q + h2) + i <= r) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[h2][i]));
                 } else {
 #pragma unroll
                     for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sv[h2][i]));
+                        for (int i = 0; i < 32; i += 2)
+                            mx4[(i >> 1) & 3] = max3f(mx4[(i >> 1) & 3], __uint_as_float(sv[h2][i]),
+                                                      __uint_as_float(sv[h2][i + 1]));
                 }
             }
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             const float mxc = mx * c;
             const bool raise = mxc > m + 8.0f;
             const float m_new = raise ? mxc : m;
@@ -288,48 +311,47 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         uint32_t ov[32];
-                        tmem_ld32(tO[t] + lrow + 32 * q, ov);
+                        tmem_ld32(tOm + lrow + 32 * q, ov);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                        tmem_st32(tO[t] + lrow + 32 * q, ov);
+                        tmem_st32(tOm + lrow + 32 * q, ov);
                     }
                 }
             }
-            // pass 2: P = exp2(S * c - m) as bf16 into shared memory; the
+            // pass 2: P = exp2(S * c - m) as bf16 pairs into TMEM over the S
+            // columns already read (64 S columns in, 32 P columns out); the
             // causal mask only matters on the diagonal block
-            float sum = 0.f;
+            uint64_t sum2 = 0;  // two partial row sums (packed)
+            const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(-m_new, -m_new);
 #pragma unroll
             for (int q = 0; q < 4; q += 2) {
                 uint32_t sv[2][32];
-                tmem_ld32(tS[t] + lrow + 32 * q, sv[0]);
-                tmem_ld32(tS[t] + lrow + 32 * (q + 1), sv[1]);
+                tmem_ld32(tSm + lrow + 32 * q, sv[0]);
+                tmem_ld32(tSm + lrow + 32 * (q + 1), sv[1]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2)
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    uint32_t pk[16];
 #pragma unroll
-                    for (int ch = 0; ch < 4; ++ch) {
-                        uint32_t pk[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int i = ch * 8 + 2 * e, col = 32 * (q + h2) + i;
-                            float p0 = ex2_approx(fmaf(__uint_as_float(sv[h2][i]), c, -m_new));
-                            float p1 = ex2_approx(fmaf(__uint_as_float(sv[h2][i + 1]), c, -m_new));
-                            if (diag) {
-                                p0 = col > r ? 0.f : p0;
-                                p1 = col + 1 > r ? 0.f : p1;
-                            }
-                            sum += p0 + p1;
-                            pk[e] = pack_bf16x2(p0, p1);
+                    for (int e = 0; e < 16; ++e) {
+                        const int i = 2 * e, col = 32 * (q + h2) + i;
+                        const uint64_t x =
+                            f2_fma(f2_pack(__uint_as_float(sv[h2][i]), __uint_as_float(sv[h2][i + 1])), c2, nm2);
+                        float p0 = ex2_approx(f2_lo(x)), p1 = ex2_approx(f2_hi(x));
+                        if (diag) {
+                            p0 = col > r ? 0.f : p0;
+                            p1 = col + 1 > r ? 0.f : p1;
                         }
-                        *reinterpret_cast<uint4*>(P + sw128_chunk(r, 4 * (q + h2) + ch)) =
-                            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        sum2 = f2_add(sum2, f2_pack(p0, p1));
+                        pk[e] = pack_bf16x2(p0, p1);
                     }
+                    tmem_st16(tSm + lrow + (uint32_t)(16 * (q + h2)), pk);
+                }
             }
-            l = l * alpha + sum;
+            l = l * alpha + (f2_lo(sum2) + f2_hi(sum2));
             m = m_new;
             tmem_wait_st();
-            fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&p_full[t]);
         }
@@ -340,7 +362,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 uint32_t ov[32];
-                tmem_ld32(tO[t] + lrow + 32 * q, ov);
+                tmem_ld32(tOm + lrow + 32 * q, ov);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i += 8) {
