@@ -313,21 +313,23 @@ int forge_attn_configure() {
 }
 
 int forge_attn_pick_splits(int B, int Hkv, int lmax) {
-    // Splits per (sequence, kv head): the count whose CTAs fill whole waves of
-    // the resident slots (3 per SM of a 148-SM B200 at ~65 KB of shared
-    // memory each) best, each extra wave costing 0.1 of efficiency: short
-    // decode attention loses most to a partly filled last wave. Fixed so
-    // workspace sizes do not depend on which device is current.
+    // Splits per (sequence, kv head) minimising waves x (fixed cost + key
+    // tiles per split): every CTA of a wave of the resident slots (3 per SM
+    // of a 148-SM B200 at ~65 KB of shared memory each) runs about as long
+    // as its tile count plus a fixed ~2 tiles (ramp, partial write and
+    // merge), so a partly filled last wave costs as much as a full one.
+    // Fixed so workspace sizes do not depend on which device is current.
     const int resident = 3 * 148;
     const int pairs = B * Hkv;
     const int cap = (lmax + 127) / 128;  // at least ~128 keys per split at full context
     int best = 1;
-    double best_score = -1e9;
+    long long best_cost = -1;
     for (int ns = 1; ns <= cap; ++ns) {
-        const int items = pairs * ns;
-        const int waves = (items + resident - 1) / resident;
-        const double score = (double)items / ((double)waves * resident) - 0.1 * waves;
-        if (score > best_score + 1e-9) { best_score = score; best = ns; }
+        const long long items = (long long)pairs * ns;
+        const long long waves = (items + resident - 1) / resident;
+        const int tiles = ((lmax + ns - 1) / ns + kTile - 1) / kTile;
+        const long long cost = waves * (2 + tiles);
+        if (best_cost < 0 || cost <= best_cost) { best_cost = cost; best = ns; }  // ties: more splits
     }
     return best;
 }
