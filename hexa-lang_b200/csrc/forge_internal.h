@@ -1,5 +1,6 @@
 // forge_internal.h — shared host-side declarations of the forge_b200 library.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -75,6 +76,18 @@ int forge_gemv_b_max_seq();
 int64_t forge_gemv_b_scratch_bytes(int K);
 int forge_gemv_b_configure();
 int forge_gemv_b_launch(const ForgeGemvArgs& a, void* scratch, cudaStream_t stream, bool pdl);
+// int4 chunks of the batched path on the tensor cores (gemv_tc.cu); the
+// scratch must start zeroed (ticket counters) and is kept so by the kernel.
+int64_t forge_gemv_tc_scratch_bytes(int K);
+int64_t forge_gemv_scratch_header();
+// cuTensorMapEncodeTiled through the runtime's driver entry point (NULL if
+// unavailable); prefill.cu.
+using ForgeEncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+ForgeEncodeTiled forge_tensor_map_encoder();  // bytes at the start of the scratch the other batched paths skip
+int forge_gemv_tc_configure();
+int forge_gemv_tc_launch(const ForgeGemvArgs& a, void* scratch, cudaStream_t stream, bool pdl);
 
 // ------------------------------------------------------ flash-decode launch
 struct ForgeAttnArgs {

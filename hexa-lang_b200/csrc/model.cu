@@ -670,8 +670,11 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
     }
     h->counters = (uint32_t*)h->alloc(4 * (size_t)h->Bmax * h->Hkv);
     h->err = (uint32_t*)h->alloc(16);
-    if (h->Bmax > 4)  // batched GEMV path (int4 above 4 sequences, bf16 above 8)
-        h->bscratch = h->alloc((size_t)forge_gemv_b_scratch_bytes(std::max({h->d, h->qd, h->F})));
+    if (h->Bmax > 4) {  // batched GEMV path (int4 above 4 sequences, bf16 above 8); starts zeroed
+        const size_t nb = (size_t)forge_gemv_b_scratch_bytes(std::max({h->d, h->qd, h->F}));
+        h->bscratch = h->alloc(nb);
+        if (h->bscratch && cudaMemset(h->bscratch, 0, nb) != cudaSuccess) h->bscratch = nullptr;
+    }
     size_t st = std::max({(size_t)h->nqkv * d, (size_t)2 * h->F * d, (size_t)d * h->F, (size_t)d * h->qd,
                           (size_t)h->Vpad * d});
     h->stA = (uint16_t*)h->alloc(st * 2);

@@ -57,8 +57,10 @@ int gemv_entry(int wkind, const void* tiles, const void* stiles, int64_t N, int6
             }
             buf[dev] = nullptr;
             cap[dev] = 0;
-            if (cudaMalloc(&buf[dev], (size_t)need) != cudaSuccess) {
+            if (cudaMalloc(&buf[dev], (size_t)need) != cudaSuccess || cudaMemset(buf[dev], 0, (size_t)need) != cudaSuccess) {
                 cudaGetLastError();
+                if (buf[dev]) cudaFree(buf[dev]);
+                buf[dev] = nullptr;
                 return forge_fail(-1, "forge_gemv: batched scratch of %lld bytes", (long long)need);
             }
             cap[dev] = need;

@@ -120,7 +120,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     uint64_t* drain = bars + 7;
     uint64_t* kv_full = bars + 8;   // [kPStages]
     uint64_t* kv_empty = bars + 8 + kPStages;
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 8 + 2 * kPStages);
+    uint64_t* done = bars + 8 + 2 * kPStages;   // every warp finished (one arrival per warp)
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
 
     __shared__ uint32_t s_abort;
     if (threadIdx.x == 0) s_abort = *reinterpret_cast<volatile uint32_t*>(a.err);
@@ -152,6 +153,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             mbar_init(&kv_empty[i], 1);
         }
         mbar_init(drain, 1);
+        mbar_init(done, kPThreads / 32);
         fence_mbar_init();
     }
     if (warp == 9) tmem_alloc(tslot, kPTmemCols);
@@ -376,35 +378,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
         }
     }
+    // End: every warp reports on an mbarrier and the TMEM-owning warp waits
+    // for all of them before it frees TMEM (after the single-lane TMA and MMA
+    // roles a CTA-wide bar.sync is not relied on to hold the other warps).
     tc_fence_before();
-    __syncthreads();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(done);
     if (warp == 9) {
+        mbar_wait(done, 0, a.err);
+        __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, kPTmemCols);
     }
 }
 
 // ---- host ------------------------------------------------------------------------
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn() {
-    static EncodeTiled fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiled>(p);
-    });
-    return fn;
-}
-
 // [rows][128] bf16 viewed as 64-column x 128-row boxes, 128-byte swizzle.
 int make_map(CUtensorMap* m, const void* ptr, int64_t rows) {
-    EncodeTiled enc = encode_fn();
+    ForgeEncodeTiled enc = forge_tensor_map_encoder();
     if (!enc) return forge_fail(-1, "flash prefill: cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {(cuuint64_t)kHD, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)kHD * 2};
@@ -429,6 +420,21 @@ int configure() {
     return 0;
 }
 }  // namespace
+
+// cuTensorMapEncodeTiled from the driver (through the runtime, no -lcuda).
+ForgeEncodeTiled forge_tensor_map_encoder() {
+    static ForgeEncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<ForgeEncodeTiled>(p);
+    });
+    return fn;
+}
+
 
 extern "C" FORGE_API int forge_flash_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o,
                                              int B, int H, int S, int hd, int causal, void* stream) {
