@@ -160,6 +160,10 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
     const int P = gridDim.x;
     const int64_t u0 = unit_begin(blockIdx.x, U, P), u1 = unit_begin(blockIdx.x + 1, U, P);
     const int nmine = (int)(u1 - u0);
+    // (tile, group) of the first unit; later units step through them
+    // incrementally (a 64-bit division per unit and thread kept the
+    // conversion unit ~50% busy in an earlier version)
+    const int tl0 = (int)(u0 / G), g0 = (int)(u0 - (int64_t)tl0 * G);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNS; ++i) {
@@ -194,14 +198,13 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
             // scales: box {16 x 8 B, 8 blocks} at (16 (g / 4), 8 tile). Rows
             // past N read as zeros and count in full.
             auto weights = [&](int i) {
-                const int64_t u = u0 + i;
-                const int tl = (int)(u / G), g = (int)(u % G);
+                const int gi = g0 + i, tl = tl0 + gi / G, g = gi - (gi / G) * G;
                 uint8_t* slot = base + (i % kNS) * kSlot;
                 tma_load_2d(slot + kSlotW, &tw, 128 * g, 8 * tl, &raw_full[i % kNS]);
                 tma_load_2d(slot + kSlotS, &ts, 16 * (g >> 2), 8 * tl, &raw_full[i % kNS]);
             };
             auto acts = [&](int i) {
-                const int g = (int)((u0 + i) % G);
+                const int gi = g0 + i, g = gi - (gi / G) * G;
                 uint8_t* slot = base + (i % kNS) * kSlot;
                 bulk_g2s(slot + kSlotAct, t.xt + (size_t)g * kActGroup, kActGroup, &raw_full[i % kNS]);
             };
@@ -304,13 +307,13 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
         float y[kHalfSeq];
 #pragma unroll
         for (int b = 0; b < kHalfSeq; ++b) y[b] = 0.f;
-        int piece_g0 = (int)(u0 % G);
+        int piece_g0 = g0;
         // A wait that runs out sets the error word; the warp then stops
         // working but still takes the piece-end barriers with the others.
         bool ok = true;
+        int tl = tl0, g = g0 - 1;
         for (int i = 0; i < nmine; ++i) {
-            const int64_t u = u0 + i;
-            const int tl = (int)(u / G), g = (int)(u % G);
+            if (++g == G) { g = 0; ++tl; }
             const int s = i % kNS, tb = i % kNAcc;
             if (ok) {
                 const bool w1 = mbar_wait(&acc_full[tb], (i / kNAcc) & 1, a.err) &&
@@ -368,7 +371,7 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
                 const bool whole = piece_g0 == 0 && g == G - 1;
                 bool fin = whole && ok;
                 if (!whole) {
-                    const int k = (u0 / G == tl) ? 0 : 1;  // first or last piece of this CTA
+                    const int k = (tl0 == tl) ? 0 : 1;  // first or last piece of this CTA
                     // 16 floats per thread (columns past the batch carry
                     // values that are never stored)
                     float4* pp = reinterpret_cast<float4*>(t.partial + (((size_t)blockIdx.x * 2 + k) * kTM + row) * kMaxSeq +
