@@ -126,10 +126,12 @@ def barrier(pg):
         pg.barrier()
 
 
-def time_dominant_gemv(fb, torch, dev, K=4096, N=2 * 11008, copies=4, reps=20):
-    """The 7B gate/up int4 GEMV (N=22016, K=4096) via the per-op C-ABI entry,
-    rotating over `copies` weight sets (copies x 45 MB > L2) so every launch
-    streams from HBM. Returns (avg ms per launch, algorithmic bytes)."""
+def time_dominant_gemv(fb, torch, dev, K=4096, N=2 * 11008, copies=4, reps=20, batch=1):
+    """The 7B gate/up int4 GEMV (N=22016, K=4096) via the per-op C-ABI entry
+    for `batch` sequences (above 4: the batched paths, whose call includes the
+    activation-quantising launch), rotating over `copies` weight sets
+    (copies x 45 MB > L2) so every launch streams from HBM. Returns (avg ms
+    per call, algorithmic bytes)."""
     lib = fb.lib()
     ws = []
     for c in range(copies):
@@ -137,22 +139,23 @@ def time_dominant_gemv(fb, torch, dev, K=4096, N=2 * 11008, copies=4, reps=20):
         fb.check(lib.forge_fill_normal_bf16(w.data_ptr(), N * K, 77, c << 40, 0.02, 0), "fill")
         ws.append(fb.q4_pack(w)[2:])
         del w
-    x = torch.randn(1, K, device=dev)
-    y = torch.empty(1, N, device=dev)
+    x = torch.randn(batch, K, device=dev)
+    y = torch.empty(batch, N, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
     for i in range(6):
         t, s = ws[i % copies]
-        fb.check(lib.forge_gemv_w4a16_g128(t.data_ptr(), s.data_ptr(), N, K, x.data_ptr(), 1, y.data_ptr(), 1, stream), "gemv")
+        fb.check(lib.forge_gemv_w4a16_g128(t.data_ptr(), s.data_ptr(), N, K, x.data_ptr(), batch, y.data_ptr(), 1,
+                                           stream), "gemv")
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(reps):
         t, s = ws[i % copies]
-        lib.forge_gemv_w4a16_g128(t.data_ptr(), s.data_ptr(), N, K, x.data_ptr(), 1, y.data_ptr(), 1, stream)
+        lib.forge_gemv_w4a16_g128(t.data_ptr(), s.data_ptr(), N, K, x.data_ptr(), batch, y.data_ptr(), 1, stream)
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    nbytes = lib.forge_q4_tile_bytes(N, K) + lib.forge_q4_scale_tile_bytes(N, K, 128) + 4 * K + 4 * N
+    nbytes = lib.forge_q4_tile_bytes(N, K) + lib.forge_q4_scale_tile_bytes(N, K, 128) + batch * (4 * K + 4 * N)
     return ms, nbytes
 
 
@@ -317,9 +320,11 @@ def main():
     dev = torch.device("cuda", local)
     if args.only_gemv:
         # the dominant kernel alone, for profiling: a few launches of the 7B
-        # gate/up int4 GEMV (22016 x 4096) over 4 weight copies (180 MB)
-        ms, nbytes = time_dominant_gemv(fb, torch, dev, reps=3)
-        print(json.dumps({"kernel": "k_gemv int4 22016x4096 bs1", "ms": ms, "bytes": nbytes}))
+        # gate/up int4 GEMV (22016 x 4096) over 4 weight copies (180 MB), for
+        # --batch sequences (32: the tensor-core path)
+        ms, nbytes = time_dominant_gemv(fb, torch, dev, reps=3 if args.batch == 1 else 20, batch=args.batch)
+        print(json.dumps({"kernel": f"int4 gemv 22016x4096 batch {args.batch}", "ms": ms, "bytes": nbytes,
+                          "gbs": nbytes / ms / 1e6}))
         return
     if args.only_prefill:
         print(json.dumps(time_prefill(fb, torch, dev, B=4, H=16, S=4096, reps=2)))
