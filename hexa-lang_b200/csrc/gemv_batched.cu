@@ -132,11 +132,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
     uint32_t it = 0;
     int slot = 0;
     bool ok = true;
+    // B fragments of this warp's two groups of piece i (they depend only on
+    // the group, so every unit walks the same pieces). Up to 8 sequences
+    // the next piece's are loaded from L2 before the current piece is
+    // waited for and computed, hiding the L2 latency that bound this loop.
+    auto load_b = [&](int i, uint4 (&bb)[2][NCB][2]) {
+        const int kt0 = i * kItemKT, ngl = min(kItemKT, KT - kt0) / 8;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int gl = 2 * warp + h;
+            if (gl < ngl) {
+                const uint4* xg = reinterpret_cast<const uint4*>(xq_g) + (size_t)(2 * (kt0 / 8 + gl)) * ncols * 4;
+#pragma unroll
+                for (int cb = 0; cb < NCB; ++cb) {
+                    const int col = min(cb * 8 + g, ncols - 1);
+                    bb[h][cb][0] = __ldg(xg + (size_t)col * 4 + t);
+                    bb[h][cb][1] = __ldg(xg + (size_t)(ncols + col) * 4 + t);
+                }
+            }
+        }
+    };
+    constexpr bool kPrefetch = NCB <= 2;
+    uint4 bcur[2][NCB][2], bnext[2][NCB][2];
+    if (kPrefetch) load_b(0, bcur);
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, slot ^= 1) {
         float totA[NCB][2], totB[NCB][2];
 #pragma unroll
         for (int c = 0; c < NCB; ++c) totA[c][0] = totA[c][1] = totB[c][0] = totB[c][1] = 0.f;
         for (int i = 0; i < nitems; ++i) {
+            if (kPrefetch) load_b(i + 1 < nitems ? i + 1 : 0, bnext);
             const int s = it % kStages;
             const uint32_t ph = (it / kStages) & 1u;
             if (!mbar_wait(&full[s], ph, a.err)) { ok = false; break; }
@@ -157,13 +181,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
                 dequant_q4_u8(w0.z, w0.w, af[1]);
                 dequant_q4_u8(w1.x, w1.y, af[2]);
                 dequant_q4_u8(w1.z, w1.w, af[3]);
-                const uint4* xg = reinterpret_cast<const uint4*>(xq_g) + (size_t)(2 * gg) * ncols * 4;
                 uint4 bf[NCB][2];
+                if (kPrefetch) {
 #pragma unroll
-                for (int cb = 0; cb < NCB; ++cb) {
-                    const int col = min(cb * 8 + g, ncols - 1);
-                    bf[cb][0] = __ldg(xg + (size_t)col * 4 + t);
-                    bf[cb][1] = __ldg(xg + (size_t)(ncols + col) * 4 + t);
+                    for (int cb = 0; cb < NCB; ++cb) {
+                        bf[cb][0] = bcur[h][cb][0];
+                        bf[cb][1] = bcur[h][cb][1];
+                    }
+                } else {
+                    const uint4* xg = reinterpret_cast<const uint4*>(xq_g) + (size_t)(2 * gg) * ncols * 4;
+#pragma unroll
+                    for (int cb = 0; cb < NCB; ++cb) {
+                        const int col = min(cb * 8 + g, ncols - 1);
+                        bf[cb][0] = __ldg(xg + (size_t)col * 4 + t);
+                        bf[cb][1] = __ldg(xg + (size_t)(ncols + col) * 4 + t);
+                    }
                 }
 #pragma unroll
                 for (int cb = 0; cb < NCB; ++cb) {
@@ -187,6 +219,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             ++it;
+            if (kPrefetch) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int cb = 0; cb < NCB; ++cb) {
+                        bcur[h][cb][0] = bnext[h][cb][0];
+                        bcur[h][cb][1] = bnext[h][cb][1];
+                    }
+            }
         }
         if (!ok) break;
         // cross-warp reduction: lane (g, t) holds rows g / g+8 of sequences 4cb + t
