@@ -26,6 +26,7 @@ enum {
     FORGE_EPI_QKV = 2,    // RoPE + KV append + q out
     FORGE_EPI_SWIGLU = 3, // s[b][f] = silu(gate) * up
     FORGE_EPI_LOGITS = 4, // logits + running argmax key
+    FORGE_EPI_RESID_TP = 5, // y[b][row] += sum over tensor-parallel ranks of W x (peer memory, batch <= 4)
 };
 
 struct ForgeGemvArgs {
@@ -62,6 +63,7 @@ struct ForgeGemvArgs {
     int32_t nvalid;        // rows >= nvalid (zero padding) never win the argmax
     int32_t row_off;       // global index of row 0 in the argmax key (vocabulary shard)
     void* bscratch;        // int4, batch > 4: forge_gemv_b_scratch_bytes(K) bytes for the batched path
+    const struct ForgeTpFusedDev* tpf;  // FORGE_EPI_RESID_TP: the ranks' exchange buffers (device memory)
     uint32_t* err;         // device error word
 };
 
@@ -162,6 +164,17 @@ int forge_tp_allgather_f32(void* comm, const float* send, float* recv, size_t co
 
 // One-shot all-reduce over NVLink peer memory (tp_allreduce.cu).
 struct ForgeTpAr;
+// Peer-memory exchange of the GEMV epilogue FORGE_EPI_RESID_TP (device
+// memory, one per rank): every rank's receive buffer [2 generations][T][cap]
+// floats and per-tile flags [2][T][max_tiles] mapped from all peers, and
+// this rank's per-tile call counters.
+struct ForgeTpFusedDev {
+    float* buf[8];
+    uint32_t* flag[8];
+    uint32_t* tile_epoch;  // [max_tiles], local
+    int T, rank, cap, max_tiles;
+};
+const ForgeTpFusedDev* forge_tp_fused_dev(const ForgeTpAr* ar);
 int forge_tp_ar_init(void* comm, int rank, int T, int cap, cudaStream_t stream, ForgeTpAr** out);
 void forge_tp_ar_destroy(ForgeTpAr* ar);
 int forge_tp_ar_capacity(const ForgeTpAr* ar);

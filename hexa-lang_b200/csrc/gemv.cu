@@ -54,6 +54,77 @@ constexpr int kMaxG = 128;                            // K <= 16384 (staging kee
 constexpr int kFixedSmem = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4;
 constexpr int kMaxSmem = 227 * 1024;
 
+__device__ __forceinline__ void sys_store_release(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t sys_load_acquire(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// FORGE_EPI_RESID_TP, run by warp 0 of the CTA that finished 16-row tile u
+// (lane (p, b) for p < 8 and b < batch <= 4 holds rows p / p+8 of sequence b):
+// the tile's share goes into this rank's slot on every rank (rank 0's share
+// carries the residual, the additions of its FORGE_EPI_RESID), a flag per
+// (rank, tile) on every rank says it landed, and once every rank's flag for
+// this tile is in, the slots are summed in rank order — the additions of
+// the separate all-reduce, so the result is the same — into the residual.
+// The per-tile call counter selects one of two buffer generations: a rank
+// can be at most one call ahead of another on a tile, because finishing a
+// tile waits for every rank's share of it. Waits are bounded (error word).
+__device__ __noinline__ void tp_resid_epilogue(const ForgeGemvArgs& a, int u, int p, int b, bool act, float ylo,
+                                               float yhi) {
+    const ForgeTpFusedDev& f = *a.tpf;
+    const int lane = threadIdx.x & 31;
+    const int T = f.T, rank = f.rank;
+    uint32_t ep = 0;
+    if (lane == 0) ep = ++f.tile_epoch[u];
+    ep = __shfl_sync(0xffffffffu, ep, 0);
+    const int gen = ep & 1;
+    const size_t i0 = (size_t)b * a.y_stride + (size_t)u * 16 + p, i1 = i0 + 8;
+    if (act) {
+        float v0 = ylo, v1 = yhi;
+        if (rank == 0) {
+            v0 = a.y[i0] + ylo;
+            v1 = a.y[i1] + yhi;
+        }
+        for (int r = 0; r < T; ++r) {
+            float* dst = f.buf[r] + ((size_t)gen * T + rank) * f.cap;
+            dst[i0] = v0;
+            dst[i1] = v1;
+        }
+        __threadfence_system();
+    }
+    __syncwarp();
+    if (lane < T) sys_store_release(f.flag[lane] + ((size_t)gen * T + rank) * f.max_tiles + u, ep);
+    bool ok = true;
+    if (lane < T) {
+        const volatile uint32_t* fl = f.flag[rank] + ((size_t)gen * T + lane) * f.max_tiles + u;
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t spins = 0;
+        while (*fl != ep) {
+            if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > FORGE_WAIT_NS) {
+                atomicOr(a.err, FORGE_DEVERR_COUNTER_TIMEOUT);
+                ok = false;
+                break;
+            }
+        }
+        (void)sys_load_acquire(const_cast<const uint32_t*>(fl));
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok && act) {
+        const float* base = f.buf[rank] + (size_t)gen * T * f.cap;
+        float s0 = __ldcv(base + i0), s1 = __ldcv(base + i1);
+        for (int r = 1; r < T; ++r) {
+            s0 += __ldcv(base + (size_t)r * f.cap + i0);
+            s1 += __ldcv(base + (size_t)r * f.cap + i1);
+        }
+        a.y[i0] = s0;
+        a.y[i1] = s1;
+    }
+}
+
 template <int WK, int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const ForgeGemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -224,11 +295,14 @@ __global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const 
         }
         named_bar_sync(1, 256);
         const int tid = threadIdx.x;
-        if (tid < 8 * a.batch) {
+        const bool act = tid < 8 * a.batch;
+        // FORGE_EPI_RESID_TP (batch <= 4): all of warp 0 takes part
+        if (act || (EPI == FORGE_EPI_RESID_TP && warp == 0)) {
             const int p = tid & 7, b = tid >> 3;
             const float* rs = red + slot * kConsumerWarps * 16 * RC;
             float ylo = 0.f, yhi = 0.f;
-            if (WK == FORGE_W_Q4) {
+            if (!act) {
+            } else if (WK == FORGE_W_Q4) {
 #pragma unroll
                 for (int w = 0; w < kConsumerWarps; ++w) {
                     ylo += rs[(w * 16 + p) * RC + b];
@@ -246,7 +320,10 @@ __global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const 
                     }
                 }
             }
-            epilogue<EPI>(a, u, p, b, ylo, yhi, best);
+            if (EPI == FORGE_EPI_RESID_TP)
+                tp_resid_epilogue(a, u, p, b, act, ylo, yhi);
+            else
+                epilogue<EPI>(a, u, p, b, ylo, yhi, best);
         }
     }
 
@@ -272,7 +349,7 @@ template <int WK, int PRO>
 int configure_epi() {
     return configure_one<WK, PRO, FORGE_EPI_STORE>() | configure_one<WK, PRO, FORGE_EPI_RESID>() |
            configure_one<WK, PRO, FORGE_EPI_QKV>() | configure_one<WK, PRO, FORGE_EPI_SWIGLU>() |
-           configure_one<WK, PRO, FORGE_EPI_LOGITS>();
+           configure_one<WK, PRO, FORGE_EPI_LOGITS>() | configure_one<WK, PRO, FORGE_EPI_RESID_TP>();
 }
 
 template <int WK, int PRO, int EPI>
@@ -284,7 +361,9 @@ int launch_one(const ForgeGemvArgs& a, cudaStream_t stream, bool pdl, int smem) 
         const char* e = getenv("FORGE_GEMV_CTAS_PER_SM");
         ctas_per_sm = (e && atoi(e) > 0 && atoi(e) <= 4) ? atoi(e) : 1;
     }
-    int grid = forge_sm_count() * ctas_per_sm;
+    // the tensor-parallel epilogue waits for the peers' CTAs of the same
+    // tile: one CTA per SM, so every CTA is resident
+    int grid = forge_sm_count() * (EPI == FORGE_EPI_RESID_TP ? 1 : ctas_per_sm);
     if (grid > units) grid = units;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -309,6 +388,7 @@ int dispatch_epi(const ForgeGemvArgs& a, cudaStream_t s, bool pdl, int smem) {
     case FORGE_EPI_QKV: return launch_one<WK, PRO, FORGE_EPI_QKV>(a, s, pdl, smem);
     case FORGE_EPI_SWIGLU: return launch_one<WK, PRO, FORGE_EPI_SWIGLU>(a, s, pdl, smem);
     case FORGE_EPI_LOGITS: return launch_one<WK, PRO, FORGE_EPI_LOGITS>(a, s, pdl, smem);
+    case FORGE_EPI_RESID_TP: return launch_one<WK, PRO, FORGE_EPI_RESID_TP>(a, s, pdl, smem);
     default: return forge_fail(-1, "gemv: unknown epilogue %d", a.epi);
     }
 }
@@ -346,6 +426,8 @@ int forge_gemv_launch(const ForgeGemvArgs& a0, cudaStream_t stream, bool pdl) {
     if (a0.pro == FORGE_PRO_RMSNORM && !a0.gain) return forge_fail(-1, "gemv: RMSNorm prologue needs a gain");
     if ((a0.x_stride % 4) || (a0.K % 16)) return forge_fail(-1, "gemv: K %% 16 == 0 and 16-byte aligned x rows required");
     if (a0.epi == FORGE_EPI_SWIGLU && a0.N != 2 * a0.F) return forge_fail(-1, "gemv: SwiGLU needs N == 2F");
+    if (a0.epi == FORGE_EPI_RESID_TP && (!a0.tpf || a0.batch > 4))
+        return forge_fail(-1, "gemv: the tensor-parallel residual epilogue takes 1..4 sequences and exchange buffers");
     if (a0.epi == FORGE_EPI_QKV && (a0.hd % 16 || a0.N != (a0.H + 2 * a0.Hkv) * a0.hd))
         return forge_fail(-1, "gemv: QKV epilogue shape mismatch");
     const bool q4 = a0.wkind == FORGE_W_Q4;

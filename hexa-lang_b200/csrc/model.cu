@@ -291,13 +291,37 @@ ForgeGemvArgs gemv_base(const ForgeB200* h, int B) {
 // product to the residual stream, the other ranks store theirs, and one
 // all-reduce (sum) leaves x + sum of all partials on every rank.
 int resid_epi(const ForgeB200* h) { return h->tp_rank == 0 ? FORGE_EPI_RESID : FORGE_EPI_STORE; }
+// small vectors (up to 32K floats, 8 sequences of 4096): one-shot through
+// peer memory; larger ones: NCCL's bandwidth-efficient protocols
+bool tp_oneshot(const ForgeB200* h, int B) {
+    return h->ar && B * h->d <= 32768 && B * h->d <= forge_tp_ar_capacity(h->ar);
+}
 int tp_sum(ForgeB200* h, float* x, int B) {
     if (!h->comm) return 0;
-    // small vectors (up to 32K floats, 8 sequences of 4096): one-shot through
-    // peer memory; larger ones: NCCL's bandwidth-efficient protocols
-    if (h->ar && B * h->d <= 32768 && B * h->d <= forge_tp_ar_capacity(h->ar))
-        return forge_tp_ar_sum_f32(h->ar, x, B * h->d, h->err, h->stream);
+    if (tp_oneshot(h, B)) return forge_tp_ar_sum_f32(h->ar, x, B * h->d, h->err, h->stream);
     return forge_tp_allreduce_sum_f32(h->comm, x, (size_t)B * h->d, h->stream);
+}
+
+// Up to 4 sequences over peer memory: the O / down GEMV's epilogue exchanges
+// each finished 16-row tile with the peers and sums the partials in rank
+// order (the bits of GEMV + tp_sum, without the all-reduce launch).
+// Opt-in with FORGE_TP_FUSED_RESID=1.
+bool tp_fused(const ForgeB200* h, int B) {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("FORGE_TP_FUSED_RESID");
+        on = (e && e[0] == '1') ? 1 : 0;
+    }
+    return on && h->ar && B <= 4 && B * h->d <= forge_tp_ar_capacity(h->ar);
+}
+int resid_gemv(ForgeB200* h, ForgeGemvArgs& g, float* x, int B, bool pdl) {
+    if (tp_fused(h, B)) {
+        g.epi = FORGE_EPI_RESID_TP;
+        g.tpf = forge_tp_fused_dev(h->ar);
+        return forge_gemv_launch(g, h->stream, pdl);
+    }
+    if (forge_gemv_launch(g, h->stream, pdl)) return -1;
+    return tp_sum(h, x, B);
 }
 
 // RMSNorm + QKV + RoPE, K/V appended at each sequence's position.
@@ -328,8 +352,7 @@ int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool p
     ForgeGemvArgs g = gemv_base(h, B);
     g.w = Ld.o_w; g.s = Ld.o_s; g.N = h->d; g.K = h->qd; g.x = ctx; g.x_stride = h->qd;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
-    if (forge_gemv_launch(g, h->stream, pdl)) return -1;
-    return tp_sum(h, x, B);
+    return resid_gemv(h, g, x, B, pdl);
 }
 
 // x += Wd (silu(Wg n) * (Wu n)), n = RMSNorm(x) * g2
@@ -343,8 +366,7 @@ int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl) {
     g = gemv_base(h, B);
     g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = h->s; g.x_stride = h->F;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
-    if (forge_gemv_launch(g, h->stream, pdl)) return -1;
-    return tp_sum(h, x, B);
+    return resid_gemv(h, g, x, B, pdl);
 }
 
 // final RMSNorm + LM head into the handle's logits, argmax keys updated
@@ -985,6 +1007,7 @@ FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
     const bool split = h->split_for(batch);
     auto launches = [&](int K) { return forge_gemv_launch_count(K, batch, split, h->q4, h->bscratch != nullptr); };
     int per_layer = launches(h->d) * 2 + launches(h->qd) + launches(h->F) + 1;
+    if (h->comm && !tp_fused(h, batch) && tp_oneshot(h, batch)) per_layer += 2;  // the peer-memory all-reduces
     return 1 + h->L * per_layer + forge_gemv_launch_count(h->d, batch, split, false, h->bscratch != nullptr) + 1;
 }
 int64_t forge_b200_width(const ForgeB200* h, int which) {

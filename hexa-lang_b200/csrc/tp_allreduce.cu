@@ -99,8 +99,11 @@ __global__ void __launch_bounds__(kThreads) k_tp_allreduce(float* x, int n, cons
 
 struct ForgeTpAr {
     ArDev dev{};
-    void* local = nullptr;   // receive buffer + flags (one allocation)
+    void* local = nullptr;   // receive buffers + flags (one allocation, mapped by every peer)
     uint32_t* epoch = nullptr;
+    ForgeTpFusedDev fused{};          // host copy
+    ForgeTpFusedDev* fused_dev = nullptr;
+    uint32_t* tile_epoch = nullptr;
     std::vector<void*> opened;
 };
 
@@ -110,11 +113,18 @@ struct ForgeTpAr {
 int forge_tp_ar_init(void* comm, int rank, int T, int cap, cudaStream_t stream, ForgeTpAr** out) {
     if (T < 2 || T > kMaxRanks || cap <= 0) return forge_fail(-1, "tp all-reduce: %d ranks (2..%d)", T, kMaxRanks);
     ForgeTpAr* ar = new ForgeTpAr();
-    cap = (cap + 3) & ~3;
+    cap = (cap + 15) & ~15;
+    const int max_tiles = cap / 16;  // 16-row tiles of a vector of cap rows
     const size_t buf_bytes = (size_t)2 * T * cap * 4, flag_bytes = (size_t)2 * T * kSlices * 4;
-    if (cudaMalloc(&ar->local, buf_bytes + flag_bytes) != cudaSuccess ||
-        cudaMemset(ar->local, 0, buf_bytes + flag_bytes) != cudaSuccess ||
-        cudaMalloc(&ar->epoch, kSlices * 4) != cudaSuccess || cudaMemset(ar->epoch, 0, kSlices * 4) != cudaSuccess) {
+    // the GEMV epilogue exchange has its own buffers and per-tile flags
+    const size_t fbuf_off = buf_bytes + flag_bytes, fbuf_bytes = (size_t)2 * T * cap * 4;
+    const size_t fflag_off = fbuf_off + fbuf_bytes, fflag_bytes = (size_t)2 * T * max_tiles * 4;
+    const size_t total = fflag_off + fflag_bytes;
+    if (cudaMalloc(&ar->local, total) != cudaSuccess || cudaMemset(ar->local, 0, total) != cudaSuccess ||
+        cudaMalloc(&ar->epoch, kSlices * 4) != cudaSuccess || cudaMemset(ar->epoch, 0, kSlices * 4) != cudaSuccess ||
+        cudaMalloc(&ar->tile_epoch, (size_t)max_tiles * 4) != cudaSuccess ||
+        cudaMemset(ar->tile_epoch, 0, (size_t)max_tiles * 4) != cudaSuccess ||
+        cudaMalloc(&ar->fused_dev, sizeof(ForgeTpFusedDev)) != cudaSuccess) {
         cudaGetLastError();
         forge_tp_ar_destroy(ar);
         return forge_fail(-1, "tp all-reduce: device allocation failed");
@@ -152,6 +162,8 @@ int forge_tp_ar_init(void* comm, int rank, int T, int cap, cudaStream_t stream, 
         }
         ar->dev.peer_buf[r] = (float*)p;
         ar->dev.peer_flag[r] = (uint32_t*)((char*)p + buf_bytes);
+        ar->fused.buf[r] = (float*)((char*)p + fbuf_off);
+        ar->fused.flag[r] = (uint32_t*)((char*)p + fflag_off);
     }
     if (rc) {
         forge_tp_ar_destroy(ar);
@@ -161,15 +173,29 @@ int forge_tp_ar_init(void* comm, int rank, int T, int cap, cudaStream_t stream, 
     ar->dev.T = T;
     ar->dev.rank = rank;
     ar->dev.cap = cap;
+    ar->fused.tile_epoch = ar->tile_epoch;
+    ar->fused.T = T;
+    ar->fused.rank = rank;
+    ar->fused.cap = cap;
+    ar->fused.max_tiles = max_tiles;
+    if (cudaMemcpy(ar->fused_dev, &ar->fused, sizeof(ForgeTpFusedDev), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaGetLastError();
+        forge_tp_ar_destroy(ar);
+        return forge_fail(-1, "tp all-reduce: exchange descriptor upload");
+    }
     *out = ar;
     return 0;
 }
+
+const ForgeTpFusedDev* forge_tp_fused_dev(const ForgeTpAr* ar) { return ar ? ar->fused_dev : nullptr; }
 
 void forge_tp_ar_destroy(ForgeTpAr* ar) {
     if (!ar) return;
     for (void* p : ar->opened) cudaIpcCloseMemHandle(p);
     if (ar->local) cudaFree(ar->local);
     if (ar->epoch) cudaFree(ar->epoch);
+    if (ar->tile_epoch) cudaFree(ar->tile_epoch);
+    if (ar->fused_dev) cudaFree(ar->fused_dev);
     delete ar;
 }
 

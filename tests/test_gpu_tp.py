@@ -3,8 +3,9 @@ the sharded model (heads, FFN groups and vocabulary split, NCCL all-reduce
 after the O and down projections, max all-reduce of the argmax keys) must give
 the single-GPU logits up to summation order and the same greedy tokens.
 Runs as two spawned rank processes, with the residual all-reduce through
-peer memory (the default) and through NCCL; skipped with fewer than two
-GPUs."""
+peer memory (the default; up to 4 sequences it runs inside the O / down
+GEMV's epilogue) and through NCCL; skipped with fewer than two GPUs. The
+fused epilogue must give the bits of the GEMV + separate all-reduce."""
 import os
 import socket
 
@@ -40,7 +41,7 @@ def _run(fb, model_kw, tp_kw, device):
     return gen, np.stack(lgs)
 
 
-def _rank_main(rank, world, port, name, ar, q):
+def _rank_main(rank, world, port, name, ar, q, fused="1"):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "hexa-lang_b200"))
@@ -48,7 +49,7 @@ def _rank_main(rank, world, port, name, ar, q):
     import torch
     import torch.distributed as dist
     import forge_b200 as fb
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), FORGE_TP_ALLREDUCE=ar)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), FORGE_TP_ALLREDUCE=ar, FORGE_TP_FUSED_RESID=fused)
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
@@ -62,18 +63,12 @@ def _rank_main(rank, world, port, name, ar, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("ar", ["peer", "nccl"])
-@pytest.mark.parametrize("name", list(CONFIGS))
-def test_tp2_matches_single_gpu(forge, cuda, name, ar):
+def _tp2(name, ar, fused="1"):
     import multiprocessing as mp
-    import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    ref_gen, ref_lgs = _run(forge, CONFIGS[name], {}, 0)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, name, ar, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, name, ar, q, fused)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -82,6 +77,17 @@ def test_tp2_matches_single_gpu(forge, cuda, name, ar):
         res[rank] = (gen, lgs, err)
     for p in procs:
         p.join(timeout=120)
+    return res
+
+
+@pytest.mark.parametrize("ar", ["peer", "nccl"])
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_tp2_matches_single_gpu(forge, cuda, name, ar):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ref_gen, ref_lgs = _run(forge, CONFIGS[name], {}, 0)
+    res = _tp2(name, ar)
     for rank in (0, 1):
         gen, lgs, err = res[rank]
         assert err is None, err
@@ -90,3 +96,16 @@ def test_tp2_matches_single_gpu(forge, cuda, name, ar):
         scale = np.abs(ref_lgs).max()
         assert np.abs(lgs - ref_lgs).max() <= 2e-3 * scale, np.abs(lgs - ref_lgs).max()
     assert np.array_equal(res[0][1], res[1][1])
+
+
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_tp2_fused_residual_same_bits(cuda, name):
+    """The exchange inside the GEMV epilogue against GEMV + one-shot all-reduce."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    fused, plain = _tp2(name, "peer", "1"), _tp2(name, "peer", "0")
+    for rank in (0, 1):
+        assert fused[rank][2] is None and plain[rank][2] is None, (fused[rank][2], plain[rank][2])
+        assert np.array_equal(fused[rank][0], plain[rank][0])
+        assert np.array_equal(fused[rank][1], plain[rank][1])
