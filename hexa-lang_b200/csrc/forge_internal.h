@@ -12,6 +12,8 @@ enum { FORGE_PERM_NONE = 0, FORGE_PERM_QKV = 1, FORGE_PERM_GATEUP = 2 };
 // to stderr, the reference's "one stderr line, return -1" contract) and
 // returns `code`.
 int forge_fail(int code, const char* fmt, ...);
+// The logical (unsharded) description a model handle was created with.
+extern "C" const struct ForgeModelDesc* forge_b200_desc_of(const struct ForgeB200* h);
 // Checks cudaGetLastError after a launch; 0 or -1.
 int forge_check_launch(const char* what);
 // Number of SMs of the current device (cached per device).

@@ -792,6 +792,8 @@ FORGE_API void forge_b200_destroy(ForgeB200* h) {
 
 FORGE_API void* forge_b200_stream(ForgeB200* h) { return h ? (void*)h->stream : nullptr; }
 
+const ForgeModelDesc* forge_b200_desc_of(const ForgeB200* h) { return h ? &h->desc : nullptr; }
+
 FORGE_API int forge_b200_load_layer(ForgeB200* h, int layer, const ForgeLayerWeights* w) {
     if (!h || !w || layer < 0 || layer >= h->L) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_load_layer: bad args");
     if (!w->wq || !w->wk || !w->wv || !w->wo || !w->wg || !w->wu || !w->wd || !w->g1 || !w->g2)

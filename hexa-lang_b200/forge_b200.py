@@ -38,6 +38,17 @@ class ForgeLayerWeights(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "wg", "wu", "wd", "g1", "g2")]
 
 
+class ForgeStTensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_int32), ("ndim", C.c_int32), ("shape", C.c_int64 * 8),
+                ("offset", C.c_int64), ("nbytes", C.c_int64), ("data", C.c_void_p)]
+
+
+# safetensors dtype codes (include/forge_safetensors.h) and their names
+ST_DTYPES = ["BOOL", "U8", "I8", "I16", "U16", "F16", "BF16", "I32", "U32", "F32", "F64", "I64", "U64",
+             "F8_E4M3", "F8_E5M2"]
+FORGE_ST_NOT_FOUND = -6
+
+
 class ForgeShapeInfo(C.Structure):
     _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("batch", C.c_int64)]
 
@@ -191,6 +202,23 @@ def lib() -> C.CDLL:
             "hexa_kv_set_positions": (i32, [C.POINTER(HexaKvCache), vp, i64]),
             "hexa_kv_write": (i32, [C.POINTER(HexaKvCache), i64, i64, vp, vp, i64]),
             "forge_api_version_v2": (C.c_uint32, []),
+            "forge_st_open": (i32, [C.c_char_p, C.POINTER(vp)]),
+            "forge_st_close": (i32, [vp]),
+            "forge_st_header": (vp, [vp, C.POINTER(C.c_int64)]),
+            "forge_st_data_offset": (i64, [vp]),
+            "forge_st_size": (i64, [vp]),
+            "forge_st_count": (i32, [vp]),
+            "forge_st_total_bytes": (i64, [vp]),
+            "forge_st_tensor_at": (i32, [vp, i32, C.POINTER(ForgeStTensor)]),
+            "forge_st_find": (i32, [vp, C.c_char_p, C.POINTER(ForgeStTensor)]),
+            "forge_st_metadata": (C.c_char_p, [vp, C.c_char_p]),
+            "forge_st_view_u8": (i32, [C.POINTER(ForgeStTensor), i64]),
+            "forge_st_read_bytes": (i64, [vp, i64, i64, vp]),
+            "forge_st_read_f32": (i64, [vp, i64, i64, vp]),
+            "forge_st_read_bf16_to_f32": (i64, [vp, i64, i64, vp]),
+            "forge_st_tensor_to_bf16": (i32, [C.POINTER(ForgeStTensor), vp, i64]),
+            "forge_st_tensor_to_f32": (i32, [C.POINTER(ForgeStTensor), vp, i64]),
+            "forge_b200_load_safetensors": (i32, [vp, i32, C.POINTER(C.c_char_p)]),
         }
         for name, (res, args) in sig.items():
             if hasattr(L, name):
@@ -218,6 +246,106 @@ def _ptr(a) -> int:
     if hasattr(a, "data_ptr"):
         return a.data_ptr()
     return a.ctypes.data
+
+
+class Safetensors:
+    """Read-only mapped safetensors file (forge_st_*; the hexa runtime's
+    safetensors_mmap_* builtins, self/runtime.h:1068-1082). Host only."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        check(lib().forge_st_open(os.fsencode(path), C.byref(h)), f"forge_st_open({path})")
+        self.h = h
+
+    def close(self):
+        rc = 0
+        if getattr(self, "h", None):
+            rc = lib().forge_st_close(self.h)
+            self.h = None
+        return rc
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def header(self) -> bytes:
+        n = C.c_int64()
+        p = lib().forge_st_header(self.h, C.byref(n))
+        return C.string_at(p, n.value)
+
+    @property
+    def data_offset(self):
+        return lib().forge_st_data_offset(self.h)
+
+    @property
+    def size(self):
+        return lib().forge_st_size(self.h)
+
+    @property
+    def total_bytes(self):
+        return lib().forge_st_total_bytes(self.h)
+
+    def __len__(self):
+        return lib().forge_st_count(self.h)
+
+    def tensor_at(self, i) -> ForgeStTensor:
+        v = ForgeStTensor()
+        check(lib().forge_st_tensor_at(self.h, i, C.byref(v)), "forge_st_tensor_at")
+        return v
+
+    def names(self):
+        return [self.tensor_at(i).name.decode() for i in range(len(self))]
+
+    def find(self, name):
+        """The tensor view, or None when the file has no such tensor."""
+        v = ForgeStTensor()
+        rc = lib().forge_st_find(self.h, name.encode(), C.byref(v))
+        if rc == FORGE_ST_NOT_FOUND:
+            return None
+        check(rc, "forge_st_find")
+        return v
+
+    def metadata(self, key):
+        r = lib().forge_st_metadata(self.h, key.encode())
+        return None if r is None else r.decode()
+
+    def read_bytes(self, off, n) -> bytes:
+        buf = C.create_string_buffer(max(n, 1))
+        r = lib().forge_st_read_bytes(self.h, off, n, buf)
+        if r < 0:
+            check(r, "forge_st_read_bytes")
+        return buf.raw[:n]
+
+    def _read_f(self, fn, off, n):
+        import numpy as np
+        out = np.empty(n, np.float32)
+        r = fn(self.h, off, n, out.ctypes.data)
+        if r < 0:
+            check(r, fn.__name__)
+        return out
+
+    def read_f32(self, off, n):
+        return self._read_f(lib().forge_st_read_f32, off, n)
+
+    def read_bf16_to_f32(self, off, n):
+        return self._read_f(lib().forge_st_read_bf16_to_f32, off, n)
+
+    def to_bf16(self, v):
+        """The tensor as bf16 bit patterns (uint16), rounded to nearest even."""
+        import numpy as np
+        n = int(np.prod([v.shape[i] for i in range(v.ndim)], dtype=np.int64))
+        out = np.empty(n, np.uint16)
+        check(lib().forge_st_tensor_to_bf16(C.byref(v), out.ctypes.data, n), "forge_st_tensor_to_bf16")
+        return out
+
+    def to_f32(self, v):
+        import numpy as np
+        n = int(np.prod([v.shape[i] for i in range(v.ndim)], dtype=np.int64))
+        out = np.empty(n, np.float32)
+        check(lib().forge_st_tensor_to_f32(C.byref(v), out.ctypes.data, n), "forge_st_tensor_to_f32")
+        return out
 
 
 class ForgeModel:
@@ -258,6 +386,13 @@ class ForgeModel:
 
     def load_embedding(self, emb, gF, head=None):
         check(lib().forge_b200_load_embedding(self.h, _ptr(emb), _ptr(gF), _ptr(head)), "load_embedding")
+
+    def load_safetensors(self, paths):
+        """Llama-layout checkpoint from one or more .safetensors shards."""
+        if isinstance(paths, (str, bytes, os.PathLike)):
+            paths = [paths]
+        arr = (C.c_char_p * len(paths))(*[os.fsencode(p) for p in paths])
+        check(lib().forge_b200_load_safetensors(self.h, len(paths), arr), "load_safetensors")
 
     def reset(self):
         check(lib().forge_b200_reset(self.h), "reset")
