@@ -12,6 +12,11 @@ enum { FORGE_PERM_NONE = 0, FORGE_PERM_QKV = 1, FORGE_PERM_GATEUP = 2 };
 // to stderr, the reference's "one stderr line, return -1" contract) and
 // returns `code`.
 int forge_fail(int code, const char* fmt, ...);
+// Reference sampler over logits rows (sample.cu); probs is the working
+// distribution [batch][pld], tokens and RNG states per row.
+int forge_sample_launch(const float* logits, int64_t ld, int batch, int vocab, double temperature, int top_k,
+                        double top_p, int64_t* rng_state, float* probs, int64_t pld, int32_t* tokens,
+                        cudaStream_t stream);
 // The logical (unsharded) description a model handle was created with.
 extern "C" const struct ForgeModelDesc* forge_b200_desc_of(const struct ForgeB200* h);
 // Checks cudaGetLastError after a launch; 0 or -1.

@@ -115,6 +115,8 @@ struct ForgeB200 {
     uint8_t* codes = nullptr;
     uint16_t* scales = nullptr;
     int32_t* h_tok = nullptr;  // pinned staging [Bmax]
+    float* samp_probs = nullptr;     // sampler distribution [Bmax][Vpad] (first sampled step)
+    int64_t* samp_rng = nullptr;     // sampler RNG states [Bmax]
     std::map<int, cudaGraphExec_t> graphs;
     std::map<int, ForgeStepArgs> fused;   // per batch size: fused-step arguments (phases on device)
     std::map<int, int> fused_ok;          // per batch size: 1 fused path fits, 0 no
@@ -926,6 +928,38 @@ FORGE_API int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tok
     if (cudaStreamSynchronize(h->stream) != cudaSuccess)
         return forge_fail(-1, "forge_b200_decode_step: %s", cudaGetErrorString(cudaGetLastError()));
     if (next_tokens) memcpy(next_tokens, stage, 4 * batch);
+    return read_err(h);
+}
+
+// One decode step whose next tokens are drawn by the reference sampler
+// (self/ml/gpu_sampler.hexa:89-277) from the step's logits on the device;
+// rng_state [batch] is read and advanced (host array).
+FORGE_API int forge_b200_decode_step_sampled(ForgeB200* h, int batch, const int32_t* tokens, int32_t* next_tokens,
+                                             double temperature, int top_k, double top_p, int64_t* rng_state) {
+    if (int rc = check_ready(h, batch)) return rc;
+    if (!tokens || !next_tokens || !rng_state)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_decode_step_sampled: null tokens or RNG state");
+    if (h->comm)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_decode_step_sampled: not available under tensor parallelism");
+    if (!h->samp_probs) {
+        h->samp_probs = (float*)h->alloc(sizeof(float) * (size_t)h->Bmax * h->Vpad);
+        h->samp_rng = (int64_t*)h->alloc(sizeof(int64_t) * (size_t)h->Bmax);
+        if (!h->samp_probs || !h->samp_rng) return forge_fail(-1, "forge_b200_decode_step_sampled: allocation failed");
+    }
+    int32_t* stage = h->h_tok;
+    if (!stage) return forge_fail(-1, "forge_b200_decode_step_sampled: no pinned staging buffer");
+    memcpy(stage, tokens, 4 * batch);
+    cudaMemcpyAsync(h->tok, stage, 4 * batch, cudaMemcpyHostToDevice, h->stream);
+    cudaMemcpyAsync(h->samp_rng, rng_state, 8 * batch, cudaMemcpyHostToDevice, h->stream);
+    if (enqueue_one(h, batch)) return -1;
+    if (forge_sample_launch(h->logits, h->Vpad, batch, h->V, temperature, top_k, top_p, h->samp_rng, h->samp_probs,
+                            h->Vpad, h->tok, h->stream))
+        return -1;
+    cudaMemcpyAsync(stage, h->tok, 4 * batch, cudaMemcpyDeviceToHost, h->stream);
+    cudaMemcpyAsync(rng_state, h->samp_rng, 8 * batch, cudaMemcpyDeviceToHost, h->stream);
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_decode_step_sampled: %s", cudaGetErrorString(cudaGetLastError()));
+    memcpy(next_tokens, stage, 4 * batch);
     return read_err(h);
 }
 

@@ -202,6 +202,8 @@ def lib() -> C.CDLL:
             "hexa_kv_set_positions": (i32, [C.POINTER(HexaKvCache), vp, i64]),
             "hexa_kv_write": (i32, [C.POINTER(HexaKvCache), i64, i64, vp, vp, i64]),
             "forge_api_version_v2": (C.c_uint32, []),
+            "forge_sample": (i32, [vp, i64, i32, i32, C.c_double, i32, C.c_double, vp, vp, vp, vp]),
+            "forge_b200_decode_step_sampled": (i32, [vp, i32, vp, vp, C.c_double, i32, C.c_double, vp]),
             "forge_st_open": (i32, [C.c_char_p, C.POINTER(vp)]),
             "forge_st_close": (i32, [vp]),
             "forge_st_header": (vp, [vp, C.POINTER(C.c_int64)]),
@@ -448,6 +450,17 @@ class ForgeModel:
         lg = np.zeros((len(t), self.vocab), np.float32) if want_logits else None
         check(lib().forge_b200_decode_step(self.h, len(t), _ptr(t), _ptr(nxt), _ptr(lg)), "decode_step")
         return (nxt, lg) if want_logits else nxt
+
+    def step_sampled(self, tokens, rng_state, temperature=0.7, top_k=40, top_p=0.9):
+        """One step with the reference sampler (defaults: gpu_sampler_default);
+        rng_state is an int64 array [batch], advanced in place."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        assert rng_state.dtype == np.int64 and rng_state.flags.c_contiguous and rng_state.size >= len(t)
+        nxt = np.zeros(len(t), np.int32)
+        check(lib().forge_b200_decode_step_sampled(self.h, len(t), _ptr(t), _ptr(nxt), float(temperature),
+                                                    int(top_k), float(top_p), _ptr(rng_state)), "decode_step_sampled")
+        return nxt
 
     def decode_device(self, batch, n_steps):
         check(lib().forge_b200_decode_device(self.h, batch, n_steps), "decode_device")

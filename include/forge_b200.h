@@ -146,6 +146,13 @@ int forge_b200_set_kv(ForgeB200* h, int layer, int seq, const uint16_t* k, const
  * tokens and optional logits [batch][vocab]); synchronous. */
 int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tokens, int32_t* next_tokens,
                            float* logits);
+/* One decode step whose next tokens are drawn from the step's logits by the
+ * sampler of self/ml/gpu_sampler.hexa:89-277 (GpuSamplerConfig: temperature
+ * <= 0 is argmax; top_k 0 and top_p >= 1 switch those filters off), on the
+ * device; rng_state [batch] holds each sequence's 64-bit RNG state
+ * (gpu_sampler_set_seed) and is advanced. Single-GPU handles; synchronous. */
+int forge_b200_decode_step_sampled(ForgeB200* h, int batch, const int32_t* tokens, int32_t* next_tokens,
+                                   double temperature, int top_k, double top_p, int64_t* rng_state);
 /* n_steps device-resident greedy steps (each feeds its argmax to the next);
  * asynchronous on the handle's stream. */
 int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps);
@@ -221,6 +228,13 @@ int64_t forge_flash_decode_noalloc_capacity(void);
 int forge_flash_decode_noalloc(const float* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos,
                                int B, int H, int Hkv, int hd, int lmax, float* out, void* stream);
 int forge_flash_decode_noalloc_status(void);
+
+/* The sampler alone on device arrays (gpu_sampler.hexa:89-277, per row):
+ * logits [batch][ld] f32, probs [batch][vocab] f32 (working buffer; holds
+ * the final distribution), rng_state [batch] int64 (advanced; may be NULL
+ * when temperature <= 0), tokens [batch] int32. Asynchronous on stream. */
+int forge_sample(const float* logits, int64_t ld, int batch, int vocab, double temperature, int top_k,
+                 double top_p, int64_t* rng_state, float* probs, int32_t* tokens, void* stream);
 
 /* Causal (or full) flash-attention prefill on the tcgen05 tensor cores:
  * q, k, v, o [B][H][S][hd] bf16 device arrays (16-byte aligned), hd = 128,

@@ -588,3 +588,106 @@ void or_ref_lcg_f32(uint32_t* state, float* out, int64_t n) {
     }
     *state = st;
 }
+
+/* ------------------------------------------------------------- sampler --
+ * self/ml/gpu_sampler.hexa: RNG at :57-65, argmax at :70-85, the pipeline at
+ * :89-277. The host buffer of the reference holds f32 (deref_f32 /
+ * write_f32); hexa floats are f64. */
+double or_sampler_rand(int64_t* state) {
+    int64_t x = *state;
+    x = x ^ (int64_t)((uint64_t)x * 8192u);
+    x = x ^ (x / 131072);
+    x = x ^ (int64_t)((uint64_t)x * 32u);
+    if (x < 0) x = (int64_t)(0u - (uint64_t)x);
+    *state = x;
+    return (double)(x % 1000000) / 1000000.0;
+}
+
+static int or_argmax_first(const float* v, int n) {
+    int best = 0;
+    double bv = v[0];
+    for (int i = 1; i < n; ++i)
+        if ((double)v[i] > bv) { bv = v[i]; best = i; }
+    return best;
+}
+
+int or_sample_token(const float* logits, int V, double temperature, int top_k, double top_p,
+                    int64_t* rng_state, float* probs) {
+    if (V <= 0) return -1;
+    if (temperature <= 0.0) return or_argmax_first(logits, V);
+    float* h = (float*)malloc(sizeof(float) * (size_t)V);
+    const double inv_t = 1.0 / temperature;
+    for (int i = 0; i < V; ++i) h[i] = (float)((double)logits[i] * inv_t);
+    double mx = h[0];
+    for (int i = 1; i < V; ++i)
+        if ((double)h[i] > mx) mx = h[i];
+    double sum_e = 0.0;
+    for (int i = 0; i < V; ++i) {
+        const double e = exp((double)h[i] - mx);
+        h[i] = (float)e;
+        sum_e = sum_e + e;
+    }
+    const double inv_sum = 1.0 / sum_e;
+    for (int i = 0; i < V; ++i) h[i] = (float)((double)h[i] * inv_sum);
+    if (top_k > 0 && top_k < V) {
+        float* sb = (float*)malloc(sizeof(float) * (size_t)V);
+        memcpy(sb, h, sizeof(float) * (size_t)V);
+        for (int j = 0; j < top_k; ++j) {  /* partial selection sort */
+            int best = j;
+            for (int m = j + 1; m < V; ++m)
+                if ((double)sb[m] > (double)sb[best]) best = m;
+            if (best != j) { float t = sb[j]; sb[j] = sb[best]; sb[best] = t; }
+        }
+        const double thr = sb[top_k - 1];
+        free(sb);
+        double sum_k = 0.0;
+        for (int i = 0; i < V; ++i) {
+            if ((double)h[i] < thr) h[i] = 0.0f;
+            else sum_k = sum_k + (double)h[i];
+        }
+        if (sum_k > 0.0) {
+            const double inv_k = 1.0 / sum_k;
+            for (int i = 0; i < V; ++i) h[i] = (float)((double)h[i] * inv_k);
+        }
+    }
+    if (top_p < 1.0 && top_p > 0.0) {
+        int* idx = (int*)malloc(sizeof(int) * (size_t)V);
+        double* val = (double*)malloc(sizeof(double) * (size_t)V);
+        int nn = 0;
+        for (int i = 0; i < V; ++i)
+            if ((double)h[i] > 0.0) { idx[nn] = i; val[nn] = h[i]; ++nn; }
+        for (int ii = 0; ii < nn; ++ii) {  /* selection sort, descending, with swaps */
+            int best = ii;
+            for (int jj = ii + 1; jj < nn; ++jj)
+                if (val[jj] > val[best]) best = jj;
+            if (best != ii) {
+                int ti = idx[ii]; idx[ii] = idx[best]; idx[best] = ti;
+                double tv = val[ii]; val[ii] = val[best]; val[best] = tv;
+            }
+        }
+        for (int i = 0; i < V; ++i) h[i] = 0.0f;
+        double cum = 0.0, sum_p = 0.0;
+        for (int i = 0; i < nn; ++i) {
+            h[idx[i]] = (float)val[i];
+            sum_p = sum_p + val[i];
+            cum = cum + val[i];
+            if (cum >= top_p) break;
+        }
+        if (sum_p > 0.0) {
+            const double inv_p = 1.0 / sum_p;
+            for (int i = 0; i < V; ++i) h[i] = (float)((double)h[i] * inv_p);
+        }
+        free(idx);
+        free(val);
+    }
+    const double r = or_sampler_rand(rng_state);
+    double cum = 0.0;
+    int chosen = V - 1;
+    for (int i = 0; i < V; ++i) {
+        cum = cum + (double)h[i];
+        if (cum > r) { chosen = i; break; }
+    }
+    if (probs) memcpy(probs, h, sizeof(float) * (size_t)V);
+    free(h);
+    return chosen;
+}

@@ -118,6 +118,22 @@ int  or_num_threads(void);
  * (mod 2^32), value = (state >> 8) / 2^24 - 0.5 in float. Writes n values
  * and advances *state. */
 void or_ref_lcg_f32(uint32_t* state, float* out, int64_t n);
+
+/* Sampler RNG step (self/ml/gpu_sampler.hexa:57-65): 64-bit two's-complement
+ * state, x ^= x*8192; x ^= x/131072 (division truncating toward zero);
+ * x ^= x*32; x = |x|; returns (x % 1000000) / 1e6. */
+double or_sampler_rand(int64_t* state);
+/* One token from logits [V] (gpu_sampler.hexa:89-277): temperature <= 0 is
+ * the first-max argmax; otherwise temperature scaling, softmax, top-k
+ * (0 < k < V: entries below the k-th largest probability zeroed,
+ * renormalised), top-p (0 < p < 1: nonzero entries sorted descending by
+ * selection sort with swaps, the shortest prefix whose running sum reaches p
+ * kept, renormalised), then the first index whose running sum exceeds one
+ * draw of the RNG (V - 1 if none). f64 arithmetic, every stored value
+ * rounded to f32, sums in the reference's order. probs (may be NULL)
+ * receives the final distribution. */
+int or_sample_token(const float* logits, int V, double temperature, int top_k, double top_p,
+                    int64_t* rng_state, float* probs);
 #ifdef __cplusplus
 }
 #endif

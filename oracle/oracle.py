@@ -69,6 +69,8 @@ def lib() -> C.CDLL:
             "or_matmul_f64": (None, [vp, vp, vp, i32, i32, i32]),
             "or_num_threads": (i32, []),
             "or_ref_lcg_f32": (None, [vp, vp, i64]),
+            "or_sampler_rand": (C.c_double, [vp]),
+            "or_sample_token": (i32, [vp, i32, C.c_double, i32, C.c_double, vp, vp]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)
@@ -87,6 +89,15 @@ def f32_to_bf16(x):
     out = np.empty(x.shape, np.uint16)
     lib().or_f32_to_bf16_n(P(x), P(out), x.size)
     return out
+
+
+def sample_token(logits, temperature, top_k, top_p, state):
+    """One draw of the reference sampler; returns (token, new_state, probs)."""
+    x = np.ascontiguousarray(logits, np.float32)
+    st = C.c_int64(int(state))
+    probs = np.zeros(x.size, np.float32)
+    tok = lib().or_sample_token(P(x), x.size, float(temperature), int(top_k), float(top_p), C.byref(st), P(probs))
+    return tok, st.value, probs
 
 
 def bf16_to_f32(b):
