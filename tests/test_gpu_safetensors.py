@@ -12,7 +12,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 CONFIGS = {
-    "gqa_bf16_untied": dict(n_layer=2, d=256, n_head=8, n_kv=2, hd=32, ffn=512, vocab=1000, q4=False, tied=False),
+    "gqa_bf16_untied": dict(n_layer=2, d=256, n_head=4, n_kv=2, hd=64, ffn=512, vocab=1000, q4=False, tied=False),
     "mha_q4_tied": dict(n_layer=2, d=256, n_head=2, n_kv=2, hd=128, ffn=768, vocab=512, q4=True, tied=True),
 }
 
@@ -112,6 +112,6 @@ def test_safetensors_load_rejects_bad_checkpoints(forge, oracle, cuda, tmp_path)
     (tmp_path / "b").mkdir()
     with pytest.raises(forge.ForgeError, match="model.layers.1.mlp.up_proj.weight missing"):
         m.load_safetensors(_checkpoint(om, cfg, tmp_path / "a", drop="model.layers.1.mlp.up_proj.weight"))
-    with pytest.raises(forge.ForgeError, match=r"self_attn.k_proj.weight has shape \[80, 256\]"):
+    with pytest.raises(forge.ForgeError, match=r"self_attn.k_proj.weight has shape \[144, 256\]"):
         m.load_safetensors(_checkpoint(om, cfg, tmp_path / "b", reshape="model.layers.0.self_attn.k_proj.weight"))
     m.close()
