@@ -53,21 +53,25 @@ constexpr int kMaxSeq = 32;                    // N = 2 x sequences <= 64
 constexpr int kActTile = 64 * 128;             // B tile: 64 columns x 128 k
 constexpr int kActAux = 128 + 256;             // sx[32] f32 + code-bias terms [64] s32
 constexpr int kActGroup = kActTile + kActAux;  // one group's block in global memory
-// raw ring slot: activation tile + sx + sums (one copy) | weights (8 blocks
-// x 2 chunks x 512 B, one 2-D TMA box) | scale blocks (8 x 128 B, one box)
-constexpr int kSlotAct = 0, kSlotAux = 8192, kSlotW = 9216, kSlotS = 17408;
-constexpr int kSlot = 18432;                   // 1024-aligned slots
-constexpr int kNS = 8;
-constexpr int kATile = kTM * 128;              // u8 A tile, 16 KB
-constexpr int kNA = 4;
-constexpr int kNAcc = 4;                       // TMEM accumulators of 64 columns
+// A unit of work is two 128-groups of one 128-row tile (one group when the
+// tile row has an odd group count and this is its last unit). Raw ring slot:
+// per group its activation tile + sx + sums (one plain bulk copy each, the
+// tiles 1024-aligned) | weights (8 blocks x 2 groups x 1 KB, one 2-D TMA
+// box) | scale blocks (8 x 128 B, one box; a box holds 4 groups).
+constexpr int kGU = 2;                          // groups per unit
+constexpr int kSlotAct0 = 0, kSlotAct1 = 9216, kSlotW = 18432, kSlotS = 34816;
+constexpr int kSlot = 35840;                    // 1024-aligned slots
+constexpr int kNS = 4;
+constexpr int kATile = kTM * 128;               // u8 A tile of one group, 16 KB
+constexpr int kNA = 2;                          // A slots of a unit (kGU tiles each)
+constexpr int kNAcc = 2;                        // TMEM accumulator sets of a unit (kGU x 64 columns)
 constexpr int kOffA = kNS * kSlot;
-constexpr int kOffBar = kOffA + kNA * kATile;
+constexpr int kOffBar = kOffA + kNA * kGU * kATile;
 constexpr int kSmem = kOffBar + 512 + 1024;    // barriers + alignment slack
 constexpr int kThreads = 448;
 constexpr int kWarpMma = 1, kWarpUnpack = 2, kWarpEpi = 6;  // arithmetic: warps 6-13
 constexpr int kEpiThreads = 256;
-constexpr uint32_t kTmemCols = 64 * kNAcc;
+constexpr uint32_t kTmemCols = 64 * kGU * kNAcc;
 
 // Byte offset of (row, byte kb) in a [rows][128 B] tile with 128-byte swizzle
 // (8-row atoms of 1 KB; the 16-byte chunk index is XORed with row % 8).
@@ -126,6 +130,7 @@ struct TcArgs {
     float* partial;      // [grid][2][128][32]
     int* ticket;         // [tiles], zero between launches
     int npad;            // MMA N: 2 x sequences rounded up to 16
+    int wbox;            // weight box width in 8-byte elements: 128 per group of a unit
 };
 
 // First unit of CTA c and the CTA that owns unit x, for U units over P CTAs.
@@ -154,16 +159,18 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.K >> 7;
+    const int G2 = (G + kGU - 1) / kGU;  // units per tile
     const int T = (a.N + kTM - 1) / kTM;
     const int nunit16 = a.N >> 4;
-    const int64_t U = (int64_t)T * G;
+    const int64_t U = (int64_t)T * G2;
     const int P = gridDim.x;
     const int64_t u0 = unit_begin(blockIdx.x, U, P), u1 = unit_begin(blockIdx.x + 1, U, P);
     const int nmine = (int)(u1 - u0);
-    // (tile, group) of the first unit; later units step through them
+    // (tile, group pair) of the first unit; later units step through them
     // incrementally (a 64-bit division per unit and thread kept the
     // conversion unit ~50% busy in an earlier version)
-    const int tl0 = (int)(u0 / G), g0 = (int)(u0 - (int64_t)tl0 * G);
+    const int tl0 = (int)(u0 / G2), g0 = (int)(u0 - (int64_t)tl0 * G2);
+    const int wrow = t.wbox * 8;  // bytes of one 16-row block in the weight box
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNS; ++i) {
@@ -197,23 +204,32 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
             // weights: box {1 group = 128 x 8 B, 8 blocks} at (128 g, 8 tile);
             // scales: box {16 x 8 B, 8 blocks} at (16 (g / 4), 8 tile). Rows
             // past N read as zeros and count in full.
+            // weights: box {2 groups = 256 x 8 B, 8 blocks} at (256 pr, 8
+            // tile) (a group past K reads as zeros and counts in full);
+            // scales: box {16 x 8 B, 8 blocks} at (16 (2 pr / 4), 8 tile)
             auto weights = [&](int i) {
-                const int gi = g0 + i, tl = tl0 + gi / G, g = gi - (gi / G) * G;
+                const int gi = g0 + i, tl = tl0 + gi / G2, pr = gi - (gi / G2) * G2;
                 uint8_t* slot = base + (i % kNS) * kSlot;
-                tma_load_2d(slot + kSlotW, &tw, 128 * g, 8 * tl, &raw_full[i % kNS]);
-                tma_load_2d(slot + kSlotS, &ts, 16 * (g >> 2), 8 * tl, &raw_full[i % kNS]);
+                tma_load_2d(slot + kSlotW, &tw, 256 * pr, 8 * tl, &raw_full[i % kNS]);
+                tma_load_2d(slot + kSlotS, &ts, 16 * (pr >> 1), 8 * tl, &raw_full[i % kNS]);
+            };
+            auto two = [&](int i) {
+                const int gi = g0 + i, pr = gi - (gi / G2) * G2;
+                return 2 * pr + 1 < G;
             };
             auto acts = [&](int i) {
-                const int gi = g0 + i, g = gi - (gi / G) * G;
+                const int gi = g0 + i, g = 2 * (gi - (gi / G2) * G2);
                 uint8_t* slot = base + (i % kNS) * kSlot;
-                bulk_g2s(slot + kSlotAct, t.xt + (size_t)g * kActGroup, kActGroup, &raw_full[i % kNS]);
+                bulk_g2s(slot + kSlotAct0, t.xt + (size_t)g * kActGroup, kActGroup, &raw_full[i % kNS]);
+                if (g + 1 < G)
+                    bulk_g2s(slot + kSlotAct1, t.xt + (size_t)(g + 1) * kActGroup, kActGroup, &raw_full[i % kNS]);
             };
-            auto wbytes = [&](int) { return (uint32_t)(8 * 1024 + 8 * 128); };
+            auto wbytes = [&](int i) { return (uint32_t)(wrow * 8 + 8 * 128 + (two(i) ? 0 : -kActGroup)); };
             // weights do not depend on the previous kernel: the first ring's
             // worth is requested before the dependency wait
             const int pre = min(kNS, nmine);
             for (int i = 0; i < pre; ++i) {
-                mbar_arrive_expect_tx(&raw_full[i], wbytes(i) + kActGroup);
+                mbar_arrive_expect_tx(&raw_full[i], wbytes(i) + 2 * kActGroup);
                 weights(i);
             }
             pdl_wait();
@@ -222,7 +238,7 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
             for (int i = pre; i < nmine; ++i) {
                 const int s = i % kNS;
                 if (!mbar_wait(&raw_empty[s], ((i / kNS) & 1) ^ 1, a.err)) break;
-                mbar_arrive_expect_tx(&raw_full[s], wbytes(i) + kActGroup);
+                mbar_arrive_expect_tx(&raw_full[s], wbytes(i) + 2 * kActGroup);
                 weights(i);
                 acts(i);
                 issued = i + 1;
@@ -238,16 +254,20 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
             int done = 0;
             for (int i = 0; i < nmine; ++i) {
                 const int s = i % kNS, as = i % kNA, tb = i % kNAcc;
+                const int gi = g0 + i, pr = gi - (gi / G2) * G2;
+                const int nh = 2 * pr + 1 < G ? 2 : 1;
                 if (!mbar_wait(&raw_full[s], (i / kNS) & 1, a.err)) break;
                 if (!mbar_wait(&a_full[as], (i / kNA) & 1, a.err)) break;
                 if (!mbar_wait(&acc_empty[tb], ((i / kNAcc) & 1) ^ 1, a.err)) break;
                 tc_fence_after();
-                const uint32_t ab = sbase + (uint32_t)(kOffA + as * kATile);
-                const uint32_t bb = sbase + (uint32_t)(s * kSlot + kSlotAct);
+                for (int h = 0; h < nh; ++h) {
+                    const uint32_t ab = sbase + (uint32_t)(kOffA + (as * kGU + h) * kATile);
+                    const uint32_t bb = sbase + (uint32_t)(s * kSlot + (h ? kSlotAct1 : kSlotAct0));
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    umma_i8(tmem + (uint32_t)(tb * 64), umma_desc_sw128(ab + 32 * k, 16, 1024),
-                            umma_desc_sw128(bb + 32 * k, 16, 1024), idesc, k > 0 ? 1u : 0u);
+                    for (int k = 0; k < 4; ++k)
+                        umma_i8(tmem + (uint32_t)((tb * kGU + h) * 64), umma_desc_sw128(ab + 32 * k, 16, 1024),
+                                umma_desc_sw128(bb + 32 * k, 16, 1024), idesc, k > 0 ? 1u : 0u);
+                }
                 umma_commit(&acc_full[tb]);
                 umma_commit(&a_empty[as]);
                 umma_commit(&raw_empty[s]);
@@ -261,18 +281,25 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
     } else if (warp < kWarpEpi) {
         // ------------------------------------------- int4 -> u8 A operand
         const int ut = threadIdx.x - kWarpUnpack * 32;  // 0..127
+        int pr = g0 - 1;
         for (int i = 0; i < nmine; ++i) {
+            if (++pr == G2) pr = 0;
             const int s = i % kNS, as = i % kNA;
+            const int nh = 2 * pr + 1 < G ? 2 : 1;
             const bool ok = mbar_wait(&raw_full[s], (i / kNS) & 1, a.err) &&
                             mbar_wait(&a_empty[as], ((i / kNA) & 1) ^ 1, a.err);
             if (!__all_sync(0xffffffffu, ok)) break;
-            const uint8_t* src = base + s * kSlot + kSlotW;
-            uint8_t* dst = base + kOffA + as * kATile;
+            for (int h = 0; h < nh; ++h) {
+            const uint8_t* src = base + s * kSlot + kSlotW + h * 1024;
+            uint8_t* dst = base + kOffA + (as * kGU + h) * kATile;
             // records = (16-row block, 64-k chunk, lane) of the packed layout;
             // blocks past N arrived as zeros, so every record is converted
             uint4 v[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const uint4*>(src + (ut + 128 * j) * 16);
+            for (int j = 0; j < 4; ++j) {
+                const int rec = ut + 128 * j;
+                v[j] = *reinterpret_cast<const uint4*>(src + (rec >> 6) * wrow + (rec & 63) * 16);
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int rec = ut + 128 * j;
@@ -285,6 +312,7 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
                     *reinterpret_cast<uint32_t*>(dst + swz128(row, kb)) = w4[w] & 0x0F0F0F0Fu;
                     *reinterpret_cast<uint32_t*>(dst + swz128(row + 8, kb)) = (w4[w] >> 4) & 0x0F0F0F0Fu;
                 }
+            }
             }
             fence_proxy_async_smem();
             __syncwarp();
@@ -313,8 +341,9 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
         bool ok = true;
         int tl = tl0, g = g0 - 1;
         for (int i = 0; i < nmine; ++i) {
-            if (++g == G) { g = 0; ++tl; }
+            if (++g == G2) { g = 0; ++tl; }  // g: the unit's group pair within the tile
             const int s = i % kNS, tb = i % kNAcc;
+            const int nh = 2 * g + 1 < G ? 2 : 1;
             if (ok) {
                 const bool w1 = mbar_wait(&acc_full[tb], (i / kNAcc) & 1, a.err) &&
                                 mbar_wait(&raw_full[s], (i / kNS) & 1, a.err);
@@ -322,19 +351,24 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
             }
             if (ok) {
                 tc_fence_after();
-                uint32_t acc[2][16];  // columns past 2 x batch hold stale values, never stored
-                tmem_ld16(tl_addr + (uint32_t)(tb * 64), acc[0]);
-                tmem_ld16(tl_addr + (uint32_t)(tb * 64 + 16), acc[1]);
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[tb]);
-                // this warp's scales and bias terms
                 const uint8_t* slot = base + s * kSlot;
-                const float4* sx4 = reinterpret_cast<const float4*>(slot + kSlotAux);
-                const int4* bias4 = reinterpret_cast<const int4*>(slot + kSlotAux + 128);
+                for (int h = 0; h < nh; ++h) {
+                uint32_t acc[2][16];  // columns past 2 x batch hold stale values, never stored
+                tmem_ld16(tl_addr + (uint32_t)((tb * kGU + h) * 64), acc[0]);
+                tmem_ld16(tl_addr + (uint32_t)((tb * kGU + h) * 64 + 16), acc[1]);
+                tmem_wait_ld();
+                if (h == nh - 1) {  // every accumulator of the unit read
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[tb]);
+                }
+                // this warp's scales and bias terms of group 2 g + h
+                const int aux = (h ? kSlotAct1 : kSlotAct0) + kActTile;
+                const float4* sx4 = reinterpret_cast<const float4*>(slot + aux);
+                const int4* bias4 = reinterpret_cast<const int4*>(slot + aux + 128);
+                const int gg = 2 * g + h;
                 const float sw = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
-                    slot + kSlotS + (row >> 4) * 128 + (r16 & 7) * 16 + (g & 3) * 4 + (r16 >> 3) * 2));
+                    slot + kSlotS + (row >> 4) * 128 + (r16 & 7) * 16 + (gg & 3) * 4 + (r16 >> 3) * 2));
                 float sxc[2][8];
                 int bias[2][16];
 #pragma unroll
@@ -360,6 +394,7 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
                         }
                     }
                 }
+                }
                 // the slot goes back to the copies only after the values read
                 // from it have been used: releasing with those shared-memory
                 // loads still outstanding let the next copy overwrite them
@@ -367,8 +402,8 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
                 if (lane == 0) mbar_arrive(&raw_empty[s]);
             }
             // end of this CTA's piece of tile tl (the same iterations in every warp)
-            if (g == G - 1 || i == nmine - 1) {
-                const bool whole = piece_g0 == 0 && g == G - 1;
+            if (g == G2 - 1 || i == nmine - 1) {
+                const bool whole = piece_g0 == 0 && g == G2 - 1;
                 bool fin = whole && ok;
                 if (!whole) {
                     const int k = (tl0 == tl) ? 0 : 1;  // first or last piece of this CTA
@@ -389,7 +424,7 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
                         int last = 0;
                         if (!s_fail) {
                             const int n = g - piece_g0 + 1;
-                            last = (atomicAdd(t.ticket + tl, n) + n == G) ? 1 : 0;
+                            last = (atomicAdd(t.ticket + tl, n) + n == G2) ? 1 : 0;
                         }
                         s_last = last;
                     }
@@ -398,14 +433,14 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
                     if (fin) {
                         __threadfence();
                         // the tile's pieces in CTA order
-                        const int c0 = unit_owner((int64_t)tl * G, U, P);
-                        const int c1 = unit_owner((int64_t)tl * G + G - 1, U, P);
+                        const int c0 = unit_owner((int64_t)tl * G2, U, P);
+                        const int c1 = unit_owner((int64_t)tl * G2 + G2 - 1, U, P);
 #pragma unroll
                         for (int b = 0; b < kHalfSeq; ++b) y[b] = 0.f;
                         // vector loads, all of a piece in flight together
 #pragma unroll 2
                         for (int c = c0; c <= c1; ++c) {
-                            const int kk = (unit_begin(c, U, P) / G == tl) ? 0 : 1;
+                            const int kk = (unit_begin(c, U, P) / G2 == tl) ? 0 : 1;
                             const float4* src = reinterpret_cast<const float4*>(
                                 t.partial + (((size_t)c * 2 + kk) * kTM + row) * kMaxSeq + kHalfSeq * hcol);
                             float4 v[kHalfSeq / 4];
@@ -489,7 +524,7 @@ template <int EPI>
 int launch_tc(const ForgeGemvArgs& a, const TcArgs& t, cudaStream_t stream, int grid) {
     CUtensorMap tw, ts;
     const int64_t blocks = a.N / 16;
-    if (map_rows(&tw, a.w, (int64_t)a.K * 8, blocks, 128) ||
+    if (map_rows(&tw, a.w, (int64_t)a.K * 8, blocks, t.wbox) ||
         map_rows(&ts, a.s, q4_groups4(a.K, 128) * 128, blocks, 16))
         return -1;
     cudaLaunchConfig_t cfg = {};
@@ -558,7 +593,8 @@ int forge_gemv_tc_launch(const ForgeGemvArgs& a, void* scratch, cudaStream_t str
     t.ticket = reinterpret_cast<int*>(sc);
     t.partial = reinterpret_cast<float*>(sc + forge_gemv_scratch_header());
     t.npad = ((2 * a.batch + 15) / 16) * 16;
-    const int64_t U = (int64_t)T * (a.K / 128);
+    t.wbox = a.K >= 256 ? 256 : 128;  // two groups a unit (one when K has a single group)
+    const int64_t U = (int64_t)T * ((a.K / 128 + kGU - 1) / kGU);
     int grid = forge_sm_count();
     if (grid > kMaxGrid) grid = kMaxGrid;
     if (grid > U) grid = (int)U;

@@ -131,7 +131,10 @@ def test_flash_decode(forge, oracle, cuda, B, H, Hkv, hd, lmax, pos):
         assert np.abs(got - ref).max() < 2e-5 * max(1.0, np.abs(ref).max()), np.abs(got - ref).max()
 
 
-@pytest.mark.parametrize("N,K", [(4096, 4096), (4096, 11008), (22016, 4096), (1376, 4096), (48, 256)])
+# K 384 / 1408 / 128: odd group counts and a single group (the tensor-core
+# path works on pairs of groups)
+@pytest.mark.parametrize("N,K", [(4096, 4096), (4096, 11008), (22016, 4096), (1376, 4096), (48, 256), (1024, 384),
+                                 (4096, 1408), (48, 128)])
 @pytest.mark.parametrize("batch", [5, 8, 17, 32, 37])
 def test_gemv_int4_batched_matches_small_batch(forge, oracle, cuda, N, K, batch):
     """Above 4 sequences the int4 GEMV streams the weights once for up to 32
