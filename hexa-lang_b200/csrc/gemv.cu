@@ -63,18 +63,21 @@ __device__ __forceinline__ uint32_t sys_load_acquire(const uint32_t* p) {
     return v;
 }
 
-// FORGE_EPI_RESID_TP, run by warp 0 of the CTA that finished 16-row tile u
-// (lane (p, b) for p < 8 and b < batch <= 4 holds rows p / p+8 of sequence b):
-// the tile's share goes into this rank's slot on every rank (rank 0's share
-// carries the residual, the additions of its FORGE_EPI_RESID), a flag per
-// (rank, tile) on every rank says it landed, and once every rank's flag for
-// this tile is in, the slots are summed in rank order — the additions of
-// the separate all-reduce, so the result is the same — into the residual.
-// The per-tile call counter selects one of two buffer generations: a rank
-// can be at most one call ahead of another on a tile, because finishing a
-// tile waits for every rank's share of it. Waits are bounded (error word).
-__device__ __noinline__ void tp_resid_epilogue(const ForgeGemvArgs& a, int u, int p, int b, bool act, float ylo,
-                                               float yhi) {
+// FORGE_EPI_RESID_TP, run by warp 0 of a CTA (lane (p, b) for p < 8 and
+// b < batch <= 4 holds rows p / p+8 of sequence b of 16-row tile u).
+// tp_resid_post, when the CTA has reduced tile u: the tile's share goes into
+// this rank's slot on every rank (rank 0's share carries the residual, the
+// additions of its FORGE_EPI_RESID) and a flag per (rank, tile) on every rank
+// says it landed. tp_resid_finish, once the CTA has posted all its tiles:
+// when every rank's flag for the tile is in, the slots are summed in rank
+// order — the additions of the separate all-reduce, so the result is the
+// same — into the residual. Posting first and waiting at the end keeps the
+// NVLink round trip off the CTA's remaining units. The per-tile call counter
+// selects one of two buffer generations: a rank can be at most one call
+// ahead of another on a tile, because its launch ends only after every
+// rank's share of its tiles arrived. Waits are bounded (error word).
+__device__ __noinline__ void tp_resid_post(const ForgeGemvArgs& a, int u, int p, int b, bool act, float ylo,
+                                           float yhi) {
     const ForgeTpFusedDev& f = *a.tpf;
     const int lane = threadIdx.x & 31;
     const int T = f.T, rank = f.rank;
@@ -98,6 +101,17 @@ __device__ __noinline__ void tp_resid_epilogue(const ForgeGemvArgs& a, int u, in
     }
     __syncwarp();
     if (lane < T) sys_store_release(f.flag[lane] + ((size_t)gen * T + rank) * f.max_tiles + u, ep);
+}
+
+__device__ __noinline__ void tp_resid_finish(const ForgeGemvArgs& a, int u, int p, int b, bool act) {
+    const ForgeTpFusedDev& f = *a.tpf;
+    const int lane = threadIdx.x & 31;
+    const int T = f.T, rank = f.rank;
+    uint32_t ep = 0;
+    if (lane == 0) ep = f.tile_epoch[u];  // this call's, set by tp_resid_post
+    ep = __shfl_sync(0xffffffffu, ep, 0);
+    const int gen = ep & 1;
+    const size_t i0 = (size_t)b * a.y_stride + (size_t)u * 16 + p, i1 = i0 + 8;
     bool ok = true;
     if (lane < T) {
         const volatile uint32_t* fl = f.flag[rank] + ((size_t)gen * T + lane) * f.max_tiles + u;
@@ -321,10 +335,14 @@ __global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const 
                 }
             }
             if (EPI == FORGE_EPI_RESID_TP)
-                tp_resid_epilogue(a, u, p, b, act, ylo, yhi);
+                tp_resid_post(a, u, p, b, act, ylo, yhi);
             else
                 epilogue<EPI>(a, u, p, b, ylo, yhi, best);
         }
+    }
+    if (EPI == FORGE_EPI_RESID_TP && warp == 0 && __all_sync(0xffffffffu, ok)) {
+        const int tid = threadIdx.x;
+        for (int u = blockIdx.x; u < units; u += gridDim.x) tp_resid_finish(a, u, tid & 7, tid >> 3, tid < 8 * a.batch);
     }
 
     if (EPI == FORGE_EPI_LOGITS && warp < 2) {
