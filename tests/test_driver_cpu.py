@@ -1,0 +1,38 @@
+"""The command-line driver (hexa-lang_b200/driver/forge_generate.c) without a
+GPU: it builds against the public headers only, prints its usage, rejects bad
+usage with status 2, and reports the library's error with status 1 when no
+device is there (no compute runs)."""
+import os
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+BIN = os.path.join(ROOT, "hexa-lang_b200", "forge_generate")
+MODEL = ["--layers", "1", "--dim", "256", "--heads", "4", "--kv-heads", "2", "--head-dim", "64", "--ffn", "512",
+         "--vocab", "1000"]
+
+
+@pytest.fixture(scope="module")
+def driver(forge):
+    if not os.path.exists(BIN):
+        subprocess.run(["make", "-C", os.path.join(ROOT, "hexa-lang_b200", "csrc"), "../forge_generate"], check=True,
+                       capture_output=True)
+    return BIN
+
+
+def test_usage(driver):
+    r = subprocess.run([driver, "--help"], capture_output=True, text=True)
+    assert r.returncode == 0 and r.stdout.startswith("usage: forge_generate")
+    for bad in ([], MODEL, MODEL + ["--gen", "4"], MODEL + ["--synthetic", "1", "--gen", "4"],
+                MODEL + ["--bogus", "--synthetic", "1", "--gen", "4", "5"]):
+        r = subprocess.run([driver] + bad, capture_output=True, text=True)
+        assert r.returncode == 2, (bad, r.stderr)
+
+
+def test_library_error_without_gpu(driver):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    r = subprocess.run([driver] + MODEL + ["--synthetic", "1", "--gen", "4", "5", "6"], capture_output=True, text=True)
+    assert r.returncode == 1 and "forge_generate: create:" in r.stderr and r.stdout == ""
