@@ -14,6 +14,12 @@
 // heads of its KV head, so each K/V byte is read once per step. The last CTA
 // of a (b, kv head) to finish (atomic ticket) merges the splits — no extra
 // launch. Scores and probabilities stay fp32; K/V are widened from bf16.
+//
+// Paged mode (the page pool of self/alloc/paged_kv.hexa): K/V rows come from
+// pages of page_tokens rows through a per-sequence page table; a key tile
+// is gathered with one bulk copy per page segment into the same shared
+// layout, so the arithmetic — and the result, bit for bit — is that of the
+// contiguous cache. Page ids are checked against the pool before any copy.
 #include <cmath>
 #include "common.cuh"
 #include "forge_internal.h"
@@ -34,7 +40,7 @@ constexpr int smem_bytes() {
     return kStages * stage_bytes<HD>() + G * HD * 4 + G * kTile * 4 + 3 * G * 4 + kStages * 8 + 16;
 }
 
-template <int HD, int G>
+template <int HD, int G, bool PAGED>
 __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint16_t* kv = reinterpret_cast<uint16_t*>(smem);
@@ -62,8 +68,13 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
     const int n = max(0, j1 - j0);
     const int ntiles = (n + kTile - 1) / kTile;
     const size_t slab = ((size_t)b * a.Hkv + kvh) * a.lmax * HD;
-    const uint16_t* K = a.kc + slab;
-    const uint16_t* V = a.vc + slab;
+    constexpr bool paged = PAGED;
+    const int32_t* ptab = paged ? a.table + (size_t)b * a.max_pages : nullptr;
+    // row r of this (sequence, kv head)
+    auto row = [&](const uint16_t* base, int r) -> const uint16_t* {
+        if (!paged) return base + slab + (size_t)r * HD;
+        return base + (((size_t)ptab[r / a.page_tokens] * a.Hkv + kvh) * a.page_tokens + r % a.page_tokens) * HD;
+    };
 
     auto issue = [&](int i) {
         const int s = i % kStages;
@@ -73,8 +84,17 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
         if (rows > 0) {
             const uint32_t bytes = (uint32_t)rows * HD * 2;
             mbar_arrive_expect_tx(&full[s], 2 * bytes);
-            bulk_g2s(dst, K + (size_t)t0 * HD, bytes, &full[s]);
-            bulk_g2s(dst + kTile * HD, V + (size_t)t0 * HD, bytes, &full[s]);
+            if (!paged) {
+                bulk_g2s(dst, row(a.kc, t0), bytes, &full[s]);
+                bulk_g2s(dst + kTile * HD, row(a.vc, t0), bytes, &full[s]);
+            } else {
+                for (int r = t0; r < t0 + rows;) {  // one copy per page segment
+                    const int seg = min(t0 + rows - r, a.page_tokens - r % a.page_tokens);
+                    bulk_g2s(dst + (size_t)(r - t0) * HD, row(a.kc, r), (uint32_t)seg * HD * 2, &full[s]);
+                    bulk_g2s(dst + (size_t)(kTile + r - t0) * HD, row(a.vc, r), (uint32_t)seg * HD * 2, &full[s]);
+                    r += seg;
+                }
+            }
         } else {
             mbar_arrive(&full[s]);
         }
@@ -83,7 +103,19 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
         for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
         fence_mbar_init();
     }
-    __syncthreads();
+    // every page this sequence reads must be a page of the pool
+    if (paged) {
+        bool bad_page = false;
+        if (!bad)
+            for (int pg = tid; pg <= P / a.page_tokens; pg += kThreads)
+                bad_page |= (unsigned)ptab[pg] >= (unsigned)a.num_pages;
+        if (__syncthreads_or(bad_page)) {
+            if (tid == 0) atomicOr(a.err, FORGE_DEVERR_BAD_INDEX);
+            return;
+        }
+    } else {
+        __syncthreads();
+    }
     if (tid == 0 && !bad)
         for (int i = 0; i < kStages && i < ntiles; ++i) issue(i);
     pdl_trigger();
@@ -116,8 +148,8 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
             // the newest row comes straight from global memory
             uint16_t* kd = const_cast<uint16_t*>(Ks) + (size_t)(nt - 1) * HD;
             uint16_t* vd = const_cast<uint16_t*>(Vs) + (size_t)(nt - 1) * HD;
-            if (tid < HD / 8) reinterpret_cast<uint4*>(kd)[tid] = reinterpret_cast<const uint4*>(K + (size_t)P * HD)[tid];
-            else if (tid < HD / 4) reinterpret_cast<uint4*>(vd)[tid - HD / 8] = reinterpret_cast<const uint4*>(V + (size_t)P * HD)[tid - HD / 8];
+            if (tid < HD / 8) reinterpret_cast<uint4*>(kd)[tid] = reinterpret_cast<const uint4*>(row(a.kc, P))[tid];
+            else if (tid < HD / 4) reinterpret_cast<uint4*>(vd)[tid - HD / 8] = reinterpret_cast<const uint4*>(row(a.vc, P))[tid - HD / 8];
         }
         __syncthreads();
         // ---- scores: two threads per key, each half a row; chunk order rotated by
@@ -265,7 +297,7 @@ template <int HD, int G>
 int launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl) {
     constexpr int smem = smem_bytes<HD, G>();
     static_assert(kWarps * G * HD * 4 <= kStages * stage_bytes<HD>(), "partial-O reduction must fit the tile buffers");
-    auto kern = k_flash_decode<HD, G>;
+    auto kern = a.table ? k_flash_decode<HD, G, true> : k_flash_decode<HD, G, false>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit, a.Hkv, a.B);
     cfg.blockDim = dim3(kThreads);
@@ -294,7 +326,10 @@ int launch_g(const ForgeAttnArgs& a, cudaStream_t s, bool pdl) {
 
 template <int HD, int G>
 int configure_one() {
-    cudaError_t e = cudaFuncSetAttribute(k_flash_decode<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(k_flash_decode<HD, G, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_flash_decode<HD, G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     return e == cudaSuccess ? 0 : forge_fail(-1, "flash-decode attr: %s", cudaGetErrorString(e));
 }
 }  // namespace
@@ -341,6 +376,9 @@ int forge_attn_launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl) {
     if (!a.q || !a.kc || !a.vc || !a.pos || !a.partial || !a.counters || !a.out || a.B <= 0 ||
         a.Hkv <= 0 || a.H % a.Hkv || a.nsplit <= 0 || a.lmax <= 0)
         return forge_fail(-1, "flash-decode: bad args");
+    if (a.table && (a.page_tokens <= 0 || a.max_pages <= 0 || a.num_pages <= 0 ||
+                    (int64_t)a.max_pages * a.page_tokens != a.lmax))
+        return forge_fail(-1, "flash-decode: bad page geometry");
     if (a.hd == 128) return launch_g<128>(a, stream, pdl);
     if (a.hd == 64) return launch_g<64>(a, stream, pdl);
     return forge_fail(-1, "flash-decode: head_dim must be 64 or 128 (got %d)", a.hd);

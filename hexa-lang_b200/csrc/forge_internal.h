@@ -110,6 +110,11 @@ struct ForgeAttnArgs {
     uint32_t* counters;    // [B][Hkv] zero-initialised merge counters
     float* out;            // [B][H*hd] fp32 context
     uint32_t* err;
+    // Paged cache (table != nullptr): kc / vc are page pools
+    // [num_pages][Hkv][page_tokens][hd]; row r of sequence b lives on page
+    // table[b * max_pages + r / page_tokens]; lmax = max_pages * page_tokens.
+    const int32_t* table;
+    int32_t max_pages, page_tokens, num_pages;
 };
 int forge_attn_launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl);
 int forge_attn_configure();

@@ -5,6 +5,7 @@
 // 16-byte device error word per device, created on first use.
 #include <mutex>
 #include "forge_internal.h"
+#include "../../include/forge_paged_kv.h"
 #include "../../include/forge_b200.h"
 
 namespace {
@@ -101,6 +102,27 @@ FORGE_API int forge_flash_decode(const float* q, const uint16_t* kc, const uint1
     ForgeAttnArgs a{};
     a.q = q; a.kc = kc; a.vc = vc; a.pos = pos; a.B = B; a.H = H; a.Hkv = Hkv; a.hd = hd; a.lmax = lmax;
     a.nsplit = forge_attn_pick_splits(B, Hkv, lmax);
+    const int64_t counters = ((int64_t)B * Hkv * 4 + 255) / 256 * 256;
+    a.counters = (uint32_t*)workspace;
+    a.partial = (float*)((char*)workspace + counters);
+    a.out = out; a.err = err;
+    return forge_attn_launch(a, (cudaStream_t)stream, false) ? FORGE_INVALID_ARGS : 0;
+}
+
+FORGE_API int forge_flash_decode_paged(const float* q, const uint16_t* k_pool, const uint16_t* v_pool, int num_pages,
+                                       const int32_t* block_table, int max_pages, int page_tokens, const int32_t* pos,
+                                       int B, int H, int Hkv, int hd, float* out, void* workspace, void* stream) {
+    if (!q || !k_pool || !v_pool || !block_table || !pos || !out || !workspace || B <= 0 || H <= 0 || Hkv <= 0 ||
+        num_pages <= 0 || max_pages <= 0 || page_tokens <= 0 || (int64_t)max_pages * page_tokens > (1 << 30))
+        return forge_fail(FORGE_INVALID_ARGS, "forge_flash_decode_paged: bad args");
+    uint32_t* err = err_word();
+    if (!err) return forge_fail(-1, "forge_flash_decode_paged: no device");
+    if (forge_attn_configure()) return -1;
+    ForgeAttnArgs a{};
+    a.q = q; a.kc = k_pool; a.vc = v_pool; a.pos = pos; a.B = B; a.H = H; a.Hkv = Hkv; a.hd = hd;
+    a.lmax = max_pages * page_tokens;
+    a.table = block_table; a.max_pages = max_pages; a.page_tokens = page_tokens; a.num_pages = num_pages;
+    a.nsplit = forge_attn_pick_splits(B, Hkv, a.lmax);
     const int64_t counters = ((int64_t)B * Hkv * 4 + 255) / 256 * 256;
     a.counters = (uint32_t*)workspace;
     a.partial = (float*)((char*)workspace + counters);

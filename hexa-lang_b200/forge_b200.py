@@ -49,6 +49,12 @@ ST_DTYPES = ["BOOL", "U8", "I8", "I16", "U16", "F16", "BF16", "I32", "U32", "F32
 FORGE_ST_NOT_FOUND = -6
 
 
+class ForgePagedKvStats(C.Structure):
+    _fields_ = [("num_pages", C.c_int32), ("page_tokens", C.c_int32), ("head_dim", C.c_int32),
+                ("used_pages", C.c_int32), ("free_pages", C.c_int32), ("seq_count", C.c_int32),
+                ("stat_alloc", C.c_int64), ("stat_release", C.c_int64), ("stat_reuse", C.c_int64)]
+
+
 class ForgeShapeInfo(C.Structure):
     _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("batch", C.c_int64)]
 
@@ -204,6 +210,18 @@ def lib() -> C.CDLL:
             "forge_api_version_v2": (C.c_uint32, []),
             "forge_sample": (i32, [vp, i64, i32, i32, C.c_double, i32, C.c_double, vp, vp, vp, vp]),
             "forge_b200_decode_step_sampled": (i32, [vp, i32, vp, vp, C.c_double, i32, C.c_double, vp]),
+            "forge_paged_kv_create": (i32, [i32, i32, i32, C.POINTER(vp)]),
+            "forge_paged_kv_destroy": (None, [vp]),
+            "forge_paged_kv_free_count": (i32, [vp]),
+            "forge_paged_kv_used_count": (i32, [vp]),
+            "forge_paged_kv_seq_count": (i32, [vp]),
+            "forge_paged_kv_register_seq": (i32, [vp, i64]),
+            "forge_paged_kv_alloc_page": (i32, [vp, i64]),
+            "forge_paged_kv_release_page": (i32, [vp, i64, i32]),
+            "forge_paged_kv_release_seq": (i32, [vp, i64]),
+            "forge_paged_kv_page_table": (i32, [vp, i64, vp, i32]),
+            "forge_paged_kv_stats": (i32, [vp, C.POINTER(ForgePagedKvStats)]),
+            "forge_flash_decode_paged": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, vp, vp, vp]),
             "forge_st_open": (i32, [C.c_char_p, C.POINTER(vp)]),
             "forge_st_close": (i32, [vp]),
             "forge_st_header": (vp, [vp, C.POINTER(C.c_int64)]),
@@ -248,6 +266,58 @@ def _ptr(a) -> int:
     if hasattr(a, "data_ptr"):
         return a.data_ptr()
     return a.ctypes.data
+
+
+class PagedKv:
+    """Host page allocator of the paged KV cache (forge_paged_kv_*; the
+    contract of self/alloc/paged_kv.hexa)."""
+
+    def __init__(self, num_pages=64, page_tokens=16, head_dim=64):
+        h = C.c_void_p()
+        check(lib().forge_paged_kv_create(num_pages, page_tokens, head_dim, C.byref(h)), "forge_paged_kv_create")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().forge_paged_kv_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    free_count = property(lambda self: lib().forge_paged_kv_free_count(self.h))
+    used_count = property(lambda self: lib().forge_paged_kv_used_count(self.h))
+    seq_count = property(lambda self: lib().forge_paged_kv_seq_count(self.h))
+
+    def register_seq(self, seq):
+        check(lib().forge_paged_kv_register_seq(self.h, seq), "register_seq")
+
+    def alloc_page(self, seq):
+        return lib().forge_paged_kv_alloc_page(self.h, seq)
+
+    def release_page(self, seq, page_id):
+        return lib().forge_paged_kv_release_page(self.h, seq, page_id) == 0
+
+    def release_seq(self, seq):
+        return lib().forge_paged_kv_release_seq(self.h, seq) == 0
+
+    def page_table(self, seq):
+        import numpy as np
+        n = lib().forge_paged_kv_page_table(self.h, seq, None, 0)
+        out = np.zeros(n, np.int32)
+        lib().forge_paged_kv_page_table(self.h, seq, out.ctypes.data if n else None, n)
+        return out.tolist()
+
+    def seq_pages(self, seq):
+        return lib().forge_paged_kv_page_table(self.h, seq, None, 0)
+
+    def stats(self):
+        s = ForgePagedKvStats()
+        check(lib().forge_paged_kv_stats(self.h, C.byref(s)), "stats")
+        return s
 
 
 class Safetensors:
