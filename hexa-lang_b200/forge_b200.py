@@ -55,6 +55,10 @@ class ForgePagedKvStats(C.Structure):
                 ("stat_alloc", C.c_int64), ("stat_release", C.c_int64), ("stat_reuse", C.c_int64)]
 
 
+class ForgeClmBlock(C.Structure):
+    _fields_ = [("cout", C.c_int64), ("rest", C.c_int64), ("offset", C.c_int64)]
+
+
 class ForgeShapeInfo(C.Structure):
     _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("batch", C.c_int64)]
 
@@ -222,6 +226,12 @@ def lib() -> C.CDLL:
             "forge_paged_kv_page_table": (i32, [vp, i64, vp, i32]),
             "forge_paged_kv_stats": (i32, [vp, C.POINTER(ForgePagedKvStats)]),
             "forge_flash_decode_paged": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, vp, vp, vp]),
+            "forge_clm_open": (i32, [C.c_char_p, C.POINTER(vp)]),
+            "forge_clm_close": (None, [vp]),
+            "forge_clm_count": (i32, [vp]),
+            "forge_clm_block": (i32, [vp, i32, C.POINTER(ForgeClmBlock)]),
+            "forge_clm_block_levels": (i32, [vp, i32, vp, vp]),
+            "forge_clm_block_to_q4g128": (i32, [vp, i32, vp, vp]),
             "forge_st_open": (i32, [C.c_char_p, C.POINTER(vp)]),
             "forge_st_close": (i32, [vp]),
             "forge_st_header": (vp, [vp, C.POINTER(C.c_int64)]),
@@ -318,6 +328,52 @@ class PagedKv:
         s = ForgePagedKvStats()
         check(lib().forge_paged_kv_stats(self.h, C.byref(s)), "stats")
         return s
+
+
+class Clm:
+    """A .clm int4 checkpoint (forge_clm_*; stdlib/flame/clm_ckpt.hexa)."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        check(lib().forge_clm_open(os.fsencode(path), C.byref(h)), f"forge_clm_open({path})")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().forge_clm_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __len__(self):
+        return lib().forge_clm_count(self.h)
+
+    def block(self, i):
+        b = ForgeClmBlock()
+        check(lib().forge_clm_block(self.h, i, C.byref(b)), "forge_clm_block")
+        return b
+
+    def levels(self, i):
+        """(q int8 [Cout][rest], scale fp32 [Cout]) as stored."""
+        import numpy as np
+        b = self.block(i)
+        q = np.empty((b.cout, b.rest), np.int8)
+        s = np.empty(b.cout, np.float32)
+        check(lib().forge_clm_block_levels(self.h, i, q.ctypes.data, s.ctypes.data), "forge_clm_block_levels")
+        return q, s
+
+    def to_q4g128(self, i):
+        """(codes u8 [Cout][rest], bf16 scales [Cout][rest / 128]) of the group-128 format."""
+        import numpy as np
+        b = self.block(i)
+        codes = np.empty((b.cout, b.rest), np.uint8)
+        sc = np.empty((b.cout, b.rest // 128), np.uint16)
+        check(lib().forge_clm_block_to_q4g128(self.h, i, codes.ctypes.data, sc.ctypes.data), "forge_clm_block_to_q4g128")
+        return codes, sc
 
 
 class Safetensors:
