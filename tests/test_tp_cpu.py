@@ -1,7 +1,7 @@
 """Host side of the tensor-parallel mode without a GPU: the shard plan every
 rank derives on its own (FFN in whole 128-row groups for int4 — 7B's 11008 =
-86 groups and 13B's 13824 = 108 groups do not divide by 8, SURVEY-style
-uneven slices — heads evenly, vocabulary in equal 16-row slices), and its
+86 groups and 13B's 13824 = 108 groups do not divide by 8, so the slices
+are uneven, the first ranks taking one group more — heads evenly, vocabulary in equal 16-row slices), and its
 agreement across processes: two `gloo` ranks share rank 0's NCCL unique id
 the way bench.py does and check that their shards tile the model exactly."""
 import os
