@@ -963,6 +963,63 @@ FORGE_API int forge_b200_decode_step_sampled(ForgeB200* h, int batch, const int3
     return read_err(h);
 }
 
+namespace {
+int64_t packed_i64(const void* args, int off) {
+    int64_t v;
+    memcpy(&v, static_cast<const char*>(args) + off, 8);
+    return v;
+}
+double packed_f64(const void* args, int off) {
+    double v;
+    memcpy(&v, static_cast<const char*>(args) + off, 8);
+    return v;
+}
+bool fits_i32(int64_t v) { return v >= INT32_MIN && v <= INT32_MAX; }
+}  // namespace
+
+FORGE_API int forge_b200_desc_from_packed(const void* args, ForgeModelDesc* d) {
+    if (!args || !d) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_desc_from_packed: null argument");
+    memset(d, 0, sizeof *d);
+    int32_t* ints[] = {&d->n_layer, &d->d_model, &d->n_head, &d->n_kv_head, &d->head_dim, &d->ffn, &d->vocab};
+    for (int i = 0; i < 7; ++i) {
+        const int64_t v = packed_i64(args, 8 * i);
+        if (!fits_i32(v)) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_desc_from_packed: field %d out of range", i);
+        *ints[i] = (int32_t)v;
+    }
+    d->rms_eps = (float)packed_f64(args, 56);
+    d->rope_theta = (float)packed_f64(args, 64);
+    int32_t* rest[] = {&d->weight_kind, &d->tied_head, &d->max_batch, &d->max_ctx, &d->act_mode};
+    for (int i = 0; i < 5; ++i) {
+        const int64_t v = packed_i64(args, 72 + 8 * i);
+        if (!fits_i32(v)) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_desc_from_packed: field %d out of range", 9 + i);
+        *rest[i] = (int32_t)v;
+    }
+    d->tp_rank = 0;
+    d->tp_size = 1;
+    return 0;
+}
+
+FORGE_API int forge_b200_create_packed(const void* args) {
+    ForgeModelDesc d;
+    if (forge_b200_desc_from_packed(args, &d)) return FORGE_INVALID_ARGS;
+    const int64_t device = packed_i64(args, 112);
+    ForgeB200** out = reinterpret_cast<ForgeB200**>(static_cast<intptr_t>(packed_i64(args, 120)));
+    if (!out || !fits_i32(device)) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create_packed: bad device or result address");
+    return forge_b200_create(&d, (int)device, out);
+}
+
+FORGE_API int forge_b200_decode_step_sampled_packed(const void* args) {
+    if (!args) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_decode_step_sampled_packed: null argument");
+    auto ptr = [&](int off) { return reinterpret_cast<void*>(static_cast<intptr_t>(packed_i64(args, off))); };
+    const int64_t batch = packed_i64(args, 8), top_k = packed_i64(args, 40);
+    if (!fits_i32(batch) || !fits_i32(top_k))
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_decode_step_sampled_packed: batch or top_k out of range");
+    return forge_b200_decode_step_sampled(static_cast<ForgeB200*>(ptr(0)), (int)batch,
+                                          static_cast<const int32_t*>(ptr(16)), static_cast<int32_t*>(ptr(24)),
+                                          packed_f64(args, 32), (int)top_k, packed_f64(args, 48),
+                                          static_cast<int64_t*>(ptr(56)));
+}
+
 FORGE_API int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps) {
     if (int rc = check_ready(h, batch)) return rc;
     for (int i = 0; i < n_steps; ++i)

@@ -214,6 +214,9 @@ def lib() -> C.CDLL:
             "forge_api_version_v2": (C.c_uint32, []),
             "forge_sample": (i32, [vp, i64, i32, i32, C.c_double, i32, C.c_double, vp, vp, vp, vp]),
             "forge_b200_decode_step_sampled": (i32, [vp, i32, vp, vp, C.c_double, i32, C.c_double, vp]),
+            "forge_b200_desc_from_packed": (i32, [vp, C.POINTER(ForgeModelDesc)]),
+            "forge_b200_create_packed": (i32, [vp]),
+            "forge_b200_decode_step_sampled_packed": (i32, [vp]),
             "forge_paged_kv_create": (i32, [i32, i32, i32, C.POINTER(vp)]),
             "forge_paged_kv_destroy": (None, [vp]),
             "forge_paged_kv_free_count": (i32, [vp]),

@@ -153,6 +153,22 @@ int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tokens, int32
  * (gpu_sampler_set_seed) and is advanced. Single-GPU handles; synchronous. */
 int forge_b200_decode_step_sampled(ForgeB200* h, int batch, const int32_t* tokens, int32_t* next_tokens,
                                    double temperature, int top_k, double top_p, int64_t* rng_state);
+/* Packed-argument forms for callers whose FFI passes at most six integer
+ * arguments and writes 8-byte fields (the hexa interpreter's 6-argument
+ * host call; the pattern of hxflash_attn_fwd_packed, self/ml/hxflash.hexa:40-62):
+ * one pointer to a block of 8-byte little-endian fields, int64 unless marked
+ * f64, at these byte offsets.
+ *   create:  0 n_layer  8 d_model  16 n_head  24 n_kv_head  32 head_dim
+ *            40 ffn  48 vocab  56 rms_eps (f64)  64 rope_theta (f64)
+ *            72 weight_kind  80 tied_head  88 max_batch  96 max_ctx
+ *            104 act_mode  112 device  120 address of the ForgeB200* result
+ *            (128 bytes; tensor parallel stays forge_b200_create_tp)
+ *   sampled step: 0 handle  8 batch  16 tokens  24 next_tokens
+ *            32 temperature (f64)  40 top_k  48 top_p (f64)  56 rng_state
+ *            (64 bytes) */
+int forge_b200_desc_from_packed(const void* args, ForgeModelDesc* out);
+int forge_b200_create_packed(const void* args);
+int forge_b200_decode_step_sampled_packed(const void* args);
 /* n_steps device-resident greedy steps (each feeds its argmax to the next);
  * asynchronous on the handle's stream. */
 int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps);
