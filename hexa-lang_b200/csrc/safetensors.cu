@@ -528,28 +528,81 @@ FORGE_API int forge_st_tensor_to_f32(const ForgeStTensor* v, float* out, int64_t
 // ---- Llama-layout loader ---------------------------------------------------
 
 namespace {
+bool is_float_dtype(int dt) {
+    return dt == FORGE_ST_BF16 || dt == FORGE_ST_F16 || dt == FORGE_ST_F32 || dt == FORGE_ST_F64;
+}
+
 struct Shards {
     std::vector<ForgeSafetensors*> files;
     std::unordered_map<std::string, ForgeStTensor> byname;
     ~Shards() {
         for (ForgeSafetensors* f : files) forge_st_close(f);
     }
+    int open(const char* who, int n_files, const char* const* paths) {
+        if (n_files <= 0 || !paths) return forge_fail(FORGE_INVALID_ARGS, "%s: no files", who);
+        for (int i = 0; i < n_files; ++i) {
+            ForgeSafetensors* st = nullptr;
+            if (forge_st_open(paths[i], &st)) return FORGE_INVALID_ARGS;
+            files.push_back(st);
+            for (int t = 0; t < forge_st_count(st); ++t) {
+                ForgeStTensor v;
+                forge_st_tensor_at(st, t, &v);
+                if (!byname.emplace(v.name, v).second)
+                    return forge_fail(FORGE_INVALID_ARGS, "%s: %s appears in two files", who, v.name);
+            }
+        }
+        return 0;
+    }
 };
 
-// Tensor `name` with the given 1-D or 2-D shape, converted into `out`.
-int fetch(const Shards& s, const std::string& name, int64_t rows, int64_t cols, std::vector<uint16_t>* bf,
-          std::vector<float>* f32) {
-    auto it = s.byname.find(name);
-    if (it == s.byname.end()) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_load_safetensors: %s missing", name.c_str());
+// One tensor the loader reads: its name and its 1-D (cols 0) or 2-D shape.
+struct Want {
+    std::string name;
+    int64_t rows, cols;
+};
+
+// Every tensor of the Llama layout for the description, in load order:
+// per layer the seven projections then the two norms, then the embedding,
+// the final norm and (untied) the head.
+std::vector<Want> llama_tensors(const ForgeModelDesc& d) {
+    const int64_t D = d.d_model, Q = (int64_t)d.n_head * d.head_dim, KV = (int64_t)d.n_kv_head * d.head_dim;
+    const int64_t F = d.ffn, V = d.vocab;
+    static const char* kProj[7] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                                   "mlp.gate_proj",    "mlp.up_proj",      "mlp.down_proj"};
+    const int64_t rows[7] = {Q, KV, KV, D, F, F, D}, cols[7] = {D, D, D, Q, D, D, F};
+    std::vector<Want> w;
+    for (int l = 0; l < d.n_layer; ++l) {
+        const std::string pre = "model.layers." + std::to_string(l) + ".";
+        for (int i = 0; i < 7; ++i) w.push_back({pre + kProj[i] + ".weight", rows[i], cols[i]});
+        w.push_back({pre + "input_layernorm.weight", D, 0});
+        w.push_back({pre + "post_attention_layernorm.weight", D, 0});
+    }
+    w.push_back({"model.embed_tokens.weight", V, D});
+    w.push_back({"model.norm.weight", D, 0});
+    if (!d.tied_head) w.push_back({"lm_head.weight", V, D});
+    return w;
+}
+
+int check_one(const Shards& s, const char* who, const Want& w) {
+    auto it = s.byname.find(w.name);
+    if (it == s.byname.end()) return forge_fail(FORGE_INVALID_ARGS, "%s: %s missing", who, w.name.c_str());
     const ForgeStTensor& v = it->second;
-    const bool ok = cols ? (v.ndim == 2 && v.shape[0] == rows && v.shape[1] == cols)
-                         : (v.ndim == 1 && v.shape[0] == rows);
+    const bool ok = w.cols ? (v.ndim == 2 && v.shape[0] == w.rows && v.shape[1] == w.cols)
+                           : (v.ndim == 1 && v.shape[0] == w.rows);
     if (!ok)
-        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_load_safetensors: %s has shape [%lld%s%lld], expected [%lld%s%lld]",
-                          name.c_str(), (long long)v.shape[0], v.ndim > 1 ? ", " : "",
-                          v.ndim > 1 ? (long long)v.shape[1] : 0LL, (long long)rows, cols ? ", " : "",
-                          (long long)cols);
-    const int64_t n = rows * (cols ? cols : 1);
+        return forge_fail(FORGE_INVALID_ARGS, "%s: %s has shape [%lld%s%lld], expected [%lld%s%lld]", who,
+                          w.name.c_str(), v.ndim > 0 ? (long long)v.shape[0] : 0LL, v.ndim > 1 ? ", " : "",
+                          v.ndim > 1 ? (long long)v.shape[1] : 0LL, (long long)w.rows, w.cols ? ", " : "",
+                          (long long)w.cols);
+    if (!is_float_dtype(v.dtype))
+        return forge_fail(FORGE_INVALID_ARGS, "%s: %s is not a floating-point tensor", who, w.name.c_str());
+    return 0;
+}
+
+// The (checked) tensor converted into bf16 or fp32.
+int fetch(const Shards& s, const Want& w, std::vector<uint16_t>* bf, std::vector<float>* f32) {
+    const ForgeStTensor& v = s.byname.at(w.name);
+    const int64_t n = w.rows * (w.cols ? w.cols : 1);
     if (bf) {
         bf->resize((size_t)n);
         return forge_st_tensor_to_bf16(&v, bf->data(), n);
@@ -559,43 +612,41 @@ int fetch(const Shards& s, const std::string& name, int64_t rows, int64_t cols, 
 }
 }  // namespace
 
-FORGE_API int forge_b200_load_safetensors(ForgeB200* h, int n_files, const char* const* paths) {
-    const ForgeModelDesc* d = forge_b200_desc_of(h);
-    if (!d || n_files <= 0 || !paths) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_load_safetensors: bad args");
+FORGE_API int forge_safetensors_check_llama(const ForgeModelDesc* d, int n_files, const char* const* paths) {
+    const char* who = "forge_safetensors_check_llama";
+    if (!d || d->n_layer <= 0 || d->d_model <= 0 || d->n_head <= 0 || d->n_kv_head <= 0 || d->head_dim <= 0 ||
+        d->ffn <= 0 || d->vocab <= 0)
+        return forge_fail(FORGE_INVALID_ARGS, "%s: bad model description", who);
     Shards s;
-    for (int i = 0; i < n_files; ++i) {
-        ForgeSafetensors* st = nullptr;
-        if (forge_st_open(paths[i], &st)) return FORGE_INVALID_ARGS;
-        s.files.push_back(st);
-        for (int t = 0; t < forge_st_count(st); ++t) {
-            ForgeStTensor v;
-            forge_st_tensor_at(st, t, &v);
-            if (!s.byname.emplace(v.name, v).second)
-                return forge_fail(FORGE_INVALID_ARGS, "forge_b200_load_safetensors: %s appears in two files", v.name);
-        }
-    }
-    const int64_t D = d->d_model, Q = (int64_t)d->n_head * d->head_dim, KV = (int64_t)d->n_kv_head * d->head_dim;
-    const int64_t F = d->ffn, V = d->vocab;
-    std::vector<uint16_t> w[7];
+    if (s.open(who, n_files, paths)) return FORGE_INVALID_ARGS;
+    for (const Want& w : llama_tensors(*d))
+        if (check_one(s, who, w)) return FORGE_INVALID_ARGS;
+    return 0;
+}
+
+FORGE_API int forge_b200_load_safetensors(ForgeB200* h, int n_files, const char* const* paths) {
+    const char* who = "forge_b200_load_safetensors";
+    const ForgeModelDesc* d = forge_b200_desc_of(h);
+    if (!d) return forge_fail(FORGE_INVALID_ARGS, "%s: null handle", who);
+    Shards s;
+    if (s.open(who, n_files, paths)) return FORGE_INVALID_ARGS;
+    const std::vector<Want> want = llama_tensors(*d);
+    for (const Want& w : want)  // everything is checked before anything is uploaded
+        if (check_one(s, who, w)) return FORGE_INVALID_ARGS;
+    std::vector<uint16_t> wb[7];
     std::vector<float> g1, g2;
-    static const char* kProj[7] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
-                                   "mlp.gate_proj",    "mlp.up_proj",      "mlp.down_proj"};
-    const int64_t rows[7] = {Q, KV, KV, D, F, F, D}, cols[7] = {D, D, D, Q, D, D, F};
+    size_t k = 0;
     for (int l = 0; l < d->n_layer; ++l) {
-        const std::string pre = "model.layers." + std::to_string(l) + ".";
         for (int i = 0; i < 7; ++i)
-            if (fetch(s, pre + kProj[i] + ".weight", rows[i], cols[i], &w[i], nullptr)) return FORGE_INVALID_ARGS;
-        if (fetch(s, pre + "input_layernorm.weight", D, 0, nullptr, &g1) ||
-            fetch(s, pre + "post_attention_layernorm.weight", D, 0, nullptr, &g2))
-            return FORGE_INVALID_ARGS;
-        ForgeLayerWeights lw{w[0].data(), w[1].data(), w[2].data(), w[3].data(), w[4].data(),
-                             w[5].data(), w[6].data(), g1.data(),  g2.data()};
+            if (fetch(s, want[k++], &wb[i], nullptr)) return FORGE_INVALID_ARGS;
+        if (fetch(s, want[k++], nullptr, &g1) || fetch(s, want[k++], nullptr, &g2)) return FORGE_INVALID_ARGS;
+        ForgeLayerWeights lw{wb[0].data(), wb[1].data(), wb[2].data(), wb[3].data(), wb[4].data(),
+                             wb[5].data(), wb[6].data(), g1.data(),  g2.data()};
         if (forge_b200_load_layer(h, l, &lw)) return FORGE_INVALID_ARGS;
     }
     std::vector<uint16_t> emb, head;
     std::vector<float> gF;
-    if (fetch(s, "model.embed_tokens.weight", V, D, &emb, nullptr) || fetch(s, "model.norm.weight", D, 0, nullptr, &gF))
-        return FORGE_INVALID_ARGS;
-    if (!d->tied_head && fetch(s, "lm_head.weight", V, D, &head, nullptr)) return FORGE_INVALID_ARGS;
+    if (fetch(s, want[k++], &emb, nullptr) || fetch(s, want[k++], nullptr, &gF)) return FORGE_INVALID_ARGS;
+    if (!d->tied_head && fetch(s, want[k++], &head, nullptr)) return FORGE_INVALID_ARGS;
     return forge_b200_load_embedding(h, emb.data(), gF.data(), d->tied_head ? nullptr : head.data());
 }

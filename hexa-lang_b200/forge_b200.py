@@ -252,6 +252,7 @@ def lib() -> C.CDLL:
             "forge_st_tensor_to_bf16": (i32, [C.POINTER(ForgeStTensor), vp, i64]),
             "forge_st_tensor_to_f32": (i32, [C.POINTER(ForgeStTensor), vp, i64]),
             "forge_b200_load_safetensors": (i32, [vp, i32, C.POINTER(C.c_char_p)]),
+            "forge_safetensors_check_llama": (i32, [C.POINTER(ForgeModelDesc), i32, C.POINTER(C.c_char_p)]),
         }
         for name, (res, args) in sig.items():
             if hasattr(L, name):

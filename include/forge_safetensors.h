@@ -98,6 +98,11 @@ int         forge_st_tensor_to_f32(const ForgeStTensor* v, float* out, int64_t n
  * description. Under tensor parallelism every rank loads the same files and
  * keeps its shard. Synchronous. */
 int forge_b200_load_safetensors(ForgeB200* h, int n_files, const char* const* paths);
+/* The checks forge_b200_load_safetensors makes before it uploads anything
+ * (every tensor present once, with the shape the description gives and a
+ * floating-point dtype), without a model handle or a GPU. 0 when the
+ * checkpoint loads; otherwise the first problem in forge_b200_last_error(). */
+int forge_safetensors_check_llama(const ForgeModelDesc* desc, int n_files, const char* const* paths);
 
 #ifdef __cplusplus
 }

@@ -224,3 +224,65 @@ def test_empty_header_and_escaped_names(forge, tmp_path):
              raw_header=b'{"\\u00e9\\ud83d\\ude00\\n\\"": {"dtype": "U8", "shape": [1], "data_offsets": [0, 1]}}')
     st2 = forge.Safetensors(p2)
     assert st2.names() == ["é\U0001F600\n\""]
+
+
+def _llama(cfg, tied, dtype="BF16", drop=(), reshape=None, int_name=None):
+    """Tensors of the Llama layout for cfg, zero-filled (shapes are what matter)."""
+    L, d, H, Hkv, hd, F, V = cfg
+    shapes = {}
+    for l in range(L):
+        p = f"model.layers.{l}."
+        shapes.update({p + "self_attn.q_proj.weight": (H * hd, d), p + "self_attn.k_proj.weight": (Hkv * hd, d),
+                       p + "self_attn.v_proj.weight": (Hkv * hd, d), p + "self_attn.o_proj.weight": (d, H * hd),
+                       p + "mlp.gate_proj.weight": (F, d), p + "mlp.up_proj.weight": (F, d),
+                       p + "mlp.down_proj.weight": (d, F), p + "input_layernorm.weight": (d,),
+                       p + "post_attention_layernorm.weight": (d,)})
+    shapes.update({"model.embed_tokens.weight": (V, d), "model.norm.weight": (d,)})
+    if not tied:
+        shapes["lm_head.weight"] = (V, d)
+    out = []
+    for name, shp in shapes.items():
+        if name in drop:
+            continue
+        if name == reshape:
+            shp = (shp[0] + 1,) + shp[1:]
+        dt = "I32" if name == int_name else dtype
+        esz = {"BF16": 2, "F16": 2, "F32": 4, "F64": 8, "I32": 4}[dt]
+        out.append((name, dt, list(shp), bytes(int(np.prod(shp)) * esz)))
+    return out
+
+
+def test_check_llama_checkpoint(forge, tmp_path):
+    cfg = (2, 128, 4, 2, 32, 256, 300)
+    L = forge.lib()
+
+    def check(tensors, tied=False, split=2, sub="c"):
+        d = tmp_path / sub
+        d.mkdir(exist_ok=True)
+        paths = []
+        for k in range(split):
+            p = str(d / f"model-{k}.safetensors")
+            write_st(p, tensors[k::split])
+            paths.append(p)
+        desc = forge.ForgeModelDesc(n_layer=cfg[0], d_model=cfg[1], n_head=cfg[2], n_kv_head=cfg[3],
+                                    head_dim=cfg[4], ffn=cfg[5], vocab=cfg[6], tied_head=int(tied))
+        arr = (forge.C.c_char_p * len(paths))(*[p.encode() for p in paths])
+        rc = L.forge_safetensors_check_llama(forge.C.byref(desc), len(paths), arr)
+        return rc, L.forge_b200_last_error().decode()
+
+    assert check(_llama(cfg, False), sub="ok")[0] == 0
+    assert check(_llama(cfg, True), tied=True, sub="tied")[0] == 0
+    assert check(_llama(cfg, False) + [("extra.bias", "F32", [3], bytes(12))], sub="extra")[0] == 0  # extras ignored
+    for dt in ("F16", "F32", "F64"):
+        assert check(_llama(cfg, False, dtype=dt), split=1, sub=dt)[0] == 0
+    rc, msg = check(_llama(cfg, True), tied=False, sub="nohead")
+    assert rc != 0 and "lm_head.weight missing" in msg
+    rc, msg = check(_llama(cfg, False, drop=("model.layers.1.mlp.down_proj.weight",)), sub="drop")
+    assert rc != 0 and "model.layers.1.mlp.down_proj.weight missing" in msg
+    rc, msg = check(_llama(cfg, False, reshape="model.layers.0.self_attn.k_proj.weight"), sub="shape")
+    assert rc != 0 and "self_attn.k_proj.weight has shape [65, 128], expected [64, 128]" in msg
+    rc, msg = check(_llama(cfg, False, int_name="model.norm.weight"), sub="int")
+    assert rc != 0 and "model.norm.weight is not a floating-point tensor" in msg
+    t = _llama(cfg, False)
+    rc, msg = check(t + [t[0]], split=2, sub="dup")  # the same name in both shards
+    assert rc != 0 and "appears in two files" in msg
