@@ -298,6 +298,7 @@ FORGE_API int forge_st_open(const char* path, ForgeSafetensors** out) {
     st->base = (const uint8_t*)m;
     const uint64_t hl = load_le<uint64_t>(st->base);
     if (hl > (uint64_t)(st->size - 8)) return st_error(st, path, "header length past the end of the file");
+    if (hl > 100000000u) return st_error(st, path, "header larger than the format's 100 MB limit");
     st->header_len = (int64_t)hl;
     const int64_t data0 = 8 + st->header_len;
 

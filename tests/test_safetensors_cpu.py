@@ -184,6 +184,7 @@ def test_conversions(forge, oracle, tmp_path):
 BAD = [
     ("short", None, "shorter than"),
     ("hlen", "hlen", "past the end"),
+    ("huge", "huge", "100 MB limit"),
     ("notjson", b"[1, 2]", "not a JSON object"),
     ("badjson", b'{"a": {"dtype": "F32", "shape": [1], "data_offsets": [0, 4]', "expected"),
     ("dtype", b'{"a": {"dtype": "F31", "shape": [1], "data_offsets": [0, 4]}}', "unknown dtype"),
@@ -208,6 +209,10 @@ def test_malformed_files_are_rejected(forge, tmp_path, case, header, msg):
         open(p, "wb").write(b"\x01\x02\x03")
     elif case == "hlen":
         open(p, "wb").write(struct.pack("<Q", 1000) + b"{}")
+    elif case == "huge":
+        with open(p, "wb") as f:  # a sparse file past the 100 MB header limit
+            f.write(struct.pack("<Q", 100000001) + b"{")
+            f.truncate(8 + 100000001)
     else:
         open(p, "wb").write(struct.pack("<Q", len(header)) + header + b"\0" * 4)
     with pytest.raises(forge.ForgeError, match=msg):
