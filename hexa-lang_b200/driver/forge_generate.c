@@ -12,6 +12,10 @@
  *                  [--weights a.safetensors[,b.safetensors...] | --synthetic SEED]
  *                  [--temperature T] [--top-k K] [--top-p P] [--seed S]
  *                  --gen N  TOKEN [TOKEN ...]
+ *   forge_generate --check <model options> --weights a.safetensors[,...]
+ *
+ * --check only validates the checkpoint against the model options (every
+ * tensor present, shaped and typed as the loader needs it); no GPU is used.
  *
  * Prints the N generated token ids on one line (stdout) and the decode rate
  * on stderr. Exit status 0 on success, 1 on a library error (its message on
@@ -32,7 +36,8 @@ static void usage(FILE* f) {
             "usage: forge_generate --layers L --dim D --heads H --kv-heads HKV --head-dim HD --ffn F --vocab V\n"
             "                      [--int4] [--tied] [--ctx N] [--device G]\n"
             "                      [--weights a.safetensors[,b...] | --synthetic SEED]\n"
-            "                      [--temperature T] [--top-k K] [--top-p P] [--seed S] --gen N TOKEN...\n");
+            "                      [--temperature T] [--top-k K] [--top-p P] [--seed S] --gen N TOKEN...\n"
+            "       forge_generate --check <model options> --weights a.safetensors[,b...]\n");
 }
 
 static int fail(ForgeB200* h, const char* what) {
@@ -59,6 +64,7 @@ int main(int argc, char** argv) {
     double temperature = 0.0, top_p = 1.0;
     long long seed = 42, synth = -1;
     char* weights = NULL;
+    int check_only = 0;
     int32_t* prompt = NULL;
     int n_prompt = 0;
     for (int i = 1; i < argc; ++i) {
@@ -88,6 +94,7 @@ int main(int argc, char** argv) {
 #undef INTARG
         if (!strcmp(a, "--int4")) { d.weight_kind = FORGE_WEIGHT_Q4_G128; continue; }
         if (!strcmp(a, "--tied")) { d.tied_head = 1; continue; }
+        if (!strcmp(a, "--check")) { check_only = 1; continue; }
         if (more && !strcmp(a, "--temperature")) { temperature = atof(argv[++i]); continue; }
         if (more && !strcmp(a, "--top-p")) { top_p = atof(argv[++i]); continue; }
         if (more && !strcmp(a, "--seed")) { seed = atoll(argv[++i]); continue; }
@@ -102,6 +109,21 @@ int main(int argc, char** argv) {
         if (!p) return 2;
         prompt = p;
         prompt[n_prompt++] = (int32_t)atoi(a);
+    }
+    if (check_only) {
+        if (!weights || d.n_layer <= 0 || d.d_model <= 0 || d.n_head <= 0 || d.n_kv_head <= 0 || d.head_dim <= 0 ||
+            d.ffn <= 0 || d.vocab <= 0) {
+            usage(stderr);
+            free(prompt);
+            return 2;
+        }
+        const char* paths[64];
+        int n = 0;
+        for (char* s = strtok(weights, ","); s && n < 64; s = strtok(NULL, ",")) paths[n++] = s;
+        free(prompt);
+        if (forge_safetensors_check_llama(&d, n, paths)) return fail(NULL, "check");
+        printf("ok: %d file(s) hold every tensor of the model\n", n);
+        return 0;
     }
     if (d.n_layer <= 0 || d.d_model <= 0 || d.n_head <= 0 || d.n_kv_head <= 0 || d.head_dim <= 0 || d.ffn <= 0 ||
         d.vocab <= 0 || n_gen <= 0 || n_prompt == 0 || (!weights && synth < 0)) {

@@ -36,3 +36,20 @@ def test_library_error_without_gpu(driver):
         pytest.skip("a GPU is present")
     r = subprocess.run([driver] + MODEL + ["--synthetic", "1", "--gen", "4", "5", "6"], capture_output=True, text=True)
     assert r.returncode == 1 and "forge_generate: create:" in r.stderr and r.stdout == ""
+
+
+def test_check_mode(driver, tmp_path):
+    """--check validates a checkpoint against the model options without a GPU."""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from test_safetensors_cpu import _llama, write_st
+    cfg = (1, 256, 4, 2, 64, 512, 1000)
+    good = str(tmp_path / "good.safetensors")
+    write_st(good, _llama(cfg, False))
+    r = subprocess.run([driver, "--check", "--weights", good] + MODEL, capture_output=True, text=True)
+    assert r.returncode == 0 and r.stdout.startswith("ok: 1 file"), r.stderr
+    bad = str(tmp_path / "bad.safetensors")
+    write_st(bad, _llama(cfg, False, drop=("model.norm.weight",)))
+    r = subprocess.run([driver, "--check", "--weights", bad] + MODEL, capture_output=True, text=True)
+    assert r.returncode == 1 and "model.norm.weight missing" in r.stderr
+    assert subprocess.run([driver, "--check"] + MODEL, capture_output=True).returncode == 2
