@@ -30,8 +30,8 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 MODEL = dict(n_layer=32, d=4096, n_head=32, n_kv=32, hd=128, ffn=11008, vocab=32000)
 CTX = 2048
 # dram__bytes_read.sum + dram__bytes_write.sum of one k_gemv launch (int4
-# gate/up 22016 x 4096, batch 1) from the ncu capture summarised in
-# profiles/k_gemv_int4_gateup_22016x4096_bs1.md (46.56 MB + 0.05 MB).
+# gate/up 22016 x 4096, batch 1) from an ncu capture of this kernel alone
+# (46.56 MB read + 0.05 MB written).
 GEMV_TRAFFIC = 46558720 + 51968
 
 

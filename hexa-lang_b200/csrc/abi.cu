@@ -344,13 +344,12 @@ int v2_flash_decode(const ForgeShapeInfo* s, const ForgeArgs* in, const ForgeArg
     const uint16_t* kc = (const uint16_t*)kv->d_k + per_layer * layer;
     const uint16_t* vc = (const uint16_t*)kv->d_v + per_layer * layer;
     // the cache's batch stride is kv->batch sequences; the kernel indexes
-    // [B][Hkv][lmax][hd] from the layer base, so B <= kv->batch is enough
+    // [B][Hkv][lmax][hd] from the layer base, so B <= kv->batch is enough.
+    // The split partials live in a workspace this family owns per device
+    // (never the allocation-free entry's shared array), and device errors
+    // land in the per-op error word that forge_ops_check reads.
     const int64_t need = forge_flash_decode_workspace_bytes((int)B, (int)H, (int)kv->n_kv_head, (int)hd, (int)kv->max_ctx);
-    if (need <= forge_flash_decode_noalloc_capacity()) {
-        const int rc = forge_flash_decode_noalloc(Q, kc, vc, kv->d_pos, (int)B, (int)H, (int)kv->n_kv_head, (int)hd,
-                                                  (int)kv->max_ctx, O, nullptr);
-        return rc ? FORGE_KERNEL_UNSUPPORTED : FORGE_OK;
-    }
+    if (need <= 0) return FORGE_INVALID_ARGS;
     static std::mutex mu;
     static void* ws[64] = {nullptr};
     static int64_t wsb[64] = {0};

@@ -22,7 +22,15 @@
 // cudaGetSymbolAddress (host code cannot use the symbol itself: in host code
 // it names a host-side stand-in, not device memory). That lookup is done
 // once per device, with the device current; make the first call on each
-// device before any stream capture begins.
+// device before any stream capture begins. The address is kept for the life
+// of the process, so the entry must not be used after cudaDeviceReset (or
+// any other teardown of the device's primary context): the kept address
+// would name memory of a context that no longer exists.
+//
+// Errors found by the kernel (a position outside the cache, a wait that ran
+// out) are recorded in a device word of this file, separate from the
+// library's other error words; forge_flash_decode_noalloc_status reads and
+// clears it. No other entry of the library uses this array or this word.
 #include <mutex>
 #include "forge_internal.h"
 #include "../../include/forge_b200.h"
@@ -97,12 +105,16 @@ FORGE_API int forge_flash_decode_noalloc(const float* q, const uint16_t* kc, con
     return forge_attn_launch(a, (cudaStream_t)stream, false) ? FORGE_INVALID_ARGS : 0;
 }
 
-// Synchronises the device, then reads and clears the error word the
-// allocation-free kernel writes (a position outside the cache).
+// Waits for all work on the current device (every stream, including
+// non-blocking ones), then reads and clears the error word the
+// allocation-free kernel writes (a position outside the cache, a wait that
+// ran out).
 FORGE_API int forge_flash_decode_noalloc_status(void) {
     void* scratch = nullptr;
     uint32_t* err = nullptr;
     if (int rc = scratch_for_device(&scratch, &err)) return rc;
+    if (cudaError_t se = cudaDeviceSynchronize(); se != cudaSuccess)
+        return forge_fail(-1, "forge_flash_decode_noalloc_status: %s", cudaGetErrorString(se));
     uint32_t e = 0;
     if (cudaMemcpyFromSymbol(&e, g_fd_err, sizeof(e)) != cudaSuccess)
         return forge_fail(-1, "forge_flash_decode_noalloc_status: %s", cudaGetErrorString(cudaGetLastError()));

@@ -18,12 +18,16 @@
 //           bit pattern (8 bits a pass); entries below it are zeroed, ties
 //           with it kept, as the reference's partial selection sort does.
 //   top-p   the boundary probability by the same radix descent with a count
-//           and an f64 sum per bucket: the largest value t such that the
+//           and a sum per bucket: the largest value t such that the
 //           entries above t sum to less than p and those at or above t reach
 //           it. Entries equal to t are kept in index order until the running
 //           sum reaches p (the reference orders equal entries by the swaps
 //           of its selection sort; the two differ only when several entries
-//           share the boundary value and not all of them are kept).
+//           share the boundary value and not all of them are kept). The
+//           bucket sums are accumulated as 64-bit fixed-point integers (each
+//           probability times 2^62, rounded): integer additions commute, so
+//           the boundary is the same on every run for the same logits,
+//           whatever order the threads' atomic additions land in.
 //   draw    the reference's Xorshift-style RNG (gpu_sampler.hexa:57-65) on
 //           a 64-bit state per sequence, in device memory.
 #include <climits>
@@ -63,10 +67,16 @@ struct Shared {
     float red_f[kWarps];
     long long red_l[kWarps];
     int hist[256];
-    double hsum[256];
+    unsigned long long hsum[256];  // fixed point, 2^-62 units
     double bcast_d[2];
     int bcast_i[4];
 };
+
+// Probability (0 <= v <= 1, sums to ~1) in 64-bit fixed point, 2^-62 units.
+__device__ __forceinline__ unsigned long long fx62(float v) {
+    return (unsigned long long)llrint((double)v * 0x1p62);
+}
+__device__ __forceinline__ double fx62_to_f64(unsigned long long x) { return (double)x * 0x1p-62; }
 
 __device__ double block_sum(double v, Shared& sh) {
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -251,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_sample(const SampleArgs a) {
         for (int shift = 24; shift >= 0 && !all; shift -= 8) {
             for (int j = threadIdx.x; j < 256; j += kThreads) {
                 sh.hist[j] = 0;
-                sh.hsum[j] = 0.0;
+                sh.hsum[j] = 0ull;
             }
             __syncthreads();
             for (int i = i0; i < i1; ++i) {
@@ -259,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_sample(const SampleArgs a) {
                 const uint32_t u = __float_as_uint(v);
                 if (v > 0.0f && (u & mask) == prefix) {
                     atomicAdd(&sh.hist[(u >> shift) & 255u], 1);
-                    atomicAdd(&sh.hsum[(u >> shift) & 255u], (double)v);
+                    atomicAdd(&sh.hsum[(u >> shift) & 255u], fx62(v));
                 }
             }
             __syncthreads();
@@ -269,8 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_sample(const SampleArgs a) {
                 for (int j = 255; j >= 0; --j) {
                     if (!sh.hist[j]) continue;
                     lowest = j;
-                    if (acc + sh.hsum[j] >= a.top_p) { pick = j; break; }
-                    acc += sh.hsum[j];
+                    const double hs = fx62_to_f64(sh.hsum[j]);
+                    if (acc + hs >= a.top_p) { pick = j; break; }
+                    acc += hs;
                 }
                 int allf = 0;
                 if (pick < 0) {
@@ -278,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_sample(const SampleArgs a) {
                         allf = 1;  // the nonzero entries never reach p: keep them all
                     } else {       // rounding between levels: the smallest nonempty bucket
                         pick = lowest;
-                        acc -= sh.hsum[lowest];
+                        acc -= fx62_to_f64(sh.hsum[lowest]);
                     }
                 }
                 sh.bcast_i[0] = pick;

@@ -238,8 +238,12 @@ int forge_flash_decode(const float* q, const uint16_t* kc, const uint16_t* vc, c
  * rejected with FORGE_INVALID_ARGS. Calls share that array, so calls that
  * overlap on the GPU race; order them on one stream. The first call on a
  * device looks up the array's device address and should happen before any
- * stream capture. No counterpart in the reference: it is an addition of
- * this library. */
+ * stream capture; that address is kept for the process, so the entry must
+ * not be used after cudaDeviceReset. Kernel errors go to an error word of
+ * this entry alone: forge_flash_decode_noalloc_status waits for the whole
+ * device, then reads and clears it (-1 once per error). No other entry of
+ * the library uses the array or the word. No counterpart in the reference:
+ * it is an addition of this library. */
 int64_t forge_flash_decode_noalloc_capacity(void);
 int forge_flash_decode_noalloc(const float* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos,
                                int B, int H, int Hkv, int hd, int lmax, float* out, void* stream);

@@ -201,6 +201,22 @@ def test_v2_flash_decode_kv_descriptor(forge, oracle, cuda):
             p = np.exp(s - s.max())
             ref = p / p.sum() @ Vf[b, h // G, :pos[b] + 1]
             assert np.abs(got[b, h * hd:(h + 1) * hd] - ref).max() < 2e-5 * max(1, np.abs(ref).max())
+    # a device-side bad position (written past the host check) is reported by
+    # the per-op error word, not by the allocation-free entry's own word
+    import torch
+    F.check(L.forge_ops_check(), "clean before")
+    L.forge_flash_decode_noalloc_status()
+
+    class _Pos:  # the descriptor's device positions as a torch view
+        __cuda_array_interface__ = {"shape": (B,), "typestr": "<i4", "data": (kv.contents.d_pos, False),
+                                    "version": 3}
+    torch.as_tensor(_Pos(), device="cuda")[1] = lmax
+    assert dispatch(F, F.FORGE_KERNEL_FLASH_DECODE, F.FORGE_PREC_PURE_BF16, (B, H, hd, 0),
+                    (Q, kv, layer), (O,), v2=True) == 0
+    torch.cuda.synchronize()
+    assert L.forge_flash_decode_noalloc_status() == 0
+    assert L.forge_ops_check() != 0
+    assert L.forge_ops_check() == 0
     L.hexa_kv_free(kv)
     L.hexa_farr_f32_free(Q)
     L.hexa_farr_f32_free(O)

@@ -6,8 +6,11 @@ forge_flash_decode_noalloc takes the same inputs and outputs as
 forge_flash_decode but keeps its scratch in a fixed library-owned device
 array instead of a caller workspace. Checked through the C ABI against the
 workspace entry on two calls in a row (the array keeps the previous call's
-contents), and for the clean rejection of shapes above its fixed size. This
-file is collected last so that a failure here leaves every other test run.
+contents), for the clean rejection of shapes above its fixed size, and for
+its error word: a position outside the cache is reported once by
+forge_flash_decode_noalloc_status (and by no other error word) and then
+reads clean. This file is collected last so that a failure here leaves
+every other test run.
 """
 import numpy as np
 import pytest
@@ -70,3 +73,33 @@ def test_noalloc_rejects_shapes_above_capacity(forge, cuda):
                                         hd, lmax, tiny.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc != 0
     assert b"scratch bytes" in lib.forge_b200_last_error()
+
+
+def test_noalloc_error_word_reports_once_and_clears(forge, oracle, cuda):
+    """A position outside the cache: the kernel's bounds check skips the
+    sequence and records the error in the entry's own word; the status call
+    returns the failure once, then reads clean. The per-op error word of the
+    rest of the library does not see it."""
+    import torch
+    lib = forge.lib()
+    B, H, Hkv, hd, lmax = 2, 8, 2, 64, 256
+    q, Kb, Vb, _ = _inputs(oracle, B, H, Hkv, hd, lmax, [0, 0], seed=11)
+    qd = torch.from_numpy(q).to(cuda)
+    kd = torch.from_numpy(Kb.view(np.int16)).to(cuda)
+    vd = torch.from_numpy(Vb.view(np.int16)).to(cuda)
+    stream = torch.cuda.current_stream().cuda_stream
+    torch.cuda.synchronize()
+    lib.forge_ops_check()                   # start from clean words
+    lib.forge_flash_decode_noalloc_status()
+    bad = torch.tensor([10, lmax], dtype=torch.int32, device=cuda)  # sequence 1 past the cache
+    out = torch.zeros((B, H * hd), device=cuda)
+    forge.check(lib.forge_flash_decode_noalloc(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), bad.data_ptr(), B, H,
+                                               Hkv, hd, lmax, out.data_ptr(), stream), "launch")
+    assert lib.forge_flash_decode_noalloc_status() != 0
+    assert b"error word" in lib.forge_b200_last_error()
+    assert lib.forge_flash_decode_noalloc_status() == 0   # cleared by the read
+    assert lib.forge_ops_check() == 0                     # never reported elsewhere
+    good = torch.tensor([10, 200], dtype=torch.int32, device=cuda)
+    forge.check(lib.forge_flash_decode_noalloc(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), good.data_ptr(), B, H,
+                                               Hkv, hd, lmax, out.data_ptr(), stream), "launch after the error")
+    forge.check(lib.forge_flash_decode_noalloc_status(), "clean call after the error")
