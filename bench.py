@@ -1,18 +1,28 @@
 """Decode throughput of the flame->forge hot path on B200.
 
-Workload (default): 7B-shape int4 weight-only decode — 32 layers, d_model
+Headline workload: 7B-shape int4 weight-only decode — 32 layers, d_model
 4096, 32 heads x 128 (MHA), SwiGLU ffn 11008, vocab 32000, linear weights
 int4 group-128 with bf16 scales, bf16 embeddings and LM head, batch 1, KV
 context 2048 (synthetic N(0, 0.5) bf16 cache), greedy steps. Weights are
 synthetic N(0, 0.02) generated on the device. A step is one greedy decode
 step for every sequence; value = tokens/s over K timed steps (max over
-ranks). Every step streams ~3.9 GB of weights+KV, far above the 126 MB L2,
-so no flush is needed between steps.
+ranks). Every step streams ~4.7 GB of weights+KV, far above the 126 MB L2,
+so no flush is needed between steps. With N > 1 processes the same model is
+split tensor-parallel over the N GPUs.
+
+batch_sweep: the 7B shape at batch 8 and 32, the 1B-shape bf16 GQA model
+(16 layers, d 2048, 32/8 heads x 64, ffn 8192, context 1024) at batch 1, 8
+and 32 and, at N > 1, the 13B-shape int4 model (40 layers, d 5120, 40 x 128,
+ffn 13824, batch 64, context 4096; at N = 1 its 221.6 GB do not fit one
+B200 and the entry says so). tp_parity (N > 1): greedy tokens and logits of
+the tensor-parallel engine against one GPU.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl forge|reference]
 
 --impl reference times the CPU path (the oracle restatement of flame's
-decode, OpenMP over the host cores) on a bounded sample of the same workload.
+decode, OpenMP over all host cores) on a bounded sample of the headline
+workload; its line also carries the reference's own single-layer decode
+check (cpu_ref, one core) where it was built.
 """
 import argparse
 import json
@@ -27,8 +37,24 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "hexa-lang_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
-MODEL = dict(n_layer=32, d=4096, n_head=32, n_kv=32, hd=128, ffn=11008, vocab=32000)
-CTX = 2048
+WORKLOADS = {
+    "7b_int4_decode": dict(n_layer=32, d=4096, n_head=32, n_kv=32, hd=128, ffn=11008, vocab=32000, q4=True, ctx=2048),
+    "1b_bf16_decode": dict(n_layer=16, d=2048, n_head=32, n_kv=8, hd=64, ffn=8192, vocab=32000, q4=False, ctx=1024),
+    "13b_int4_tp_decode": dict(n_layer=40, d=5120, n_head=40, n_kv=40, hd=128, ffn=13824, vocab=32000, q4=True,
+                               ctx=4096),
+}
+MODEL = WORKLOADS["7b_int4_decode"]
+CTX = MODEL["ctx"]
+HBM_BYTES = 183359 * 2**20  # one B200 (nvidia-smi total)
+
+
+def config_of(world, batch):
+    """The headline workload's config dict (both arms print the same one)."""
+    m = MODEL
+    return {"workload": "7b_int4_decode", "n_layer": m["n_layer"], "d_model": m["d"], "heads": m["n_head"],
+            "head_dim": m["hd"], "ffn": m["ffn"], "vocab": m["vocab"], "batch": batch, "ctx": CTX,
+            "parallelism": f"tp{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (4.7 GB streamed per step)"}
 # dram__bytes_read.sum + dram__bytes_write.sum of one k_gemv launch (int4
 # gate/up 22016 x 4096, batch 1) from an ncu capture of this kernel alone
 # (46.56 MB read + 0.05 MB written).
@@ -127,12 +153,14 @@ def barrier(pg):
 
 
 def time_dominant_gemv(fb, torch, dev, K=4096, N=2 * 11008, copies=4, reps=20, batch=1):
-    """The 7B gate/up int4 GEMV (N=22016, K=4096) via the per-op C-ABI entry
-    for `batch` sequences (above 4: the batched paths, whose call includes the
-    activation-quantising launch), rotating over `copies` weight sets
-    (copies x 45 MB > L2) so every launch streams from HBM. Returns (avg ms
-    per call, algorithmic bytes)."""
+    """The 7B gate/up int4 GEMV (N=22016 rows, K=4096; under tensor
+    parallelism this rank's row shard) via the per-op C-ABI entry for `batch`
+    sequences (above 4: the batched paths, whose call includes the
+    activation-quantising launch), rotating over `copies` weight sets (more
+    than L2 in total) so every launch streams from HBM. Returns (avg ms per
+    call, algorithmic bytes)."""
     lib = fb.lib()
+    copies = max(copies, -(-4 * 2**27 // max(1, N * K // 2)))  # > 512 MB in total
     ws = []
     for c in range(copies):
         w = torch.empty((N, K), dtype=torch.int16, device=dev)
@@ -186,10 +214,21 @@ def time_prefill(fb, torch, dev, B=8, H=32, S=4096, reps=10):
             "launches": reps}
 
 
+def all_cores():
+    """Host threads for the CPU legs: every core the process may run on
+    (torchrun sets OMP_NUM_THREADS=1 for its workers; the CPU legs run on
+    one rank only, so they take the whole host)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except Exception:
+        n = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    return n
+
+
 def cpu_sample(batch, ctx, reps=2):
     """Oracle decode of the same 7B int4 shape on the host cores: one layer and
     the LM head are timed and the step extrapolated to 32 layers."""
-    import numpy as np
     import oracle as orc
     m = MODEL
     res = {}
@@ -207,21 +246,53 @@ def cpu_sample(batch, ctx, reps=2):
         del om, kc, vc
     t_layer = max(res[1] - res[0], 1e-9)
     t_step = m["n_layer"] * t_layer + res[0]
-    return {"value": batch / t_step, "unit": "tok/s", "cores": orc.lib().or_num_threads(), "kind": "port",
-            "sample": f"oracle decode of 1 layer + LM head of the 7B int4 shape at ctx {ctx}, batch {batch}, "
-                      f"best of {reps}; step = 32 x layer ({t_layer*1e3:.1f} ms) + head ({res[0]*1e3:.1f} ms)"}
+    out = {"value": batch / t_step, "unit": "tok/s", "cores": orc.lib().or_num_threads(), "kind": "port",
+           "sample": f"oracle decode of 1 layer + LM head of the 7B int4 shape at ctx {ctx}, batch {batch}, "
+                     f"best of {reps}; step = 32 x layer ({t_layer*1e3:.1f} ms) + head ({res[0]*1e3:.1f} ms)"}
+    ref = cpu_ref_sample()
+    if ref:
+        out["reference_cpu_ref"] = ref
+    return out
+
+
+def cpu_ref_sample(lengths=(256, 1024, 2048)):
+    """The reference's own f64 single-layer decode check, cpu_ref
+    (tool/decode_eager_baseline.cu:160-198: d 768, 12 x 64 MHA, ffn 3072,
+    single thread), built from the reference source into oracle/_ref where
+    the reference tree was present; ms per layer at the given cache lengths."""
+    import numpy as np
+    import oracle as orc
+    R = orc.ref_lib()
+    if R is None:
+        return None
+    keys = ("x", "g1", "g2", "Wq", "Wk", "Wv", "Wo", "Wg", "Wu", "Wd", "Kc", "Vc")
+    res = {}
+    for L in lengths:
+        inp = orc.ref_inputs(L)
+        bufs = [np.ascontiguousarray(inp[k]) for k in keys]
+        y = np.empty(orc.REF_D, np.float64)
+        ts = []
+        for _ in range(2):
+            t0 = time.perf_counter()
+            R.ref_cpu_ref(*[b.ctypes.data for b in bufs], L, y.ctypes.data)
+            ts.append(time.perf_counter() - t0)
+        res[str(L)] = min(ts) * 1e3
+    return {"unit": "ms per layer", "cores": 1, "kind": "reference",
+            "shape": "d 768, 12 x 64 MHA, ffn 3072, f64 (the reference's fixed check shape)", "ms_by_ctx": res}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
+    cores = all_cores()
     sample = cpu_sample(args.batch, CTX, reps=max(1, min(args.steps, 2)))
+    sample["cores"] = cores
     v = sample["value"]
     print(json.dumps({
         "impl": "reference", "metric": "decode tok/s (7B-shape int4 g128, bs%d, ctx %d)" % (args.batch, CTX),
         "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "higher_is_better": True, "dtype": "int4 weights / f64 compute", "data": "synthetic",
-        "config": {"workload": "7b_int4_decode", "batch": args.batch, "ctx": CTX},
+        "config": config_of(world, args.batch),
         "cpu_baseline": sample, "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
@@ -233,23 +304,33 @@ def tp_id(fb, pg, rank):
     return obj[0]
 
 
-def run_decode(fb, torch, pg, local, world, rank, B, K, W):
-    """K timed greedy steps of the 7B int4 model at batch B (device-resident
+def model_bytes(m, B, ctx):
+    """Weights + KV cache of a workload on one GPU (for the does-not-fit check)."""
+    lin = m["n_layer"] * ((m["n_head"] + 2 * m["n_kv"]) * m["hd"] * m["d"] + m["n_head"] * m["hd"] * m["d"] +
+                          3 * m["ffn"] * m["d"])
+    w = lin * (0.5 + 2 / 128) if m["q4"] else lin * 2
+    kv = 2 * m["n_layer"] * B * m["n_kv"] * m["hd"] * 2 * (ctx + 64)
+    return w + 2 * m["vocab"] * m["d"] * 2 + kv
+
+
+def run_decode(fb, torch, pg, local, world, rank, B, K, W, name="7b_int4_decode", e2e=True):
+    """K timed greedy steps of workload `name` at batch B (device-resident
     tokens), then K steps through the host C-ABI call (e2e). With N > 1
-    processes the model is split tensor-parallel over the N GPUs (one NCCL
+    processes the model is split tensor-parallel over the N GPUs (one
     all-reduce after the O and after the down projection)."""
-    m = MODEL
-    lmax = CTX + W + 2 * K + 8
+    m = WORKLOADS[name]
+    ctx = m["ctx"]
+    lmax = ctx + W + 2 * K + 8
     tp = dict(tp_rank=rank, tp_size=world, nccl_id=tp_id(fb, pg, rank)) if world > 1 else {}
     fm = fb.ForgeModel(m["n_layer"], m["d"], m["n_head"], m["n_kv"], m["hd"], m["ffn"], m["vocab"],
-                       weight_kind=fb.FORGE_WEIGHT_Q4_G128, tied_head=False, max_batch=B, max_ctx=lmax,
-                       device=local, **tp)
+                       weight_kind=fb.FORGE_WEIGHT_Q4_G128 if m["q4"] else fb.FORGE_WEIGHT_BF16, tied_head=False,
+                       max_batch=B, max_ctx=lmax, device=local, **tp)
     fm.init_synthetic(1234, 0.02)
-    fm.fill_kv_synthetic(99, CTX, 0.5)
+    fm.fill_kv_synthetic(99, ctx, 0.5)
     # warm-up (graph capture + replays)
     fm.decode_device(B, W)
     fm.sync()
-    ctx_mid = CTX + W + K // 2
+    ctx_mid = ctx + W + K // 2
     stream = torch.cuda.ExternalStream(fm.stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(pg)
@@ -263,37 +344,83 @@ def run_decode(fb, torch, pg, local, world, rank, B, K, W):
     ms = e0.elapsed_time(e1) / K
     ms = max_over_ranks(pg, ms)
     value = B / (ms / 1e3)  # the N ranks decode the same B sequences together
-    # end-to-end through the host C-ABI call: H2D tokens, step, D2H next tokens
-    toks = [1] * B
-    for _ in range(3):
-        toks = fm.step(toks)
-    torch.cuda.synchronize()
-    barrier(pg)
-    t0 = time.perf_counter()
-    e2 = torch.cuda.Event(enable_timing=True)
-    e3 = torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
-    for _ in range(K):
-        toks = fm.step(toks)
-    e3.record(stream)
-    torch.cuda.synchronize()
-    wall = (time.perf_counter() - t0) / K * 1e3
-    e2e_ms = max(e2.elapsed_time(e3) / K, wall)
-    e2e_ms = max_over_ranks(pg, e2e_ms)
-    step_bytes = fm.step_bytes(B, ctx_mid) * world  # every rank streams its shard
-    launches = fm.launches_per_step(B) * K
+    out = {"workload": name, "batch": B, "ctx": ctx, "value": value, "unit": "tok/s", "ms_per_step": ms,
+           "clocks": clk.summary()}
+    if e2e:
+        # end to end through the host C-ABI call: H2D tokens, step, D2H next tokens
+        toks = [1] * B
+        for _ in range(3):
+            toks = fm.step(toks)
+        torch.cuda.synchronize()
+        barrier(pg)
+        t0 = time.perf_counter()
+        e2 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for _ in range(K):
+            toks = fm.step(toks)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) / K * 1e3
+        e2e_ms = max(e2.elapsed_time(e3) / K, wall)
+        e2e_ms = max_over_ranks(pg, e2e_ms)
+        out["e2e"] = {"value": B / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                      "d2h_bytes_per_step": 4 * B, "ms_per_step": e2e_ms}
+    # this rank's shard bytes; the whole job streams world x that
+    rank_bytes = fm.step_bytes(B, ctx_mid)
+    total = max_over_ranks(pg, rank_bytes) * world
     peak, peak_kind = peaks()
-    step_gbs = step_bytes / (ms / 1e3) / 1e9
+    gbs = total / (ms / 1e3) / 1e9
+    out["hbm_roofline_step"] = {"bytes_per_step": total, "achieved_gbs": gbs, "peak_gbs": peak * world,
+                                "frac": gbs / (peak * world), "per_gpu_frac": gbs / world / peak,
+                                "peak_kind": peak_kind, "frac_of_8tbs_nominal": gbs / world / 8000.0}
+    out["gpu_launches"] = fm.launches_per_step(B) * K
     fm.close()
-    return {
-        "batch": B, "value": value, "ms_per_step": ms, "clocks": clk.summary(),
-        "hbm_roofline_step": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "peak_gbs": peak,
-                              "frac": step_gbs / peak, "peak_kind": peak_kind,
-                              "frac_of_8tbs_nominal": step_gbs / 8000.0},
-        "e2e": {"value": B / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
-                "d2h_bytes_per_step": 4 * B, "ms_per_step": e2e_ms},
-        "gpu_launches": launches,
-    }
+    return out
+
+
+def tp_parity(fb, torch, pg, local, world, rank):
+    """Greedy tokens and logits of the tensor-parallel engine against one GPU
+    (rank 0) with the same seeded weights: a small GQA int4 model (2 layers,
+    d 512, 8/2 heads x 64, ffn 1536, vocab 2000; 6 logit steps at batch 2 and
+    32 greedy tokens), and the first 8 greedy tokens of the 7B shape."""
+    import numpy as np
+    cases = [("small_gqa_int4", dict(cfg=(2, 512, 8, 2, 64, 1536, 2000), std=0.05, n_gen=32, batch=2, steps=6)),
+             ("7b_int4", dict(cfg=(32, 4096, 32, 32, 128, 11008, 32000), std=0.02, n_gen=8, batch=1, steps=0))]
+    prompts = np.array([[3, 17, 5, 99], [8, 2, 64, 1]], np.int32)
+    res = {"ok": True, "n_ranks": world}
+
+    def run(cfg, kw, tp):
+        B = kw["batch"]
+        fm = fb.ForgeModel(*cfg, weight_kind=fb.FORGE_WEIGHT_Q4_G128, max_batch=B, max_ctx=64, device=local, **tp)
+        fm.init_synthetic(1234, kw["std"])
+        gen = fm.generate(prompts[:B], kw["n_gen"])
+        fm.reset()
+        toks, lgs = prompts[:B, 0].copy(), []
+        for _ in range(kw["steps"]):
+            toks, lg = fm.step(toks, want_logits=True)
+            lgs.append(lg)
+        fm.close()
+        return gen, (np.stack(lgs) if lgs else None)
+
+    for name, kw in cases:
+        gen, lgs = run(kw["cfg"], kw, dict(tp_rank=rank, tp_size=world, nccl_id=tp_id(fb, pg, rank)))
+        ok_local = 1.0
+        entry = {}
+        if rank == 0:
+            rg, rl = run(kw["cfg"], kw, {})
+            tok_ok = bool(np.array_equal(gen, rg))
+            entry = {"tokens_equal": tok_ok, "n_tokens": int(gen.size)}
+            if lgs is not None:
+                scale = float(np.abs(rl).max())
+                err = float(np.abs(lgs - rl).max())
+                entry.update(max_abs_logit_err=err, logit_scale=scale, bound=2e-3 * scale)
+                tok_ok = tok_ok and err <= 2e-3 * scale
+            ok_local = 1.0 if tok_ok else 0.0
+            res[name] = entry
+        ok_all = -max_over_ranks(pg, -ok_local)
+        res["ok"] = res["ok"] and ok_all > 0.5
+    return res
 
 
 def main():
@@ -304,8 +431,7 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", default="forge", choices=["forge", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--also-batch", type=int, nargs="*", default=[32],
-                    help="further batch sizes measured after the main one (reported under batch_sweep)")
+    ap.add_argument("--no-sweep", action="store_true", help="headline workload only")
     ap.add_argument("--only-gemv", action="store_true", help="run only the dominant GEMV (for profiling)")
     ap.add_argument("--only-prefill", action="store_true", help="run only the flash prefill (for profiling)")
     ap.add_argument("--no-prefill", action="store_true")
@@ -320,7 +446,7 @@ def main():
     dev = torch.device("cuda", local)
     if args.only_gemv:
         # the dominant kernel alone, for profiling: a few launches of the 7B
-        # gate/up int4 GEMV (22016 x 4096) over 4 weight copies (180 MB), for
+        # gate/up int4 GEMV (22016 x 4096) over several weight copies, for
         # --batch sequences (32: the tensor-core path)
         ms, nbytes = time_dominant_gemv(fb, torch, dev, reps=3 if args.batch == 1 else 20, batch=args.batch)
         print(json.dumps({"kernel": f"int4 gemv 22016x4096 batch {args.batch}", "ms": ms, "bytes": nbytes,
@@ -331,19 +457,37 @@ def main():
         return
     B, K, W = args.batch, args.steps, max(3, args.warmup)
     r = run_decode(fb, torch, pg, local, world, rank, B, K, W)
-    extra = []
-    for B2 in args.also_batch:
-        if B2 != B:
-            r2 = run_decode(fb, torch, pg, local, world, rank, B2, max(3, K // 4), W)
-            extra.append({k: r2[k] for k in ("batch", "value", "ms_per_step", "hbm_roofline_step", "e2e", "gpu_launches")})
+    sweep = []
+    if not args.no_sweep:
+        K2 = max(3, K // 4)
+        plan = [("7b_int4_decode", b) for b in (8, 32) if b != B]
+        plan += [("1b_bf16_decode", b) for b in (1, 8, 32)]
+        plan.append(("13b_int4_tp_decode", 64))
+        for name, b2 in plan:
+            m = WORKLOADS[name]
+            if model_bytes(m, b2, m["ctx"]) / world > 0.95 * HBM_BYTES:
+                sweep.append({"workload": name, "batch": b2, "ctx": m["ctx"], "value": None,
+                              "unavailable": f"does not fit: {model_bytes(m, b2, m['ctx']) / 1e9:.1f} GB of weights "
+                                             f"and KV cache over {world} GPU(s) of {HBM_BYTES / 1e9:.0f} GB"})
+                continue
+            r2 = run_decode(fb, torch, pg, local, world, rank, b2, K2, W, name=name, e2e=False)
+            sweep.append({k: r2[k] for k in ("workload", "batch", "ctx", "value", "unit", "ms_per_step",
+                                             "hbm_roofline_step", "gpu_launches")})
+    parity = tp_parity(fb, torch, pg, local, world, rank) if world > 1 else None
     peak, peak_kind = peaks()
-    gemv_ms, gemv_bytes = time_dominant_gemv(fb, torch, dev)
+    # the dominant kernel: gate/up GEMV (at N > 1 this rank's row shard)
+    rows = 2 * (fb.tp_split(MODEL["ffn"], 128, rank, world)[1] if world > 1 else MODEL["ffn"])
+    gemv_ms, gemv_bytes = time_dominant_gemv(fb, torch, dev, N=rows)
+    gemv_ms = max_over_ranks(pg, gemv_ms)
     achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
-    prefill = None if args.no_prefill else time_prefill(fb, torch, dev)
+    prefill = None if (args.no_prefill or world > 1) else time_prefill(fb, torch, dev)
     if rank != 0:
         return
-    cpu = None if args.no_cpu else cpu_sample(B, CTX)
-    B = r["batch"]
+    cpu = None
+    if not args.no_cpu and world == 1:
+        cores = all_cores()
+        cpu = cpu_sample(B, CTX)
+        cpu["cores"] = cores
     out = {
         "metric": "decode tok/s (7B-shape int4 g128, bs%d, ctx %d)" % (B, CTX),
         "value": r["value"], "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -351,18 +495,17 @@ def main():
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "int4 weights (g128 bf16 scales), bf16 KV/head, fp32 accumulate",
         "data": "synthetic",
-        "config": {"workload": "7b_int4_decode", "n_layer": 32, "d_model": 4096, "heads": 32, "head_dim": 128,
-                   "ffn": 11008, "vocab": 32000, "batch": B, "ctx": CTX,
-                   "parallelism": f"tp{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (3.9 GB streamed per step)"},
+        "config": config_of(world, B),
         "hbm_roofline_step": r["hbm_roofline_step"],
-        "roofline": {"bound": "hbm", "kernel": "k_gemv<int4, gate/up 22016x4096>", "achieved": achieved,
-                     "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": GEMV_TRAFFIC,
+        "roofline": {"bound": "hbm", "kernel": f"k_gemv<int4, gate/up {rows}x4096>", "achieved": achieved,
+                     "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": GEMV_TRAFFIC if world == 1 else None,
                      "peak_kind": peak_kind, "launch_ms": gemv_ms, "bytes_per_launch": gemv_bytes},
         "e2e": r["e2e"],
         "gpu_launches": r["gpu_launches"],
         "clocks": r["clocks"],
-        "batch_sweep": extra,
+        "batch_sweep": sweep,
+        "tp_parity": parity,
         "prefill": prefill,
         "cpu_baseline": cpu,
     }

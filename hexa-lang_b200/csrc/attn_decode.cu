@@ -330,6 +330,9 @@ int configure_one() {
                                          200 * 1024);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_flash_decode<HD, G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    for (auto f : {k_flash_decode<HD, G, false>, k_flash_decode<HD, G, true>})
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     return e == cudaSuccess ? 0 : forge_fail(-1, "flash-decode attr: %s", cudaGetErrorString(e));
 }
 }  // namespace

@@ -229,6 +229,18 @@ __device__ void grid_arrive(const ForgeStepArgs& sa) {
     }
 }
 
+// The staging routines are inlined into the standalone GEMV; in this kernel
+// (one CTA per SM, many phase types) they stay out of line so their
+// registers do not add to every phase's.
+template <int PRO, int NT>
+__device__ __noinline__ void stage_q8_call(const ForgeGemvArgs& a, uint8_t* xq, float* sxf, int* ssum, float* red) {
+    stage_x_q8<PRO, NT>(a, xq, sxf, ssum, red);
+}
+template <int PRO, int NT>
+__device__ __noinline__ void stage_bf16_call(const ForgeGemvArgs& a, uint16_t* xf, float* red) {
+    stage_x<PRO, NT>(a, xf, red);
+}
+
 // ------------------------------------------------------------------ GEMV
 template <int WK, int PRO, int EPI>
 __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGemvArgs& a, uint32_t& it, int S) {
@@ -242,9 +254,9 @@ __device__ void gemv_phase(const Smem& m, const ForgeStepArgs& sa, const ForgeGe
     int* ssum = reinterpret_cast<int*>(m.sx + kMaxGroups * 4);
     uint8_t* xq = reinterpret_cast<uint8_t*>(m.xf);
     if (WK == FORGE_W_Q4) {
-        stage_x_q8<PRO, kNT>(a, xq, sxf, ssum, m.red);
+        stage_q8_call<PRO, kNT>(a, xq, sxf, ssum, m.red);
     } else {
-        stage_x<PRO, kNT>(a, m.xf, m.red);
+        stage_bf16_call<PRO, kNT>(a, m.xf, m.red);
         zero_x_pad<kNT>(a, m.xf);
     }
     if (PRO == FORGE_PRO_EMBED_RMSNORM && blockIdx.x == 0) {

@@ -72,6 +72,9 @@ struct ForgeGemvArgs {
     void* bscratch;        // int4, batch > 4: forge_gemv_b_scratch_bytes(K) bytes for the batched path
     const struct ForgeTpFusedDev* tpf;  // FORGE_EPI_RESID_TP: the ranks' exchange buffers (device memory)
     uint32_t* err;         // device error word
+    // Optional timeline [grid][4] %globaltimer stamps (CTA start, dependency
+    // released, activations staged, units done), FORGE_GRAPH_TRACE only.
+    unsigned long long* trace;
 };
 
 // Launches the decode GEMV (one or more launches when the batch exceeds one
@@ -115,8 +118,20 @@ struct ForgeAttnArgs {
     // table[b * max_pages + r / page_tokens]; lmax = max_pages * page_tokens.
     const int32_t* table;
     int32_t max_pages, page_tokens, num_pages;
+    // Flat kernel (attn_flat.cu): partial slots per (b, kv head); partial is
+    // [B][Hkv][flat_slots][H/Hkv][hd + 2].
+    int32_t flat_slots;
+    // Optional timeline [grid][4] (start, dependency released, first query
+    // loaded, done), flat kernel only, FORGE_GRAPH_TRACE only.
+    unsigned long long* trace;
 };
 int forge_attn_launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl);
+// Flat small-batch flash-decode (attn_flat.cu).
+bool forge_attn_flat_supported(int B, int H, int Hkv, int hd);
+int forge_attn_flat_slots(int hd, int lmax);
+int64_t forge_attn_flat_partial_floats(int B, int H, int hd, int lmax);
+int forge_attn_flat_configure();
+int forge_attn_flat_launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl);
 int forge_attn_configure();
 int forge_attn_pick_splits(int B, int Hkv, int lmax);
 int64_t forge_attn_partial_floats(int B, int H, int hd, int nsplit);

@@ -40,8 +40,16 @@ namespace {
 #ifndef FORGE_GEMV_STAGES
 #define FORGE_GEMV_STAGES 4
 #endif
-#ifndef FORGE_GEMV_MIN_BLOCKS
-#define FORGE_GEMV_MIN_BLOCKS 1
+// Registers per thread: 112 (the compiler's free choice was 148-166). The
+// register file is split over four sub-partitions of 16K registers and a
+// 9-warp CTA puts three warps on one of them; at 112 a GEMV CTA and a
+// flash-decode CTA (72) fit one SM together, so under programmatic dependent
+// launch the attention kernel's KV stream starts while the QKV projection
+// runs. Two GEMV CTAs would need 96 or fewer, which was measured slower
+// (the weight stream of the next GEMV overlaps less than the lost registers
+// cost in the MMA loop).
+#ifndef FORGE_GEMV_MAXNREG
+#define FORGE_GEMV_MAXNREG 112
 #endif
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
@@ -140,7 +148,7 @@ __device__ __noinline__ void tp_resid_finish(const ForgeGemvArgs& a, int u, int 
 }
 
 template <int WK, int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const ForgeGemvArgs a) {
+__global__ void __maxnreg__(FORGE_GEMV_MAXNREG) k_gemv(const ForgeGemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* stages = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -161,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const 
     const int units = a.N >> 4;
 
     if (threadIdx.x == 0) {
+        if (a.trace) a.trace[blockIdx.x * 4 + 0] = globaltimer_ns();
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
@@ -206,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const 
 
     // ---------------------------------------------------------- consumers
     pdl_wait();
+    if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4 + 1] = globaltimer_ns();
     if (WK == FORGE_W_Q4) {
         stage_x_q8<PRO, 256>(a, xq, sxf, ssum, red);
     } else {
@@ -213,6 +223,7 @@ __global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const 
         zero_x_pad<256>(a, xf);
     }
     named_bar_sync(1, 256);
+    if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4 + 2] = globaltimer_ns();
 
     const int g = lane >> 2, t = lane & 3;
     const int ncols = (WK == FORGE_W_Q4 || a.split) ? 2 * a.batch : a.batch;
@@ -340,6 +351,7 @@ __global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const 
                 epilogue<EPI>(a, u, p, b, ylo, yhi, best);
         }
     }
+    if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4 + 3] = globaltimer_ns();
     if (EPI == FORGE_EPI_RESID_TP && warp == 0 && __all_sync(0xffffffffu, ok)) {
         const int tid = threadIdx.x;
         for (int u = blockIdx.x; u < units; u += gridDim.x) tp_resid_finish(a, u, tid & 7, tid >> 3, tid < 8 * a.batch);
@@ -361,6 +373,12 @@ __global__ void __launch_bounds__(kThreads, FORGE_GEMV_MIN_BLOCKS) k_gemv(const 
 template <int WK, int PRO, int EPI>
 int configure_one() {
     cudaError_t e = cudaFuncSetAttribute(k_gemv<WK, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    // every decode kernel asks for the largest shared-memory carveout, so an
+    // SM never has to be reconfigured (which needs it idle) before the next
+    // kernel's CTA can join the one still running there
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemv<WK, PRO, EPI>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
     return e == cudaSuccess ? 0 : forge_fail(-1, "gemv: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
 }
 template <int WK, int PRO>

@@ -522,6 +522,8 @@ int forge_gemv_b_configure() {
     cudaError_t e = cudaSuccess;
     auto set = [&](const void* f) {
         if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     };
 #define FORGE_SET_B(E) \
     set((const void*)k_gemv_b<E, 2>); set((const void*)k_gemv_b<E, 4>); set((const void*)k_gemv_b<E, 8>)

@@ -37,7 +37,7 @@ __device__ __forceinline__ float4 load_x4(const ForgeGemvArgs& a, int b, const f
 // bf16-weight prologue (consumer warps): optional RMSNorm, hi/lo bf16 split,
 // fragment-order store.
 template <int PRO, int NT>
-__device__ __noinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, float* red) {
+__device__ __forceinline__ void stage_x(const ForgeGemvArgs& a, uint16_t* xf, float* red) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.K;
     const int ncols = a.split ? 2 * a.batch : a.batch;
@@ -184,7 +184,7 @@ __device__ __forceinline__ int xq_index(int k, int col, int ncols) {
 // and the column sums of hi and lo (ssum[g][2b], ssum[g][2b+1]) that remove
 // the +7 code bias of the weights after the integer dot product.
 template <int PRO, int NT, int MAXP = 3>
-__device__ __noinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, float* sxf, int* ssum,
+__device__ __forceinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, float* sxf, int* ssum,
                                         float* red) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.K;
@@ -271,21 +271,25 @@ __device__ __noinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, flo
             for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
             const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
             const float is = amax > 0.f ? 127.0f / amax : 0.0f;
+            const float is256 = 256.0f * is;
             int shi = 0, slo = 0;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                uint32_t hw = 0, lw = 0;
+                int hi[4], lo[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const float x = e[4 * c + j];
-                    const float hq = fminf(fmaxf(rintf(x * is), -127.f), 127.f);
-                    const float lq = fminf(fmaxf(rintf((x - sc * hq) * (256.0f * is)), -127.f), 127.f);
-                    const int hi = (int)hq, lo = (int)lq;
-                    shi += hi;
-                    slo += lo;
-                    hw |= (uint32_t)(hi & 0xFF) << (8 * j);
-                    lw |= (uint32_t)(lo & 0xFF) << (8 * j);
+                    // |x| <= amax, so x * is rounds into [-127, 127]: no clamp
+                    const float hq = rintf(x * is);
+                    const float lq = fminf(fmaxf(rintf((x - sc * hq) * is256), -127.f), 127.f);
+                    hi[j] = (int)hq;
+                    lo[j] = (int)lq;
                 }
+                // low bytes of four ints into one word (byte j = element j)
+                const uint32_t hw = __byte_perm(__byte_perm(hi[0], hi[1], 0x0040), __byte_perm(hi[2], hi[3], 0x0040), 0x5410);
+                const uint32_t lw = __byte_perm(__byte_perm(lo[0], lo[1], 0x0040), __byte_perm(lo[2], lo[3], 0x0040), 0x5410);
+                shi = __dp4a((int)hw, 0x01010101, shi);  // sum of the four signed bytes
+                slo = __dp4a((int)lw, 0x01010101, slo);
                 if (k0 < K) {
                     *reinterpret_cast<uint32_t*>(xq + xq_index(k0 + 4 * c, 2 * b, ncols)) = hw;
                     *reinterpret_cast<uint32_t*>(xq + xq_index(k0 + 4 * c, 2 * b + 1, ncols)) = lw;

@@ -563,6 +563,8 @@ int forge_gemv_tc_configure() {
     cudaError_t e = cudaSuccess;
     auto set = [&](const void* f, int bytes) {
         if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     };
     set((const void*)k_gemv_tc<FORGE_EPI_STORE>, kSmem);
     set((const void*)k_gemv_tc<FORGE_EPI_RESID>, kSmem);

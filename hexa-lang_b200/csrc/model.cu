@@ -110,6 +110,7 @@ struct ForgeB200 {
     float* partial = nullptr;
     uint32_t* counters = nullptr;
     int nsplit = 1;
+    bool flat_attn = false;  // small batches on attn_flat.cu (FORGE_ATTN=flat)
     uint32_t* err = nullptr;
     uint16_t *stA = nullptr, *stB = nullptr;
     uint8_t* codes = nullptr;
@@ -125,6 +126,9 @@ struct ForgeB200 {
     int force_graph = 0;
     unsigned long long* trace = nullptr;  // fused-step timeline (FORGE_STEP_TRACE)
     int trace_n = 0;
+    // multi-kernel step timeline (FORGE_GRAPH_TRACE): [node][grid][4] stamps
+    unsigned long long* gtrace = nullptr;
+    int gtrace_cap = 0, gtrace_next = 0;
     std::vector<void*> allocs;
     bool weights_ready = false;
     // tensor parallel shard (tp_size 1: the whole model). H, Hkv, F, V and
@@ -326,6 +330,12 @@ int resid_gemv(ForgeB200* h, ForgeGemvArgs& g, float* x, int B, bool pdl) {
     return tp_sum(h, x, B);
 }
 
+// Next node's slot of the multi-kernel step timeline (or null).
+unsigned long long* trace_slot(ForgeB200* h) {
+    if (!h->gtrace || h->gtrace_next >= h->gtrace_cap) return nullptr;
+    return h->gtrace + (size_t)(h->gtrace_next++) * forge_sm_count() * 4;
+}
+
 // RMSNorm + QKV + RoPE, K/V appended at each sequence's position.
 int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl) {
     const LayerDev& Ld = h->layers[l];
@@ -335,6 +345,7 @@ int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl) 
     g.epi = FORGE_EPI_QKV; g.q_out = q; g.kc = h->kc + (size_t)l * h->kv_layer; g.vc = h->vc + (size_t)l * h->kv_layer;
     g.pos = h->pos; g.H = h->H; g.Hkv = h->Hkv; g.hd = h->hd; g.lmax = h->lmax;
     g.rope_cos = h->rope_cos; g.rope_sin = h->rope_sin;
+    g.trace = trace_slot(h);
     return forge_gemv_launch(g, h->stream, pdl);
 }
 
@@ -343,8 +354,13 @@ int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pd
     ForgeAttnArgs at{};
     at.q = q; at.kc = h->kc + (size_t)l * h->kv_layer; at.vc = h->vc + (size_t)l * h->kv_layer; at.pos = h->pos;
     at.B = B; at.H = h->H; at.Hkv = h->Hkv; at.hd = h->hd; at.lmax = h->lmax;
-    at.nsplit = forge_attn_pick_splits(B, h->Hkv, h->lmax);
     at.partial = h->partial; at.counters = h->counters; at.out = ctx; at.err = h->err;
+    at.trace = trace_slot(h);
+    if (h->flat_attn && forge_attn_flat_supported(B, h->H, h->Hkv, h->hd)) {
+        at.flat_slots = forge_attn_flat_slots(h->hd, h->lmax);
+        return forge_attn_flat_launch(at, h->stream, pdl);
+    }
+    at.nsplit = forge_attn_pick_splits(B, h->Hkv, h->lmax);
     return forge_attn_launch(at, h->stream, pdl);
 }
 
@@ -354,6 +370,7 @@ int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool p
     ForgeGemvArgs g = gemv_base(h, B);
     g.w = Ld.o_w; g.s = Ld.o_s; g.N = h->d; g.K = h->qd; g.x = ctx; g.x_stride = h->qd;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
+    g.trace = trace_slot(h);
     return resid_gemv(h, g, x, B, pdl);
 }
 
@@ -364,10 +381,12 @@ int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl) {
     g.w = Ld.gu_w; g.s = Ld.gu_s; g.N = 2 * h->F; g.K = h->d; g.x = x; g.x_stride = h->d;
     g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g2; g.eps = h->desc.rms_eps;
     g.epi = FORGE_EPI_SWIGLU; g.s_out = h->s; g.F = h->F;
+    g.trace = trace_slot(h);
     if (forge_gemv_launch(g, h->stream, pdl)) return -1;
     g = gemv_base(h, B);
     g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = h->s; g.x_stride = h->F;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
+    g.trace = trace_slot(h);
     return resid_gemv(h, g, x, B, pdl);
 }
 
@@ -379,6 +398,7 @@ int enqueue_head(ForgeB200* h, int B, const float* x, bool pdl) {
     g.pro = FORGE_PRO_RMSNORM; g.gain = h->gF; g.eps = h->desc.rms_eps;
     g.epi = FORGE_EPI_LOGITS; g.y = h->logits; g.y_stride = h->Vpad; g.argmax_key = h->amax; g.nvalid = h->V;
     g.row_off = h->v0;
+    g.trace = trace_slot(h);
     if (forge_gemv_launch(g, h->stream, pdl)) return -1;
     return h->comm ? forge_tp_allreduce_max_u64(h->comm, h->amax, (size_t)B, h->stream) : 0;
 }
@@ -521,7 +541,12 @@ cudaGraphExec_t graph_for(ForgeB200* h, int B) {
         forge_fail(-1, "forge_b200: begin capture failed");
         return nullptr;
     }
+    h->gtrace_next = 0;
     int rc = enqueue_step(h, B);
+    if (h->gtrace) {
+        h->trace = h->gtrace;
+        h->trace_n = h->gtrace_next;
+    }
     cudaError_t e = cudaStreamEndCapture(h->stream, &graph);
     if (rc || e != cudaSuccess) {
         if (graph) cudaGraphDestroy(graph);
@@ -627,7 +652,8 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
     cudaGetDeviceProperties(&prop, device);
     if (prop.major != 10) return forge_fail(FORGE_KERNEL_UNSUPPORTED, "forge_b200_create: needs an sm_100 device (got sm_%d%d)", prop.major, prop.minor);
 
-    if (forge_gemv_configure() || forge_gemv_b_configure() || forge_attn_configure()) return -1;
+    if (forge_gemv_configure() || forge_gemv_b_configure() || forge_attn_configure() || forge_attn_flat_configure())
+        return -1;
     forge_sm_count();
     ForgeB200* h = new ForgeB200();
     h->desc = m;
@@ -683,7 +709,18 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
         int ns = fused_splits(h, B);
         if (ns * B > max_split) max_split = ns * B;
     }
-    h->partial = (float*)h->alloc(sizeof(float) * (size_t)max_split * h->H * (h->hd + 2));
+    size_t partial_floats = (size_t)max_split * h->H * (h->hd + 2);
+    {
+        // FORGE_ATTN=flat: the flat small-batch flash-decode (attn_flat.cu) for up to 32
+        // sequences; by default the per-(sequence, head, split) kernel, which is faster
+        // at batch 1 as measured so far
+        const char* e = getenv("FORGE_ATTN");
+        h->flat_attn = e && strcmp(e, "flat") == 0;
+        for (int B = 1; B <= h->Bmax; ++B)
+            if (h->flat_attn && forge_attn_flat_supported(B, h->H, h->Hkv, h->hd))
+                partial_floats = std::max(partial_floats, (size_t)forge_attn_flat_partial_floats(B, h->H, h->hd, h->lmax));
+    }
+    h->partial = (float*)h->alloc(sizeof(float) * partial_floats);
     h->bar = (unsigned long long*)h->alloc(16);
     h->epoch = (uint32_t*)h->alloc(16);
     {
@@ -693,6 +730,12 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
         h->force_graph = (e && strcmp(e, "fused") == 0) ? 0 : 1;
     }
     h->counters = (uint32_t*)h->alloc(4 * (size_t)h->Bmax * h->Hkv);
+    if (getenv("FORGE_GRAPH_TRACE")) {
+        h->gtrace_cap = 5 * h->L + 2;
+        const size_t n = (size_t)h->gtrace_cap * forge_sm_count() * 4;
+        h->gtrace = (unsigned long long*)h->alloc(8 * n);
+        if (h->gtrace) cudaMemset(h->gtrace, 0, 8 * n);
+    }
     h->err = (uint32_t*)h->alloc(16);
     if (h->Bmax > 4) {  // batched GEMV path (int4 above 4 sequences, bf16 above 8); starts zeroed
         const size_t nb = (size_t)forge_gemv_b_scratch_bytes(std::max({h->d, h->qd, h->F}));

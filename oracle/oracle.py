@@ -147,21 +147,26 @@ class OracleModel:
     head t=1 and layer l matrix j at t = 2 + 7*l + j; gains are 1.0."""
 
     def __init__(self, n_layer, d, n_head, n_kv, hd, ffn, vocab, *, q4=False, tied=False,
-                 eps=1e-5, theta=10000.0, seed=1234, std=0.02, weights=None):
+                 eps=1e-5, theta=10000.0, seed=1234, std=0.02, weights=None, keep_bf16=True):
+        """keep_bf16=False (synthetic int4 models only): each layer matrix is
+        generated, quantised and its bf16 copy dropped, so a full-size model
+        (7B: 13 GB of bf16) holds only its int4 codes and scales."""
         self.cfg = dict(n_layer=n_layer, d=d, n_head=n_head, n_kv=n_kv, hd=hd, ffn=ffn, vocab=vocab)
         self.q4, self.tied = q4, tied
         shapes = {"wq": (n_head * hd, d), "wk": (n_kv * hd, d), "wv": (n_kv * hd, d),
                   "wo": (d, n_head * hd), "wg": (ffn, d), "wu": (ffn, d), "wd": (d, ffn)}
         self.keep = []
         self.bf16 = {}   # logical bf16 weights (what the device is given)
+        lazy = weights is None and q4 and not keep_bf16
         if weights is None:
             self.bf16["emb"] = fill_normal_bf16(vocab * d, seed, 0, std).reshape(vocab, d)
             if not tied:
                 self.bf16["head"] = fill_normal_bf16(vocab * d, seed, 1 << 40, std).reshape(vocab, d)
-            for l in range(n_layer):
-                for j, nm in enumerate(MAT_NAMES):
-                    r, c = shapes[nm]
-                    self.bf16[(l, nm)] = fill_normal_bf16(r * c, seed, (2 + 7 * l + j) << 40, std).reshape(r, c)
+            if not lazy:
+                for l in range(n_layer):
+                    for j, nm in enumerate(MAT_NAMES):
+                        r, c = shapes[nm]
+                        self.bf16[(l, nm)] = fill_normal_bf16(r * c, seed, (2 + 7 * l + j) << 40, std).reshape(r, c)
             self.gains = {k: np.ones(d, np.float32) for k in
                           ["gF"] + [(l, g) for l in range(n_layer) for g in ("g1", "g2")]}
         else:
@@ -171,8 +176,14 @@ class OracleModel:
             L = self.layers[l]
             L.g1 = P(self._k(self.gains[(l, "g1")]))
             L.g2 = P(self._k(self.gains[(l, "g2")]))
-            for nm in MAT_NAMES:
-                setattr(L, nm, self._mat(self.bf16[(l, nm)], q4))
+            for j, nm in enumerate(MAT_NAMES):
+                if lazy:
+                    r, c = shapes[nm]
+                    w = fill_normal_bf16(r * c, seed, (2 + 7 * l + j) << 40, std).reshape(r, c)
+                    setattr(L, nm, self._mat(w, q4))
+                    del w
+                else:
+                    setattr(L, nm, self._mat(self.bf16[(l, nm)], q4))
         m = OrModel()
         m.n_layer, m.d, m.n_head, m.n_kv, m.hd, m.ffn, m.vocab = n_layer, d, n_head, n_kv, hd, ffn, vocab
         m.eps, m.theta = eps, theta

@@ -73,3 +73,29 @@ def test_flash_prefill_dispatch_family(forge, cuda):
     assert (o - ref).abs().max().item() <= 2e-2
     for d in descs + [out]:
         L.hexa_farr_bf16_free(d)
+
+
+def test_flash_prefill_benchmark_shape(forge, cuda):
+    """The benchmark's prefill (B 8, H 32, S 4096, head dim 128, causal): the
+    whole launch runs; eight (batch, head) pairs spread over the grid are
+    compared with the fp32 reference row by row (every query row of 4096),
+    plus a B 1, H 4 launch at the same length checked in full."""
+    import torch
+    for B, H, pairs in ((1, 4, [(0, h) for h in range(4)]),
+                        (8, 32, [(0, 0), (1, 31), (2, 7), (3, 16), (4, 3), (5, 28), (6, 12), (7, 21)])):
+        S = 4096
+        g = torch.Generator(device=cuda).manual_seed(4096 + B)
+        q, k, v = (torch.randn(B, H, S, 128, generator=g, device=cuda).to(torch.bfloat16) for _ in range(3))
+        o = torch.full_like(q, float("nan"))
+        torch.cuda.synchronize()
+        forge.check(forge.lib().forge_flash_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S,
+                                                    128, 1, torch.cuda.current_stream().cuda_stream), "prefill")
+        torch.cuda.synchronize()
+        forge.check(forge.lib().forge_ops_check(), "prefill error word")
+        assert torch.isfinite(o.float()).all()
+        for b, h in pairs:
+            ref = _ref(torch, q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1], v[b:b + 1, h:h + 1], True)
+            err = (o[b:b + 1, h:h + 1].float() - ref).abs()
+            assert err.max().item() <= 2e-2, (B, H, b, h, err.max().item())
+            assert err.mean().item() <= 2e-3, (B, H, b, h, err.mean().item())
+        del q, k, v, o
