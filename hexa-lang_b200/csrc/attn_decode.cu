@@ -67,7 +67,8 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
     const int j1 = min(Lc, j0 + chunk);
     const int n = max(0, j1 - j0);
     const int ntiles = (n + kTile - 1) / kTile;
-    const size_t slab = ((size_t)b * a.Hkv + kvh) * a.lmax * HD;
+    const int sq = a.seq_of ? a.seq_of[b] : b;  // cache sequence of query row b
+    const size_t slab = ((size_t)sq * a.Hkv + kvh) * a.lmax * HD;
     constexpr bool paged = PAGED;
     const int32_t* ptab = paged ? a.table + (size_t)b * a.max_pages : nullptr;
     // row r of this (sequence, kv head)

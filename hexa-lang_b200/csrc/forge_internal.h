@@ -75,6 +75,9 @@ struct ForgeGemvArgs {
     // Optional timeline [grid][4] %globaltimer stamps (CTA start, dependency
     // released, activations staged, units done), FORGE_GRAPH_TRACE only.
     unsigned long long* trace;
+    // Prompt prefill: row b of the launch is position pos[b] of cache
+    // sequence seq_of[b] (null: row b is sequence b).
+    const int32_t* seq_of;
 };
 
 // Launches the decode GEMV (one or more launches when the batch exceeds one
@@ -124,6 +127,9 @@ struct ForgeAttnArgs {
     // Optional timeline [grid][4] (start, dependency released, first query
     // loaded, done), flat kernel only, FORGE_GRAPH_TRACE only.
     unsigned long long* trace;
+    // Prompt prefill (split kernel, contiguous cache): query row b attends
+    // to rows 0..pos[b] of cache sequence seq_of[b] (null: sequence b).
+    const int32_t* seq_of;
 };
 int forge_attn_launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl);
 // Flat small-batch flash-decode (attn_flat.cu).

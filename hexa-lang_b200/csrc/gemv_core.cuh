@@ -130,7 +130,8 @@ __device__ __forceinline__ void epilogue(const ForgeGemvArgs& a, int u, int p, i
         const int c = 8 * i + p, c2 = c + hd / 2;
         const int bg = a.b0 + b;
         const int P = a.pos[bg];
-        if (P < 0 || P >= a.lmax) { atomicOr(a.err, FORGE_DEVERR_BAD_INDEX); return; }
+        const int sq = a.seq_of ? a.seq_of[bg] : bg;  // cache sequence of this row
+        if (P < 0 || P >= a.lmax || sq < 0) { atomicOr(a.err, FORGE_DEVERR_BAD_INDEX); return; }
         if (head < a.H + a.Hkv) {
             const float cs = a.rope_cos[(size_t)P * (hd / 2) + c];
             const float sn = a.rope_sin[(size_t)P * (hd / 2) + c];
@@ -141,12 +142,12 @@ __device__ __forceinline__ void epilogue(const ForgeGemvArgs& a, int u, int p, i
                 q[c] = o1;
                 q[c2] = o2;
             } else {
-                uint16_t* k = a.kc + (((size_t)bg * a.Hkv + (head - a.H)) * a.lmax + P) * hd;
+                uint16_t* k = a.kc + (((size_t)sq * a.Hkv + (head - a.H)) * a.lmax + P) * hd;
                 k[c] = f32_to_bf16_bits(o1);
                 k[c2] = f32_to_bf16_bits(o2);
             }
         } else {
-            uint16_t* v = a.vc + (((size_t)bg * a.Hkv + (head - a.H - a.Hkv)) * a.lmax + P) * hd;
+            uint16_t* v = a.vc + (((size_t)sq * a.Hkv + (head - a.H - a.Hkv)) * a.lmax + P) * hd;
             v[c] = f32_to_bf16_bits(ylo);
             v[c2] = f32_to_bf16_bits(yhi);
         }

@@ -126,6 +126,14 @@ struct ForgeB200 {
     int force_graph = 0;
     unsigned long long* trace = nullptr;  // fused-step timeline (FORGE_STEP_TRACE)
     int trace_n = 0;
+    // prompt prefill rows (grown on demand): activations, per-row token /
+    // position / sequence, split partials and merge counters
+    struct {
+        int64_t cap = 0;
+        float *x = nullptr, *q = nullptr, *ctx = nullptr, *s = nullptr, *partial = nullptr;
+        int32_t *tok = nullptr, *pos = nullptr, *seq = nullptr;
+        uint32_t* counters = nullptr;
+    } pre;
     // multi-kernel step timeline (FORGE_GRAPH_TRACE): [node][grid][4] stamps
     unsigned long long* gtrace = nullptr;
     int gtrace_cap = 0, gtrace_next = 0;
@@ -336,26 +344,50 @@ unsigned long long* trace_slot(ForgeB200* h) {
     return h->gtrace + (size_t)(h->gtrace_next++) * forge_sm_count() * 4;
 }
 
+// Prompt prefill: every row of a launch is one prompt position of one
+// sequence (row -> position, row -> cache sequence), with its own split
+// partials and merge counters; `exact` keeps hi/lo activations for bf16
+// weights at any row count.
+struct RowMap {
+    const int32_t* pos;
+    const int32_t* seq;
+    float* partial;
+    uint32_t* counters;
+    bool exact;
+};
+
 // RMSNorm + QKV + RoPE, K/V appended at each sequence's position.
-int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl) {
+int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl, const RowMap* rm = nullptr) {
     const LayerDev& Ld = h->layers[l];
     ForgeGemvArgs g = gemv_base(h, B);
+    if (rm && rm->exact) g.split = 1;
     g.w = Ld.qkv_w; g.s = Ld.qkv_s; g.N = h->nqkv; g.K = h->d;
     g.x = x; g.x_stride = h->d; g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g1; g.eps = h->desc.rms_eps;
     g.epi = FORGE_EPI_QKV; g.q_out = q; g.kc = h->kc + (size_t)l * h->kv_layer; g.vc = h->vc + (size_t)l * h->kv_layer;
     g.pos = h->pos; g.H = h->H; g.Hkv = h->Hkv; g.hd = h->hd; g.lmax = h->lmax;
     g.rope_cos = h->rope_cos; g.rope_sin = h->rope_sin;
     g.trace = trace_slot(h);
+    if (rm) {
+        g.pos = rm->pos;
+        g.seq_of = rm->seq;
+    }
     return forge_gemv_launch(g, h->stream, pdl);
 }
 
 // Split-K flash-decode over positions 0..pos of every sequence.
-int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pdl) {
+int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pdl, const RowMap* rm = nullptr) {
     ForgeAttnArgs at{};
     at.q = q; at.kc = h->kc + (size_t)l * h->kv_layer; at.vc = h->vc + (size_t)l * h->kv_layer; at.pos = h->pos;
     at.B = B; at.H = h->H; at.Hkv = h->Hkv; at.hd = h->hd; at.lmax = h->lmax;
     at.partial = h->partial; at.counters = h->counters; at.out = ctx; at.err = h->err;
     at.trace = trace_slot(h);
+    if (rm) {
+        // every cached row of a prompt row was written by this pass's QKV
+        // kernel: no copies before the dependency, so no programmatic launch
+        at.pos = rm->pos; at.seq_of = rm->seq; at.partial = rm->partial; at.counters = rm->counters;
+        at.nsplit = forge_attn_pick_splits(B, h->Hkv, h->lmax);
+        return forge_attn_launch(at, h->stream, false);
+    }
     if (h->flat_attn && forge_attn_flat_supported(B, h->H, h->Hkv, h->hd)) {
         at.flat_slots = forge_attn_flat_slots(h->hd, h->lmax);
         return forge_attn_flat_launch(at, h->stream, pdl);
@@ -365,9 +397,10 @@ int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pd
 }
 
 // x += Wo ctx
-int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool pdl) {
+int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool pdl, const RowMap* rm = nullptr) {
     const LayerDev& Ld = h->layers[l];
     ForgeGemvArgs g = gemv_base(h, B);
+    if (rm && rm->exact) g.split = 1;
     g.w = Ld.o_w; g.s = Ld.o_s; g.N = h->d; g.K = h->qd; g.x = ctx; g.x_stride = h->qd;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
     g.trace = trace_slot(h);
@@ -375,26 +408,30 @@ int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool p
 }
 
 // x += Wd (silu(Wg n) * (Wu n)), n = RMSNorm(x) * g2
-int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl) {
+int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl, const RowMap* rm = nullptr, float* s = nullptr) {
     const LayerDev& Ld = h->layers[l];
+    const bool exact = rm && rm->exact;
+    if (!s) s = h->s;
     ForgeGemvArgs g = gemv_base(h, B);
+    if (exact) g.split = 1;
     g.w = Ld.gu_w; g.s = Ld.gu_s; g.N = 2 * h->F; g.K = h->d; g.x = x; g.x_stride = h->d;
     g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g2; g.eps = h->desc.rms_eps;
-    g.epi = FORGE_EPI_SWIGLU; g.s_out = h->s; g.F = h->F;
+    g.epi = FORGE_EPI_SWIGLU; g.s_out = s; g.F = h->F;
     g.trace = trace_slot(h);
     if (forge_gemv_launch(g, h->stream, pdl)) return -1;
     g = gemv_base(h, B);
-    g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = h->s; g.x_stride = h->F;
+    if (exact) g.split = 1;
+    g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = s; g.x_stride = h->F;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
     g.trace = trace_slot(h);
     return resid_gemv(h, g, x, B, pdl);
 }
 
 // final RMSNorm + LM head into the handle's logits, argmax keys updated
-int enqueue_head(ForgeB200* h, int B, const float* x, bool pdl) {
+int enqueue_head(ForgeB200* h, int B, const float* x, bool pdl, int x_stride = 0) {
     ForgeGemvArgs g = gemv_base(h, B);
     g.wkind = FORGE_W_BF16;
-    g.w = h->head_w; g.s = nullptr; g.N = h->Vpad; g.K = h->d; g.x = x; g.x_stride = h->d;
+    g.w = h->head_w; g.s = nullptr; g.N = h->Vpad; g.K = h->d; g.x = x; g.x_stride = x_stride ? x_stride : h->d;
     g.pro = FORGE_PRO_RMSNORM; g.gain = h->gF; g.eps = h->desc.rms_eps;
     g.epi = FORGE_EPI_LOGITS; g.y = h->logits; g.y_stride = h->Vpad; g.argmax_key = h->amax; g.nvalid = h->V;
     g.row_off = h->v0;
@@ -830,6 +867,9 @@ FORGE_API void forge_b200_destroy(ForgeB200* h) {
     if (h->ar) forge_tp_ar_destroy(h->ar);
     if (h->comm) forge_tp_comm_destroy(h->comm);  // after the graphs that hold its collectives
     for (void* p : h->allocs) cudaFree(p);
+    for (void* p : {(void*)h->pre.x, (void*)h->pre.q, (void*)h->pre.ctx, (void*)h->pre.s, (void*)h->pre.partial,
+                    (void*)h->pre.tok, (void*)h->pre.pos, (void*)h->pre.seq, (void*)h->pre.counters})
+        if (p) cudaFree(p);
     if (h->h_tok) cudaFreeHost(h->h_tok);
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;
@@ -945,6 +985,26 @@ int enqueue_one(ForgeB200* h, int B) {
     return cudaGraphLaunch(g, h->stream) == cudaSuccess ? 0 : forge_fail(-1, "forge_b200: graph launch failed");
 }
 
+// Enqueues the copy of the last head's logits [batch][vocab] to the host
+// (under tensor parallelism every rank holds one vocabulary slice: they are
+// gathered first, and every rank calls this).
+int enqueue_logits_copy(ForgeB200* h, int batch, float* logits) {
+    if (!h->comm) {
+        cudaMemcpy2DAsync(logits, sizeof(float) * h->V, h->logits, sizeof(float) * h->Vpad, sizeof(float) * h->V,
+                          batch, cudaMemcpyDeviceToHost, h->stream);
+        return 0;
+    }
+    const size_t per = (size_t)batch * h->Vpad;
+    if (forge_tp_allgather_f32(h->comm, h->logits, h->logits_all, per, h->stream)) return -1;
+    for (int r = 0; r < h->tp_size; ++r) {
+        const int nv = std::max(0, std::min(h->Vpad, h->Vfull - r * h->Vpad));
+        if (nv)
+            cudaMemcpy2DAsync(logits + (size_t)r * h->Vpad, sizeof(float) * h->Vfull, h->logits_all + r * per,
+                              sizeof(float) * h->Vpad, sizeof(float) * nv, batch, cudaMemcpyDeviceToHost, h->stream);
+    }
+    return 0;
+}
+
 FORGE_API int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tokens, int32_t* next_tokens, float* logits) {
     if (int rc = check_ready(h, batch)) return rc;
     if (!tokens) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_decode_step: null tokens");
@@ -954,20 +1014,7 @@ FORGE_API int forge_b200_decode_step(ForgeB200* h, int batch, const int32_t* tok
     cudaMemcpyAsync(h->tok, stage, 4 * batch, cudaMemcpyHostToDevice, h->stream);
     if (enqueue_one(h, batch)) return -1;
     if (next_tokens) cudaMemcpyAsync(stage, h->tok, 4 * batch, cudaMemcpyDeviceToHost, h->stream);
-    if (logits && !h->comm) {
-        cudaMemcpy2DAsync(logits, sizeof(float) * h->V, h->logits, sizeof(float) * h->Vpad, sizeof(float) * h->V,
-                          batch, cudaMemcpyDeviceToHost, h->stream);
-    } else if (logits) {
-        // every rank holds one vocabulary slice: gather them (all ranks call this)
-        const size_t per = (size_t)batch * h->Vpad;
-        if (forge_tp_allgather_f32(h->comm, h->logits, h->logits_all, per, h->stream)) return -1;
-        for (int r = 0; r < h->tp_size; ++r) {
-            const int nv = std::max(0, std::min(h->Vpad, h->Vfull - r * h->Vpad));
-            if (nv)
-                cudaMemcpy2DAsync(logits + (size_t)r * h->Vpad, sizeof(float) * h->Vfull, h->logits_all + r * per,
-                                  sizeof(float) * h->Vpad, sizeof(float) * nv, batch, cudaMemcpyDeviceToHost, h->stream);
-        }
-    }
+    if (logits && enqueue_logits_copy(h, batch, logits)) return -1;
     if (cudaStreamSynchronize(h->stream) != cudaSuccess)
         return forge_fail(-1, "forge_b200_decode_step: %s", cudaGetErrorString(cudaGetLastError()));
     if (next_tokens) memcpy(next_tokens, stage, 4 * batch);
@@ -1070,26 +1117,106 @@ FORGE_API int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps) {
     return 0;
 }
 
+namespace {
+// Grows the prefill buffers to R rows (outside any stream capture).
+int prefill_reserve(ForgeB200* h, int64_t R) {
+    auto& P = h->pre;
+    if (R <= P.cap) return 0;
+    cudaStreamSynchronize(h->stream);
+    for (void* p : {(void*)P.x, (void*)P.q, (void*)P.ctx, (void*)P.s, (void*)P.partial, (void*)P.tok, (void*)P.pos,
+                    (void*)P.seq, (void*)P.counters})
+        if (p) cudaFree(p);
+    P = {};
+    int64_t part = 0;  // split partials for any row count up to R
+    for (int64_t r = 1; r <= R; ++r)
+        part = std::max(part, r * forge_attn_pick_splits((int)r, h->Hkv, h->lmax));
+    bool ok = cudaMalloc(&P.x, 4 * R * h->d) == cudaSuccess && cudaMalloc(&P.q, 4 * R * h->qd) == cudaSuccess &&
+              cudaMalloc(&P.ctx, 4 * R * h->qd) == cudaSuccess && cudaMalloc(&P.s, 4 * R * h->F) == cudaSuccess &&
+              cudaMalloc(&P.partial, 4 * part * h->H * (h->hd + 2)) == cudaSuccess &&
+              cudaMalloc(&P.tok, 4 * R) == cudaSuccess && cudaMalloc(&P.pos, 4 * R) == cudaSuccess &&
+              cudaMalloc(&P.seq, 4 * R) == cudaSuccess && cudaMalloc(&P.counters, 4 * R * h->Hkv) == cudaSuccess &&
+              cudaMemset(P.counters, 0, 4 * R * h->Hkv) == cudaSuccess;
+    if (ok && !h->bscratch) {  // the batched GEMV paths (more than 4 rows)
+        const size_t nb = (size_t)forge_gemv_b_scratch_bytes(std::max({h->d, h->qd, h->F}));
+        h->bscratch = h->alloc(nb);
+        ok = h->bscratch && cudaMemset(h->bscratch, 0, nb) == cudaSuccess;
+    }
+    if (!ok) {
+        cudaGetLastError();
+        return forge_fail(-1, "forge_b200_prefill: out of device memory for %lld rows", (long long)R);
+    }
+    P.cap = R;
+    return 0;
+}
+
+// All prompt positions of `batch` sequences through the model at once.
+int prefill_impl(ForgeB200* h, int batch, const int32_t* prompt, int n, int exact_mode) {
+    const int64_t R = (int64_t)batch * n;
+    if (int rc = prefill_reserve(h, R)) return rc;
+    auto& P = h->pre;
+    std::vector<int32_t> tok(R), pos(R), seq(R);
+    for (int b = 0; b < batch; ++b)
+        for (int p = 0; p < n; ++p) {
+            const int64_t r = (int64_t)b * n + p;
+            tok[r] = prompt[r];
+            pos[r] = p;
+            seq[r] = b;
+            if (tok[r] < 0 || tok[r] >= h->Vfull)
+                return forge_fail(FORGE_INVALID_ARGS, "forge_b200_prefill: token %d outside the vocabulary", tok[r]);
+        }
+    cudaStream_t st = h->stream;
+    if (cudaMemcpyAsync(P.tok, tok.data(), 4 * R, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(P.pos, pos.data(), 4 * R, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(P.seq, seq.data(), 4 * R, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_prefill: H2D of the prompt failed");
+    // exact_mode: 1 hi/lo activations for bf16 weights at any row count,
+    // 0 the model's own activation policy (bf16 activations above 4 rows)
+    const RowMap rm{P.pos, P.seq, P.partial, P.counters, exact_mode == 1};
+    int rc = forge_embed_launch(h->emb, h->d, h->Vfull, P.tok, (int)R, P.x, h->err, st, false);
+    for (int l = 0; l < h->L && !rc; ++l)
+        rc = enqueue_qkv(h, l, (int)R, P.x, P.q, true, &rm) || enqueue_attn(h, l, (int)R, P.q, P.ctx, false, &rm) ||
+             enqueue_oproj(h, l, (int)R, P.ctx, P.x, true, &rm) || enqueue_mlp(h, l, (int)R, P.x, true, &rm, P.s);
+    if (rc) return -1;
+    // last position of every sequence: final norm, LM head, argmax; the
+    // finaliser records the token as step n-1 and moves the positions to n
+    if (enqueue_head(h, batch, P.x + (size_t)(n - 1) * h->d, true, n * h->d)) return -1;
+    k_set_i32<<<1, 256, 0, st>>>(h->pos, batch, n - 1);
+    k_set_i32<<<1, 1, 0, st>>>(h->step, 1, n - 1);
+    return forge_argmax_finalize_launch(h->amax, batch, h->tok, h->hist, h->step, h->pos, h->hist_cap, st, false);
+}
+}  // namespace
+
+FORGE_API int forge_b200_prefill(ForgeB200* h, int batch, const int32_t* prompt, int n_prompt, int exact,
+                                 int32_t* next_tok, float* logits) {
+    if (int rc = check_ready(h, batch)) return rc;
+    if (!prompt || n_prompt <= 0 || n_prompt > h->lmax)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_prefill: bad prompt length %d", n_prompt);
+    if (forge_b200_reset(h)) return -1;
+    if (int rc = prefill_impl(h, batch, prompt, n_prompt, exact)) return rc;
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_prefill: %s", cudaGetErrorString(cudaGetLastError()));
+    if (int e = read_err(h)) return e;
+    if (next_tok && cudaMemcpy(next_tok, h->tok, 4 * (size_t)batch, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_prefill: D2H of the next tokens failed");
+    if (logits) {
+        if (enqueue_logits_copy(h, batch, logits)) return -1;
+        if (cudaStreamSynchronize(h->stream) != cudaSuccess)
+            return forge_fail(-1, "forge_b200_prefill: logits copy: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+    return 0;
+}
+
 FORGE_API int forge_b200_generate(ForgeB200* h, int batch, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out) {
     if (int rc = check_ready(h, batch)) return rc;
     if (!prompt || !out || n_prompt <= 0 || n_gen <= 0 || n_prompt + n_gen - 1 > h->lmax)
         return forge_fail(FORGE_INVALID_ARGS, "forge_b200_generate: bad prompt/generation length");
     if (forge_b200_reset(h)) return -1;
-    std::vector<int32_t> col(batch);
-    int32_t* pin = nullptr;
-    if (cudaHostAlloc((void**)&pin, 4 * (size_t)batch * n_prompt, cudaHostAllocDefault) != cudaSuccess)
-        return forge_fail(-1, "forge_b200_generate: pinned alloc failed");
-    for (int p = 0; p < n_prompt; ++p)
-        for (int b = 0; b < batch; ++b) pin[(size_t)p * batch + b] = prompt[(size_t)b * n_prompt + p];
-    int rc = 0;
-    for (int p = 0; p < n_prompt && !rc; ++p) {
-        cudaMemcpyAsync(h->tok, pin + (size_t)p * batch, 4 * batch, cudaMemcpyHostToDevice, h->stream);
-        rc = enqueue_one(h, batch);
-    }
+    // the whole prompt in one pass (hi/lo activations unless the model asks
+    // for bf16 ones), then one decode step per further token
+    int rc = prefill_impl(h, batch, prompt, n_prompt, h->desc.act_mode == 2 ? 0 : 1);
     for (int i = 1; i < n_gen && !rc; ++i) rc = enqueue_one(h, batch);
     if (cudaStreamSynchronize(h->stream) != cudaSuccess)
         rc = forge_fail(-1, "forge_b200_generate: %s", cudaGetErrorString(cudaGetLastError()));
-    cudaFreeHost(pin);
     if (rc) return rc;
     if (int e = read_err(h)) return e;
     std::vector<int32_t> hist((size_t)n_gen * batch);

@@ -153,6 +153,14 @@ def lib() -> C.CDLL:
             "forge_b200_generate": (i32, [vp, i32, vp, i32, i32, vp]),
             "forge_b200_sync": (i32, [vp]),
             "forge_b200_step_bytes": (i64, [vp, i32, i32]),
+            "forge_b200_prefill": (i32, [vp, i32, vp, i32, i32, vp, vp]),
+            "forge_train_rmsnorm_rows": (i32, [vp, i64, i64, C.c_double, vp, vp]),
+            "forge_train_rmsnorm_bwd_rows": (i32, [vp, vp, i64, i64, vp, vp]),
+            "forge_train_adamw_step": (i32, [vp, vp, vp, vp, i64] + [C.c_double] * 5 + [i64, vp, vp]),
+            "forge_train_rope": (i32, [vp, vp, vp, i64, i64, i64, i32, vp, vp]),
+            "forge_train_silu": (i32, [vp, vp, i64, i32, vp, vp]),
+            "forge_train_attn_fwd": (i32, [vp, vp, vp, i64, i64, i64, i64, vp, vp, vp]),
+            "forge_train_attn_bwd": (i32, [vp, vp, vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp, vp]),
             "forge_b200_launches_per_step": (i32, [vp, i32]),
             "forge_b200_step_trace": (i32, [vp, vp, i32]),
             "forge_b200_uses_fused_step": (i32, [vp, i32]),
@@ -597,6 +605,19 @@ class ForgeModel:
 
     def sync(self):
         check(lib().forge_b200_sync(self.h), "sync")
+
+    def prefill(self, prompt, exact=1, want_logits=False):
+        """All prompt positions in one pass; returns the next token of every
+        sequence (and its logits). prompt: [batch][n] (or [n])."""
+        import numpy as np
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        if p.ndim == 1:
+            p = p[None, :]
+        nxt = np.zeros(p.shape[0], np.int32)
+        lg = np.zeros((p.shape[0], self.vocab), np.float32) if want_logits else None
+        check(lib().forge_b200_prefill(self.h, p.shape[0], _ptr(p), p.shape[1], int(exact), _ptr(nxt), _ptr(lg)),
+              "prefill")
+        return (nxt, lg) if want_logits else nxt
 
     def generate(self, prompt, n_gen):
         import numpy as np

@@ -172,8 +172,24 @@ int forge_b200_decode_step_sampled_packed(const void* args);
 /* n_steps device-resident greedy steps (each feeds its argmax to the next);
  * asynchronous on the handle's stream. */
 int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps);
-/* Greedy generation: prompt [batch][n_prompt] fed token by token, then
- * n_gen argmax tokens into out [batch][n_gen]; synchronous. */
+/* Prompt prefill: every position of prompt [batch][n_prompt] through the
+ * model in one pass (decoder_block_lib.hexa:217-508, all positions; the
+ * batched GEMVs stream each weight tile once per 32 prompt rows, causal
+ * attention of every row over its own sequence's cache), K/V of positions
+ * 0..n_prompt-1 written to the cache, then the final norm, LM head and
+ * argmax of the last position: next_tok [batch] (may be NULL) and logits
+ * [batch][vocab] (may be NULL). The handle is reset first and left at
+ * position n_prompt, ready for forge_b200_decode_step / _decode_device.
+ * exact: 1 keeps hi/lo activations for bf16 weights at any row count, 0
+ * follows the model's act_mode (bf16 activations above 4 rows). Synchronous.
+ * Under tensor parallelism every rank calls it with the same prompt. */
+int forge_b200_prefill(ForgeB200* h, int batch, const int32_t* prompt, int n_prompt, int exact,
+                       int32_t* next_tok, float* logits);
+/* Greedy generation: prompt [batch][n_prompt] prefilled in one pass (hi/lo
+ * activations unless act_mode is 2), then n_gen argmax tokens into out
+ * [batch][n_gen] (the first from the prefill, the rest one decode step
+ * each); synchronous. Replaces flame's decode loop (decoder_lib.hexa:93-208,
+ * 485-500: full recompute per token). */
 int forge_b200_generate(ForgeB200* h, int batch, const int32_t* prompt, int n_prompt, int n_gen,
                         int32_t* out);
 /* Waits for the handle's stream; fails if a kernel raised its error word. */
@@ -279,6 +295,34 @@ int forge_q4_unpack_tiles(const void* tiles, const void* scale_tiles, int64_t N,
                           int group, uint8_t* codes, uint16_t* scales, void* stream);
 int64_t forge_q4_tile_bytes(int64_t N, int64_t K);
 int64_t forge_q4_scale_tile_bytes(int64_t N, int64_t K, int group);
+
+/* ---- Training-side families (float64, as the reference's forge kernels in
+ * self/cuda/runtime_cuda_emit.hexa) on caller-owned device arrays; 0 or an
+ * error code; asynchronous on `stream`. Same contracts as the reference's
+ * _hx_cuda_farr_*_gpu entries, minus its farr table (device pointers here).
+ *   rmsnorm_rows      y[r] = x[r] / sqrt(mean(x[r]^2) + eps)          (:1098, :1577)
+ *   rmsnorm_bwd_rows  dx = inv dxn - inv^3 x dot(dxn, x) / C, eps 1e-6 (:1130, :1609)
+ *   adamw_step        decoupled-wd AdamW; m, v updated in place; out may be w
+ *                     (step_t >= 1; bias corrections 1 - beta^t)       (:1170-1230, :1640-1780)
+ *   rope              rotate-half RoPE on [T][nheads][hd], tables [T][hd];
+ *                     bwd = its transpose                              (:2228-2280, :2582-2596)
+ *   silu              mode 0 silu(x), 1 d silu / dx, 2 silu(x) * gate_b
+ *                     (the gate with flame's series exp)               (:2171-2195, :3033)
+ *   attn_fwd          causal GQA attention, P [nh][T][T] kept, ctx [T][nh*hd];
+ *                     q [T][nh][hd], k and v [T][nkv][hd]              (:2819-2895, :3159)
+ *   attn_bwd          dq, dk, dv from q, k, v, P, dctx; scratch [nh][T][T] (:2896-3031, :3237) */
+int forge_train_rmsnorm_rows(const double* x, int64_t R, int64_t C, double eps, double* y, void* stream);
+int forge_train_rmsnorm_bwd_rows(const double* x, const double* dxn, int64_t R, int64_t C, double* dx, void* stream);
+int forge_train_adamw_step(double* w, double* m, double* v, const double* g, int64_t n, double lr, double b1,
+                           double b2, double eps, double wd, int64_t step_t, double* out, void* stream);
+int forge_train_rope(const double* t, const double* cos_t, const double* sin_t, int64_t T, int64_t nheads,
+                     int64_t hd, int bwd, double* out, void* stream);
+int forge_train_silu(const double* x, const double* gate_b, int64_t n, int mode, double* out, void* stream);
+int forge_train_attn_fwd(const double* q, const double* k, const double* v, int64_t T, int64_t nh, int64_t nkv,
+                         int64_t hd, double* p, double* ctx, void* stream);
+int forge_train_attn_bwd(const double* q, const double* k, const double* v, const double* p, const double* dctx,
+                         int64_t T, int64_t nh, int64_t nkv, int64_t hd, double* dq, double* dk, double* dv,
+                         double* scratch, void* stream);
 
 #ifdef __cplusplus
 }

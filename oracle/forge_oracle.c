@@ -691,3 +691,157 @@ int or_sample_token(const float* logits, int V, double temperature, int top_k, d
     free(h);
     return chosen;
 }
+
+/* ------------------------------------------------ training-side families */
+double or_dt_exp(double x) {
+    int r = 0;
+    double xr = x;
+    while ((xr > 0.0 ? xr : 0.0 - xr) > 0.25) { xr = xr / 2.0; r++; }
+    double term = 1.0, acc = 1.0;
+    for (int k = 1; k < 12; k++) { term = term * xr / (double)k; acc = acc + term; }
+    for (int i = 0; i < r; i++) acc = acc * acc;
+    return acc;
+}
+
+double or_attn_scale(int64_t hd) {
+    double x = (double)hd, g = x > 1.0 ? x : 1.0;
+    for (int i = 0; i < 24; i++) g = 0.5 * (g + x / g);
+    return 1.0 / g;
+}
+
+void or_train_rmsnorm_rows(const double* x, int64_t R, int64_t C, double eps, double* y) {
+    for (int64_t r = 0; r < R; r++) {
+        double ss = 0.0;
+        for (int64_t j = 0; j < C; j++) ss += x[r * C + j] * x[r * C + j];
+        double inv = 1.0 / sqrt(ss / (double)C + eps);
+        for (int64_t j = 0; j < C; j++) y[r * C + j] = x[r * C + j] * inv;
+    }
+}
+
+void or_train_rmsnorm_bwd_rows(const double* x, const double* dxn, int64_t R, int64_t C, double* dx) {
+    for (int64_t r = 0; r < R; r++) {
+        const double* xr = x + r * C;
+        const double* dr = dxn + r * C;
+        double ss = 0.0, dot = 0.0;
+        for (int64_t j = 0; j < C; j++) ss += xr[j] * xr[j];
+        for (int64_t j = 0; j < C; j++) dot += dr[j] * xr[j];
+        double inv = 1.0 / sqrt(ss / (double)C + 1e-6);
+        double coef = (inv * inv * inv) / (double)C;
+        for (int64_t i = 0; i < C; i++) dx[r * C + i] = inv * dr[i] - coef * xr[i] * dot;
+    }
+}
+
+void or_train_adamw(double* w, double* m, double* v, const double* g, int64_t n, double lr, double b1, double b2,
+                    double eps, double wd, int64_t step_t, double* out) {
+    double b1t = 1.0, b2t = 1.0;
+    for (int64_t e = 0; e < step_t; e++) { b1t *= b1; b2t *= b2; }
+    const double c1 = 1.0 - b1t, c2 = 1.0 - b2t;
+    for (int64_t i = 0; i < n; i++) {
+        double gi = g[i], wi0 = w[i];
+        double mi = b1 * m[i] + (1.0 - b1) * gi;
+        double vi = b2 * v[i] + (1.0 - b2) * gi * gi;
+        double mhat = mi / c1, vhat = vi / c2;
+        double denom = sqrt(vhat) + eps;
+        double wi = wi0 - lr * wd * wi0 - lr * mhat / denom;
+        m[i] = mi;
+        v[i] = vi;
+        out[i] = wi;
+    }
+}
+
+void or_train_rope(const double* t, const double* c, const double* s, int64_t T, int64_t nheads, int64_t hd, int bwd,
+                   double* out) {
+    const int64_t half = hd / 2, total = T * nheads * hd;
+    for (int64_t i = 0; i < total; i++) {
+        int64_t col = i % hd, row = i - col, tt = i / (nheads * hd), bse = tt * hd;
+        if (!bwd) {
+            double rh = col < half ? 0.0 - t[row + half + col] : t[row + col - half];
+            out[i] = t[row + col] * c[bse + col] + rh * s[bse + col];
+        } else {
+            double gs = col < half ? t[row + half + col] * s[bse + half + col]
+                                   : 0.0 - t[row + col - half] * s[bse + col - half];
+            out[i] = t[row + col] * c[bse + col] + gs;
+        }
+    }
+}
+
+void or_train_silu(const double* a, const double* b, int64_t n, int mode, double* out) {
+    for (int64_t i = 0; i < n; i++) {
+        double x = a[i];
+        if (mode == 0) {
+            out[i] = x * (1.0 / (1.0 + exp(-x)));
+        } else if (mode == 1) {
+            double sg = 1.0 / (1.0 + exp(-x));
+            out[i] = sg * (1.0 + x * (1.0 - sg));
+        } else {
+            double sig = 1.0 / (1.0 + or_dt_exp(0.0 - x));
+            out[i] = (x * sig) * b[i];
+        }
+    }
+}
+
+void or_train_attn_fwd(const double* q, const double* k, const double* v, int64_t T, int64_t nh, int64_t nkv,
+                       int64_t hd, double* p, double* ctx) {
+    const int64_t n_rep = nh / nkv, d = nh * hd;
+    const double scale = or_attn_scale(hd);
+    for (int64_t hh = 0; hh < nh; hh++)
+        for (int64_t i = 0; i < T; i++) {
+            int64_t kvh = hh / n_rep, L = i + 1;
+            double* pr = p + (hh * T + i) * T;
+            for (int64_t j = 0; j < T; j++) pr[j] = 0.0;
+            for (int64_t j = 0; j < L; j++) {
+                double dot = 0.0;
+                for (int64_t cc = 0; cc < hd; cc++) dot += q[(i * nh + hh) * hd + cc] * k[(j * nkv + kvh) * hd + cc];
+                pr[j] = dot * scale;
+            }
+            double mx = pr[0];
+            for (int64_t j = 1; j < L; j++) if (pr[j] > mx) mx = pr[j];
+            double tot = 0.0;
+            for (int64_t j = 0; j < L; j++) { pr[j] = or_dt_exp(pr[j] - mx); tot += pr[j]; }
+            for (int64_t j = 0; j < L; j++) pr[j] = pr[j] / tot;
+            for (int64_t c2 = 0; c2 < hd; c2++) {
+                double acc = 0.0;
+                for (int64_t j = 0; j < L; j++) acc += pr[j] * v[(j * nkv + kvh) * hd + c2];
+                ctx[i * d + hh * hd + c2] = acc;
+            }
+        }
+}
+
+void or_train_attn_bwd(const double* q, const double* k, const double* v, const double* p, const double* dctx,
+                       int64_t T, int64_t nh, int64_t nkv, int64_t hd, double* dq, double* dk, double* dv) {
+    const int64_t n_rep = nh / nkv, d = nh * hd;
+    const double scale = or_attn_scale(hd);
+    double* ds = (double*)calloc((size_t)(nh * T * T), sizeof(double));
+    for (int64_t hh = 0; hh < nh; hh++)
+        for (int64_t i = 0; i < T; i++) {
+            int64_t kvh = hh / n_rep;
+            double* dr = ds + (hh * T + i) * T;
+            const double* pr = p + (hh * T + i) * T;
+            for (int64_t j = 0; j <= i; j++) {
+                double acc = 0.0;
+                for (int64_t cc = 0; cc < hd; cc++) acc += dctx[i * d + hh * hd + cc] * v[(j * nkv + kvh) * hd + cc];
+                dr[j] = acc;
+            }
+            double sdot = 0.0;
+            for (int64_t j = 0; j <= i; j++) sdot += pr[j] * dr[j];
+            for (int64_t j = 0; j <= i; j++) dr[j] = (pr[j] * (dr[j] - sdot)) * scale;
+            for (int64_t c2 = 0; c2 < hd; c2++) {
+                double acc = 0.0;
+                for (int64_t j = 0; j <= i; j++) acc += dr[j] * k[(j * nkv + kvh) * hd + c2];
+                dq[(i * nh + hh) * hd + c2] = acc;
+            }
+        }
+    for (int64_t j = 0; j < T; j++)
+        for (int64_t kvh = 0; kvh < nkv; kvh++)
+            for (int64_t cc = 0; cc < hd; cc++) {
+                double av = 0.0, ak = 0.0;
+                for (int64_t hh = kvh * n_rep; hh < (kvh + 1) * n_rep; hh++)
+                    for (int64_t i = j; i < T; i++) {
+                        av += p[(hh * T + i) * T + j] * dctx[i * d + hh * hd + cc];
+                        ak += ds[(hh * T + i) * T + j] * q[(i * nh + hh) * hd + cc];
+                    }
+                dv[(j * nkv + kvh) * hd + cc] = av;
+                dk[(j * nkv + kvh) * hd + cc] = ak;
+            }
+    free(ds);
+}

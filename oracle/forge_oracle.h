@@ -134,6 +134,32 @@ double or_sampler_rand(int64_t* state);
  * receives the final distribution. */
 int or_sample_token(const float* logits, int V, double temperature, int top_k, double top_p,
                     int64_t* rng_state, float* probs);
+/* ---- Training-side forge families, float64, the reference's sequential
+ * order of operations (self/cuda/runtime_cuda_emit.hexa), no contraction. */
+/* flame's series exp (runtime_cuda_emit.hexa:2709-2725): halve until
+ * |x| <= 1/4 (r times), 12 Taylor terms, square r times. */
+double or_dt_exp(double x);
+/* 1 / dt_sqrt(hd): 24 Newton steps from max(x, 1) (:2726-2740). */
+double or_attn_scale(int64_t hd);
+/* y = x / sqrt(mean(x^2) + eps) per row (:1095-1120). */
+void or_train_rmsnorm_rows(const double* x, int64_t R, int64_t C, double eps, double* y);
+/* dx = inv dxn - inv^3 x dot(dxn, x) / C, eps 1e-6 (:1123-1165). */
+void or_train_rmsnorm_bwd_rows(const double* x, const double* dxn, int64_t R, int64_t C, double* dx);
+/* AdamW with decoupled weight decay; m, v in place (:1167-1230, host
+ * bias corrections :1640-1705). out may be w. */
+void or_train_adamw(double* w, double* m, double* v, const double* g, int64_t n, double lr, double b1, double b2,
+                    double eps, double wd, int64_t step_t, double* out);
+/* rotate-half RoPE on [T][nheads][hd], tables [T][hd]; bwd = transpose (:2228-2280). */
+void or_train_rope(const double* t, const double* c, const double* s, int64_t T, int64_t nheads, int64_t hd, int bwd,
+                   double* out);
+/* mode 0 silu, 1 silu', 2 silu(a) b with or_dt_exp (:2171-2195, :3033-3045). */
+void or_train_silu(const double* a, const double* b, int64_t n, int mode, double* out);
+/* causal GQA attention, P [nh][T][T], ctx [T][nh*hd] (:2819-2895). */
+void or_train_attn_fwd(const double* q, const double* k, const double* v, int64_t T, int64_t nh, int64_t nkv,
+                       int64_t hd, double* p, double* ctx);
+/* its backward: dq [T][nh][hd], dk and dv [T][nkv][hd] (:2896-3031). */
+void or_train_attn_bwd(const double* q, const double* k, const double* v, const double* p, const double* dctx,
+                       int64_t T, int64_t nh, int64_t nkv, int64_t hd, double* dq, double* dk, double* dv);
 #ifdef __cplusplus
 }
 #endif

@@ -71,6 +71,15 @@ def lib() -> C.CDLL:
             "or_ref_lcg_f32": (None, [vp, vp, i64]),
             "or_sampler_rand": (C.c_double, [vp]),
             "or_sample_token": (i32, [vp, i32, C.c_double, i32, C.c_double, vp, vp]),
+            "or_dt_exp": (C.c_double, [C.c_double]),
+            "or_attn_scale": (C.c_double, [i64]),
+            "or_train_rmsnorm_rows": (None, [vp, i64, i64, C.c_double, vp]),
+            "or_train_rmsnorm_bwd_rows": (None, [vp, vp, i64, i64, vp]),
+            "or_train_adamw": (None, [vp, vp, vp, vp, i64] + [C.c_double] * 5 + [i64, vp]),
+            "or_train_rope": (None, [vp, vp, vp, i64, i64, i64, i32, vp]),
+            "or_train_silu": (None, [vp, vp, i64, i32, vp]),
+            "or_train_attn_fwd": (None, [vp, vp, vp, i64, i64, i64, i64, vp, vp]),
+            "or_train_attn_bwd": (None, [vp, vp, vp, vp, vp, i64, i64, i64, i64, vp, vp, vp]),
         }
         for n, (r, a) in sig.items():
             f = getattr(L, n)

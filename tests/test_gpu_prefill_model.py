@@ -1,0 +1,116 @@
+"""Prompt prefill through the engine (forge_b200_prefill: all prompt positions
+in one pass, K/V written to the cache, LM head on the last position) against
+the oracle, through the C ABI:
+
+  * the logits of the last position equal flame's full-recompute forward
+    (nn_decoder_fwd, decoder_lib.hexa:93-208: every position through every
+    block, final norm and head on the last row; the oracle's or_full_forward
+    in float64) within the decode tests' bound, and the argmax agrees;
+  * the cache rows 0..n-1 equal the oracle's KV-cache decode of the same
+    prompt (bf16 rounding);
+  * prefill followed by decode steps gives the oracle's logits and tokens;
+  * several sequences at once, prompt lengths 1 to 40 (one 16-row tile, the
+    batched int4 paths above 4 and 24 rows, chunks of 32 rows).
+bf16-weight models run with hi/lo activations (exact = 1), as generate does.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CONFIGS = {
+    "tiny_bf16": dict(n_layer=4, d=256, n_head=4, n_kv=4, hd=64, ffn=688, vocab=4096, q4=False, tied=True),
+    "gqa_bf16": dict(n_layer=2, d=512, n_head=8, n_kv=2, hd=64, ffn=1024, vocab=2048, q4=False, tied=False),
+    "mha_q4": dict(n_layer=2, d=512, n_head=4, n_kv=4, hd=128, ffn=1280, vocab=2048, q4=True, tied=False),
+    "gqa_q4": dict(n_layer=2, d=512, n_head=8, n_kv=2, hd=64, ffn=1024, vocab=2048, q4=True, tied=False),
+}
+
+
+def _models(oracle, forge, cfg, max_batch, max_ctx):
+    om = oracle.OracleModel(cfg["n_layer"], cfg["d"], cfg["n_head"], cfg["n_kv"], cfg["hd"], cfg["ffn"],
+                            cfg["vocab"], q4=cfg["q4"], tied=cfg["tied"], seed=1234, std=0.02)
+    fm = forge.ForgeModel(cfg["n_layer"], cfg["d"], cfg["n_head"], cfg["n_kv"], cfg["hd"], cfg["ffn"], cfg["vocab"],
+                          weight_kind=forge.FORGE_WEIGHT_Q4_G128 if cfg["q4"] else forge.FORGE_WEIGHT_BF16,
+                          tied_head=cfg["tied"], max_batch=max_batch, max_ctx=max_ctx)
+    fm.init_synthetic(1234, 0.02)
+    return om, fm
+
+
+@pytest.mark.parametrize("name", list(CONFIGS))
+@pytest.mark.parametrize("n,batch", [(1, 1), (5, 1), (16, 2), (40, 1), (24, 3)])
+def test_prefill_matches_full_forward(forge, oracle, cuda, name, n, batch):
+    cfg = CONFIGS[name]
+    om, fm = _models(oracle, forge, cfg, batch, 64)
+    rng = np.random.default_rng(77 + n * 10 + batch)
+    prompt = rng.integers(0, cfg["vocab"], (batch, n)).astype(np.int32)
+    nxt, lg = fm.prefill(prompt, exact=1, want_logits=True)
+    for b in range(batch):
+        ref = om.full_forward(prompt[b])
+        err = float(np.abs(lg[b] - ref).max())
+        # the full recompute keeps K/V in float64; the engine's cache is
+        # bf16, which moves logits by up to ~1e-2 (the north-star bf16 bound
+        # is 2e-2; the cache-exact comparison is the next test)
+        assert err < 2e-2, f"seq {b}: max |dlogit| {err}"
+        assert np.median(np.abs(lg[b] - ref)) < 2e-3
+        top2 = np.sort(ref)[-2:]
+        if top2[1] - top2[0] > 2 * err:
+            assert nxt[b] == int(np.argmax(ref)), (b, nxt[b], int(np.argmax(ref)))
+    fm.close()
+
+
+@pytest.mark.parametrize("name", ["gqa_bf16", "mha_q4"])
+def test_prefill_cache_and_decode_match_oracle(forge, oracle, cuda, name):
+    """K/V rows written by the prefill, then 8 decode steps on top of them."""
+    cfg = CONFIGS[name]
+    n, steps = 19, 8
+    om, fm = _models(oracle, forge, cfg, 1, 48)
+    prompt = np.random.default_rng(5).integers(0, cfg["vocab"], n).astype(np.int32)
+    nxt, lg = fm.prefill(prompt, exact=1, want_logits=True)
+    kc, vc = om.new_cache(1, 48)
+    for p in range(n):
+        ref_lg, ref_am = om.decode_step(kc, vc, [prompt[p]], [p], oracle.OR_KV_BF16)
+    assert np.abs(lg[0] - ref_lg[0]).max() < 5e-3
+    for l in range(cfg["n_layer"]):
+        k, v = fm.get_kv(l, 0, cfg["n_kv"], 48, cfg["hd"])
+        kr, vr = oracle.f32_to_bf16(kc[l, 0]), oracle.f32_to_bf16(vc[l, 0])
+        kd = np.abs(oracle.bf16_to_f32(k[:, :n]) - oracle.bf16_to_f32(kr[:, :n])).max()
+        vd = np.abs(oracle.bf16_to_f32(v[:, :n]) - oracle.bf16_to_f32(vr[:, :n])).max()
+        assert kd < 2e-2 and vd < 2e-2, (l, kd, vd)
+    tok = int(ref_am[0])
+    for s in range(steps):
+        got, glg = fm.step([tok], want_logits=True)
+        ref_lg, ref_am = om.decode_step(kc, vc, [tok], [n + s], oracle.OR_KV_BF16)
+        err = float(np.abs(glg[0] - ref_lg[0]).max())
+        assert err < 5e-3, (s, err)
+        top2 = np.sort(ref_lg[0])[-2:]
+        if top2[1] - top2[0] > 2 * err:
+            assert got[0] == ref_am[0]
+        tok = int(ref_am[0])
+    fm.close()
+
+
+def test_generate_prefills_the_prompt(forge, oracle, cuda):
+    """generate() = prefill + decode steps: tokens equal the oracle's greedy
+    run over a 37-token prompt (batched int4 path for the prompt rows)."""
+    cfg = CONFIGS["gqa_q4"]
+    om, fm = _models(oracle, forge, cfg, 1, 64)
+    prompt = np.random.default_rng(9).integers(0, cfg["vocab"], 37).astype(np.int32)
+    ref, margins = om.greedy(prompt, 12)
+    got = fm.generate(prompt, 12)[0]
+    print(f"min top-2 margin {margins.min():.4g}")
+    assert np.array_equal(got, ref), (got, ref, margins)
+    fm.close()
+
+
+def test_prefill_bf16_activations_close_to_exact(forge, cuda):
+    """exact = 0 on bf16 weights: bf16 activations above 4 rows (the batched
+    bf16 GEMV), within the bf16 bound of the hi/lo pass."""
+    c = CONFIGS["gqa_bf16"]
+    fm = forge.ForgeModel(c["n_layer"], c["d"], c["n_head"], c["n_kv"], c["hd"], c["ffn"], c["vocab"],
+                          weight_kind=forge.FORGE_WEIGHT_BF16, max_batch=2, max_ctx=64)
+    fm.init_synthetic(1234, 0.02)
+    prompt = np.random.default_rng(3).integers(0, c["vocab"], (2, 33)).astype(np.int32)
+    _, exact = fm.prefill(prompt, exact=1, want_logits=True)
+    _, fast = fm.prefill(prompt, exact=0, want_logits=True)
+    assert np.abs(exact - fast).max() < 2e-2 * max(1.0, np.abs(exact).max())
+    fm.close()
