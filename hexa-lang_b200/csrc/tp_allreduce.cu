@@ -11,12 +11,14 @@
 // bits. Two buffer generations alternate, so a rank that runs ahead writes
 // into the generation its peers finished reading.
 //
-// Every wait is bounded (%globaltimer, 2 s): on expiry the kernel sets the
-// handle's error word and returns.
+// Every wait is bounded (%globaltimer; 2 s, or FORGE_WAIT_NS at set-up): on
+// expiry the kernel sets the handle's error word and returns.
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 #include "common.cuh"
 #include "forge_internal.h"
+#include "../../include/forge_b200.h"
 
 namespace {
 constexpr int kSlices = 16;      // CTAs per all-reduce; each owns a contiguous slice
@@ -28,7 +30,16 @@ struct ArDev {
     uint32_t* peer_flag[kMaxRanks]; // rank r's flags [2][T][kSlices]
     uint32_t* epoch;                // this rank's [kSlices] counters
     int T, rank, cap;
+    unsigned long long wait_ns;     // limit of each flag wait (FORGE_WAIT_NS at set-up)
 };
+
+// Flag-wait limit: FORGE_WAIT_NS from the environment (nanoseconds, at least
+// 1 ms), else the library's 2 s.
+unsigned long long wait_limit_ns() {
+    const char* e = getenv("FORGE_WAIT_NS");
+    const unsigned long long v = e ? strtoull(e, nullptr, 10) : 0ull;
+    return v >= 1000000ull ? v : (unsigned long long)FORGE_WAIT_NS;
+}
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -77,7 +88,7 @@ __global__ void __launch_bounds__(kThreads) k_tp_allreduce(float* x, int n, cons
         const uint64_t t0 = globaltimer_ns();
         uint32_t spins = 0;
         while (*f != ep) {
-            if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > FORGE_WAIT_NS) {
+            if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > d.wait_ns) {
                 atomicOr(err, FORGE_DEVERR_COUNTER_TIMEOUT);
                 s_ok = 0;
                 break;
@@ -173,6 +184,7 @@ int forge_tp_ar_init(void* comm, int rank, int T, int cap, cudaStream_t stream, 
     ar->dev.T = T;
     ar->dev.rank = rank;
     ar->dev.cap = cap;
+    ar->dev.wait_ns = wait_limit_ns();
     ar->fused.tile_epoch = ar->tile_epoch;
     ar->fused.T = T;
     ar->fused.rank = rank;
@@ -205,4 +217,65 @@ int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStrea
     if (!ar || n <= 0 || n > ar->dev.cap) return forge_fail(-1, "tp all-reduce: %d floats above capacity", n);
     k_tp_allreduce<<<kSlices, kThreads, 0, stream>>>(x, n, ar->dev, err);
     return forge_check_launch("tp all-reduce");
+}
+
+// Self-test of the bounded peer wait, on one GPU, with no peer: the
+// exchange buffers of T ranks all live in this process's memory and only
+// rank 0 runs its all-reduce, so its waits for the flags of ranks 1..T-1
+// (which nothing raises) run out after wait_ns. Reports the device error
+// bits and the kernel's wall time, then checks that the context still runs
+// work (a second, one-rank launch that needs no flags). 0 when the launch
+// ended and the context is usable; the error bits say whether it timed out.
+extern "C" FORGE_API int forge_tp_selftest_absent_peer(int T, int n, unsigned long long wait_ns, uint32_t* err_bits,
+                                                       double* ms) {
+    if (T < 2 || T > kMaxRanks || n <= 0 || n > (1 << 20) || wait_ns < 1000000ull || !err_bits || !ms)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_tp_selftest_absent_peer: bad args");
+    const int cap = (n + 15) & ~15;
+    const size_t buf_bytes = (size_t)2 * T * cap * 4, flag_bytes = (size_t)2 * T * kSlices * 4;
+    void* local = nullptr;
+    uint32_t *epoch = nullptr, *err = nullptr;
+    float* x = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = 0;
+    if (cudaMalloc(&local, buf_bytes + flag_bytes) != cudaSuccess || cudaMemset(local, 0, buf_bytes + flag_bytes) ||
+        cudaMalloc(&epoch, kSlices * 4) != cudaSuccess || cudaMemset(epoch, 0, kSlices * 4) ||
+        cudaMalloc(&err, 16) != cudaSuccess || cudaMemset(err, 0, 16) || cudaMalloc(&x, 4 * (size_t)n) != cudaSuccess ||
+        cudaMemset(x, 0, 4 * (size_t)n) || cudaEventCreate(&e0) || cudaEventCreate(&e1))
+        rc = forge_fail(-1, "forge_tp_selftest_absent_peer: device allocation failed");
+    if (!rc) {
+        ArDev d{};
+        for (int r = 0; r < T; ++r) {  // every "peer" is this process's own buffer
+            d.peer_buf[r] = (float*)local;
+            d.peer_flag[r] = (uint32_t*)((char*)local + buf_bytes);
+        }
+        d.epoch = epoch;
+        d.T = T;
+        d.rank = 0;
+        d.cap = cap;
+        d.wait_ns = wait_ns;
+        cudaEventRecord(e0);
+        k_tp_allreduce<<<kSlices, kThreads>>>(x, n, d, err);
+        cudaEventRecord(e1);
+        if (cudaEventSynchronize(e1) != cudaSuccess) {
+            rc = forge_fail(-1, "forge_tp_selftest_absent_peer: %s", cudaGetErrorString(cudaGetLastError()));
+        } else {
+            float t = 0.f;
+            cudaEventElapsedTime(&t, e0, e1);
+            *ms = t;
+            cudaMemcpy(err_bits, err, 4, cudaMemcpyDeviceToHost);
+            // the context still runs work: one rank alone needs no flags
+            d.T = 1;
+            cudaMemset(err, 0, 4);
+            k_tp_allreduce<<<kSlices, kThreads>>>(x, n, d, err);
+            uint32_t e2 = 0;
+            if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&e2, err, 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
+                e2 != 0)
+                rc = forge_fail(-1, "forge_tp_selftest_absent_peer: context unusable after the timeout");
+        }
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    for (void* p : {local, (void*)epoch, (void*)err, (void*)x})
+        if (p) cudaFree(p);
+    return rc;
 }

@@ -154,6 +154,7 @@ def lib() -> C.CDLL:
             "forge_b200_sync": (i32, [vp]),
             "forge_b200_step_bytes": (i64, [vp, i32, i32]),
             "forge_b200_prefill": (i32, [vp, i32, vp, i32, i32, vp, vp]),
+            "forge_tp_selftest_absent_peer": (i32, [i32, i32, C.c_uint64, vp, vp]),
             "forge_train_rmsnorm_rows": (i32, [vp, i64, i64, C.c_double, vp, vp]),
             "forge_train_rmsnorm_bwd_rows": (i32, [vp, vp, i64, i64, vp, vp]),
             "forge_train_adamw_step": (i32, [vp, vp, vp, vp, i64] + [C.c_double] * 5 + [i64, vp, vp]),
@@ -641,6 +642,25 @@ class ForgeModel:
     @property
     def stream(self):
         return lib().forge_b200_stream(self.h)
+
+
+def tp_heartbeat(store, rank, world, step, timeout_s=5.0):
+    """Host-side liveness check of a tensor-parallel group before a step is
+    launched: every rank posts forge_hb/<step>/<rank> in a shared key-value
+    store (a torch.distributed Store) and waits for the other ranks' keys of
+    the same step. A rank that left between steps (exited, crashed, stopped)
+    is found here, on the host, before any kernel or collective of the step
+    is launched — a device collective with a missing peer would otherwise
+    wait on the GPU until its own bounded wait (FORGE_WAIT_NS) ran out.
+    Raises ForgeError naming the ranks that are missing."""
+    import datetime
+    store.set(f"forge_hb/{step}/{rank}", "1")
+    keys = [f"forge_hb/{step}/{r}" for r in range(world)]
+    try:
+        store.wait(keys, datetime.timedelta(seconds=timeout_s))
+    except Exception:
+        missing = [r for r in range(world) if not store.check([f"forge_hb/{step}/{r}"])]
+        raise ForgeError(f"tensor-parallel rank(s) {missing} missed the heartbeat of step {step}")
 
 
 def tp_unique_id() -> bytes:

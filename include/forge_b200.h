@@ -296,6 +296,16 @@ int forge_q4_unpack_tiles(const void* tiles, const void* scale_tiles, int64_t N,
 int64_t forge_q4_tile_bytes(int64_t N, int64_t K);
 int64_t forge_q4_scale_tile_bytes(int64_t N, int64_t K, int group);
 
+/* Failure-detection self-test of the tensor-parallel peer exchange on one
+ * GPU: the exchange buffers of T ranks (2..8) live in this process and only
+ * rank 0 runs its all-reduce of n floats, so its waits for the other ranks'
+ * flags run out after wait_ns (>= 1 ms). Writes the device error bits
+ * (2 = a flag wait ran out) and the kernel's time in ms, then checks that
+ * the context still runs work. 0 when the launch ended and the context is
+ * usable. The engine's own limit is 2 s, or FORGE_WAIT_NS (ns) read when a
+ * tensor-parallel handle is created. */
+int forge_tp_selftest_absent_peer(int T, int n, unsigned long long wait_ns, uint32_t* err_bits, double* ms);
+
 /* ---- Training-side families (float64, as the reference's forge kernels in
  * self/cuda/runtime_cuda_emit.hexa) on caller-owned device arrays; 0 or an
  * error code; asynchronous on `stream`. Same contracts as the reference's
