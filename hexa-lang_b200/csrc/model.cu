@@ -914,6 +914,12 @@ FORGE_API int forge_b200_init_synthetic(ForgeB200* h, uint64_t seed, float std) 
     return 0;
 }
 
+/* The same with the std as a double, for FFIs that pass every float
+ * argument as a double (hexa's @link extern fn). */
+FORGE_API int forge_b200_init_synthetic_d(ForgeB200* h, uint64_t seed, double std) {
+    return forge_b200_init_synthetic(h, seed, (float)std);
+}
+
 FORGE_API int forge_b200_reset(ForgeB200* h) {
     if (!h) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_reset: null handle");
     cudaSetDevice(h->device);

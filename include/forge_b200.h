@@ -131,6 +131,8 @@ int forge_b200_load_layer(ForgeB200* h, int layer, const ForgeLayerWeights* w);
 int forge_b200_load_embedding(ForgeB200* h, const uint16_t* emb, const float* final_gain,
                               const uint16_t* head /* NULL when tied */);
 int forge_b200_init_synthetic(ForgeB200* h, uint64_t seed, float std);
+/* The same, std as a double (FFIs that pass floats as doubles: hexa's extern fn). */
+int forge_b200_init_synthetic_d(ForgeB200* h, uint64_t seed, double std);
 
 /* KV cache / positions. fill_kv_synthetic writes N(0, std) K/V for positions
  * [0, ctx_len) of every sequence and sets every position to ctx_len. */
