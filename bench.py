@@ -379,6 +379,59 @@ def run_decode(fb, torch, pg, local, world, rank, B, K, W, name="7b_int4_decode"
     return out
 
 
+def run_serve(fb, torch, local, n_req=64, max_batch=32, seed=5):
+    """Continuous batching (forge_serve over the 7B int4 model): n_req
+    requests with prompts of 64-512 tokens and 32-128 generated tokens, half
+    queued at the start and the rest arriving 4 per iteration, max_batch
+    running at once, a KV budget that never preempts. Wall clock (host) around
+    the whole run: scheduling, one ragged engine pass per iteration (prompt
+    rows of the admitted requests + one row per decoding request), H2D of the
+    rows and D2H of the next tokens. Tokens generated / second."""
+    import numpy as np
+    m = MODEL
+    fm = fb.ForgeModel(m["n_layer"], m["d"], m["n_head"], m["n_kv"], m["hd"], m["ffn"], m["vocab"],
+                       weight_kind=fb.FORGE_WEIGHT_Q4_G128, max_batch=max_batch, max_ctx=640, device=local)
+    fm.init_synthetic(1234, 0.02)
+    rng = np.random.default_rng(seed)
+    reqs = [(rng.integers(0, m["vocab"], int(rng.integers(64, 513))).astype(np.int32), int(rng.integers(32, 129)))
+            for _ in range(n_req)]
+
+    def one_run(rs):
+        sv = fb.ForgeServe(fm, max_batch, max_batch * 640)
+        pending = list(enumerate(rs))
+        for rid, (p, g) in pending[:len(rs) // 2]:
+            sv.add_request(rid, max_gen=g, prompt=p)
+        pending = pending[len(rs) // 2:]
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        step = 0
+        while True:
+            for rid, (p, g) in pending[:4]:
+                sv.add_request(rid, max_gen=g, prompt=p)
+            pending = pending[4:]
+            st = sv.stats()
+            if not pending and st["queue_size"] == 0 and st["running_count"] == 0:
+                break
+            sv.run_step(step)
+            step += 1
+        wall = time.perf_counter() - t0
+        out = sv.throughput(), sv.engine_time(), wall, step
+        sv.close()
+        return out
+
+    one_run(reqs[:8])  # warm-up: buffers and the batched paths
+    thr, (eng_ms, rows, passes), wall, steps = one_run(reqs)
+    fm.close()
+    gen = sum(g for _, g in reqs)
+    assert thr["total_tokens"] == gen
+    return {"workload": "7b_int4 continuous batching (forge_serve)", "requests": n_req, "max_batch": max_batch,
+            "prompt_tokens": int(sum(len(p) for p, _ in reqs)), "generated_tokens": gen,
+            "value": gen / wall, "unit": "generated tok/s (wall clock)", "wall_s": wall, "iterations": steps,
+            "engine_ms": eng_ms, "engine_rows": rows, "engine_passes": passes,
+            "tokens_per_step": thr["tokens_per_step"], "avg_latency_steps": thr["avg_latency"],
+            "avg_wait_steps": thr["avg_wait_time"]}
+
+
 def tp_parity(fb, torch, pg, local, world, rank):
     """Greedy tokens and logits of the tensor-parallel engine against one GPU
     (rank 0) with the same seeded weights: a small GQA int4 model (2 layers,
@@ -435,6 +488,8 @@ def main():
     ap.add_argument("--only-gemv", action="store_true", help="run only the dominant GEMV (for profiling)")
     ap.add_argument("--only-prefill", action="store_true", help="run only the flash prefill (for profiling)")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-serve", action="store_true")
+    ap.add_argument("--only-serve", action="store_true", help="run only the continuous-batching workload")
     args = ap.parse_args()
     world, rank, local, pg = dist_setup()
     if args.impl == "reference":
@@ -454,6 +509,9 @@ def main():
         return
     if args.only_prefill:
         print(json.dumps(time_prefill(fb, torch, dev, B=4, H=16, S=4096, reps=2)))
+        return
+    if args.only_serve:
+        print(json.dumps(run_serve(fb, torch, local)))
         return
     B, K, W = args.batch, args.steps, max(3, args.warmup)
     r = run_decode(fb, torch, pg, local, world, rank, B, K, W)
@@ -481,6 +539,7 @@ def main():
     gemv_ms = max_over_ranks(pg, gemv_ms)
     achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
     prefill = None if (args.no_prefill or world > 1) else time_prefill(fb, torch, dev)
+    serve = None if (args.no_serve or world > 1) else run_serve(fb, torch, local)
     if rank != 0:
         return
     cpu = None
@@ -507,6 +566,7 @@ def main():
         "batch_sweep": sweep,
         "tp_parity": parity,
         "prefill": prefill,
+        "serve": serve,
         "cpu_baseline": cpu,
     }
     print(json.dumps(out))

@@ -78,6 +78,14 @@ __global__ void k_argmax_extract(unsigned long long* keys, int B, int32_t* tok) 
     }
 }
 
+// dst[r] = src[rows[r]] for r < n, rows of d floats (one CTA per row).
+__global__ void k_gather_rows(const float* __restrict__ src, const int32_t* __restrict__ rows, int d,
+                              float* __restrict__ dst) {
+    const float* a = src + (size_t)rows[blockIdx.x] * d;
+    float* o = dst + (size_t)blockIdx.x * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) o[i] = a[i];
+}
+
 __global__ void k_add_i32(int32_t* p, int n, int32_t v) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] += v;
 }
@@ -132,6 +140,7 @@ struct ForgeB200 {
         int64_t cap = 0;
         float *x = nullptr, *q = nullptr, *ctx = nullptr, *s = nullptr, *partial = nullptr;
         int32_t *tok = nullptr, *pos = nullptr, *seq = nullptr;
+        int32_t* sel = nullptr;  // [2][Bmax]: rows that take the LM head, their tokens
         uint32_t* counters = nullptr;
     } pre;
     // multi-kernel step timeline (FORGE_GRAPH_TRACE): [node][grid][4] stamps
@@ -916,6 +925,12 @@ FORGE_API int forge_b200_init_synthetic(ForgeB200* h, uint64_t seed, float std) 
 
 /* The same with the std as a double, for FFIs that pass every float
  * argument as a double (hexa's @link extern fn). */
+FORGE_API int forge_b200_get_desc(const ForgeB200* h, ForgeModelDesc* out) {
+    if (!h || !out) return forge_fail(FORGE_INVALID_ARGS, "forge_b200_get_desc: null argument");
+    *out = h->desc;
+    return 0;
+}
+
 FORGE_API int forge_b200_init_synthetic_d(ForgeB200* h, uint64_t seed, double std) {
     return forge_b200_init_synthetic(h, seed, (float)std);
 }
@@ -979,6 +994,23 @@ FORGE_API int forge_b200_set_kv(ForgeB200* h, int layer, int seq, const uint16_t
                   cudaMemcpy2D(h->vc + off, pitch, v, (size_t)n_pos * row, (size_t)n_pos * row, h->Hkv,
                                cudaMemcpyHostToDevice) != cudaSuccess))
         return forge_fail(-1, "forge_b200_set_kv: H2D failed");
+    return 0;
+}
+
+FORGE_API int forge_b200_get_kv_rows(ForgeB200* h, int layer, int seq, uint16_t* k, uint16_t* v, int n_pos) {
+    if (!h || layer < 0 || layer >= h->L || seq < 0 || seq >= h->Bmax || !k || !v || n_pos < 0 || n_pos > h->lmax)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_get_kv_rows: bad args");
+    cudaSetDevice(h->device);
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess) return forge_fail(-1, "forge_b200_get_kv_rows: sync failed");
+    const size_t per_seq = (size_t)h->Hkv * h->lmax * h->hd;
+    const size_t off = (size_t)layer * h->kv_layer + (size_t)seq * per_seq;
+    const size_t row = (size_t)h->hd * 2, pitch = (size_t)h->lmax * row;
+    // cache [Hkv][lmax][hd] -> host [Hkv][n_pos][hd]
+    if (n_pos && (cudaMemcpy2D(k, (size_t)n_pos * row, h->kc + off, pitch, (size_t)n_pos * row, h->Hkv,
+                               cudaMemcpyDeviceToHost) != cudaSuccess ||
+                  cudaMemcpy2D(v, (size_t)n_pos * row, h->vc + off, pitch, (size_t)n_pos * row, h->Hkv,
+                               cudaMemcpyDeviceToHost) != cudaSuccess))
+        return forge_fail(-1, "forge_b200_get_kv_rows: D2H failed");
     return 0;
 }
 
@@ -1130,7 +1162,7 @@ int prefill_reserve(ForgeB200* h, int64_t R) {
     if (R <= P.cap) return 0;
     cudaStreamSynchronize(h->stream);
     for (void* p : {(void*)P.x, (void*)P.q, (void*)P.ctx, (void*)P.s, (void*)P.partial, (void*)P.tok, (void*)P.pos,
-                    (void*)P.seq, (void*)P.counters})
+                    (void*)P.seq, (void*)P.sel, (void*)P.counters})
         if (p) cudaFree(p);
     P = {};
     int64_t part = 0;  // split partials for any row count up to R
@@ -1140,7 +1172,8 @@ int prefill_reserve(ForgeB200* h, int64_t R) {
               cudaMalloc(&P.ctx, 4 * R * h->qd) == cudaSuccess && cudaMalloc(&P.s, 4 * R * h->F) == cudaSuccess &&
               cudaMalloc(&P.partial, 4 * part * h->H * (h->hd + 2)) == cudaSuccess &&
               cudaMalloc(&P.tok, 4 * R) == cudaSuccess && cudaMalloc(&P.pos, 4 * R) == cudaSuccess &&
-              cudaMalloc(&P.seq, 4 * R) == cudaSuccess && cudaMalloc(&P.counters, 4 * R * h->Hkv) == cudaSuccess &&
+              cudaMalloc(&P.seq, 4 * R) == cudaSuccess && cudaMalloc(&P.sel, 8 * (size_t)h->Bmax) == cudaSuccess &&
+              cudaMalloc(&P.counters, 4 * R * h->Hkv) == cudaSuccess &&
               cudaMemset(P.counters, 0, 4 * R * h->Hkv) == cudaSuccess;
     if (ok && !h->bscratch) {  // the batched GEMV paths (more than 4 rows)
         const size_t nb = (size_t)forge_gemv_b_scratch_bytes(std::max({h->d, h->qd, h->F}));
@@ -1190,6 +1223,45 @@ int prefill_impl(ForgeB200* h, int batch, const int32_t* prompt, int n, int exac
     k_set_i32<<<1, 1, 0, st>>>(h->step, 1, n - 1);
     return forge_argmax_finalize_launch(h->amax, batch, h->tok, h->hist, h->step, h->pos, h->hist_cap, st, false);
 }
+
+// R ragged rows (token, position, sequence) through the model, then the LM
+// head and argmax of n_out of them; tokens into P.sel + Bmax.
+int forward_rows_impl(ForgeB200* h, int R, const int32_t* tok, const int32_t* pos, const int32_t* seq, int n_out,
+                      const int32_t* out_rows, int exact_mode) {
+    std::vector<int64_t> keys(R);
+    for (int r = 0; r < R; ++r) {
+        if (tok[r] < 0 || tok[r] >= h->Vfull)
+            return forge_fail(FORGE_INVALID_ARGS, "forge_b200_forward_rows: token %d outside the vocabulary", tok[r]);
+        if (seq[r] < 0 || seq[r] >= h->Bmax || pos[r] < 0 || pos[r] >= h->lmax)
+            return forge_fail(FORGE_INVALID_ARGS, "forge_b200_forward_rows: row %d: sequence %d / position %d out of range",
+                              r, seq[r], pos[r]);
+        keys[r] = (int64_t)seq[r] * h->lmax + pos[r];
+    }
+    std::sort(keys.begin(), keys.end());
+    if (std::adjacent_find(keys.begin(), keys.end()) != keys.end())
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_forward_rows: two rows write the same cache position");
+    for (int i = 0; i < n_out; ++i)
+        if (out_rows[i] < 0 || out_rows[i] >= R)
+            return forge_fail(FORGE_INVALID_ARGS, "forge_b200_forward_rows: output row %d outside 0..%d", out_rows[i], R - 1);
+    if (int rc = prefill_reserve(h, R)) return rc;
+    auto& P = h->pre;
+    cudaStream_t st = h->stream;
+    if (cudaMemcpyAsync(P.tok, tok, 4 * (size_t)R, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(P.pos, pos, 4 * (size_t)R, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(P.seq, seq, 4 * (size_t)R, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(P.sel, out_rows, 4 * (size_t)n_out, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_forward_rows: H2D of the rows failed");
+    const RowMap rm{P.pos, P.seq, P.partial, P.counters, exact_mode == 1};
+    int rc = forge_embed_launch(h->emb, h->d, h->Vfull, P.tok, R, P.x, h->err, st, false);
+    for (int l = 0; l < h->L && !rc; ++l)
+        rc = enqueue_qkv(h, l, R, P.x, P.q, true, &rm) || enqueue_attn(h, l, R, P.q, P.ctx, false, &rm) ||
+             enqueue_oproj(h, l, R, P.ctx, P.x, true, &rm) || enqueue_mlp(h, l, R, P.x, true, &rm, P.s);
+    if (rc) return -1;
+    k_gather_rows<<<n_out, 256, 0, st>>>(P.x, P.sel, h->d, h->x);
+    if (enqueue_head(h, n_out, h->x, false)) return -1;
+    k_argmax_extract<<<1, 1024, 0, st>>>(h->amax, n_out, P.sel + h->Bmax);
+    return cudaGetLastError() == cudaSuccess ? 0 : forge_fail(-1, "forge_b200_forward_rows: launch failed");
+}
 }  // namespace
 
 FORGE_API int forge_b200_prefill(ForgeB200* h, int batch, const int32_t* prompt, int n_prompt, int exact,
@@ -1210,6 +1282,21 @@ FORGE_API int forge_b200_prefill(ForgeB200* h, int batch, const int32_t* prompt,
             return forge_fail(-1, "forge_b200_prefill: logits copy: %s", cudaGetErrorString(cudaGetLastError()));
     }
     return 0;
+}
+
+FORGE_API int forge_b200_forward_rows(ForgeB200* h, int n_rows, const int32_t* tok, const int32_t* pos,
+                                      const int32_t* seq, int n_out, const int32_t* out_rows, int exact,
+                                      int32_t* next_tok, float* logits) {
+    if (int rc = check_ready(h, n_out)) return rc;
+    if (n_rows <= 0 || !tok || !pos || !seq || !out_rows)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_forward_rows: no rows or a null array");
+    if (int rc = forward_rows_impl(h, n_rows, tok, pos, seq, n_out, out_rows, exact)) return rc;
+    if (next_tok)
+        cudaMemcpyAsync(next_tok, h->pre.sel + h->Bmax, 4 * (size_t)n_out, cudaMemcpyDeviceToHost, h->stream);
+    if (logits && enqueue_logits_copy(h, n_out, logits)) return -1;
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess)
+        return forge_fail(-1, "forge_b200_forward_rows: %s", cudaGetErrorString(cudaGetLastError()));
+    return read_err(h);
 }
 
 FORGE_API int forge_b200_generate(ForgeB200* h, int batch, const int32_t* prompt, int n_prompt, int n_gen, int32_t* out) {

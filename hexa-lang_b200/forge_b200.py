@@ -59,6 +59,31 @@ class ForgeClmBlock(C.Structure):
     _fields_ = [("cout", C.c_int64), ("rest", C.c_int64), ("offset", C.c_int64)]
 
 
+# continuous batching (include/forge_serve.h): request phases and records
+FORGE_CB_QUEUED, FORGE_CB_PREFILL, FORGE_CB_DECODE, FORGE_CB_PREEMPTED, FORGE_CB_SWAPPED, FORGE_CB_DONE = range(6)
+SERVE_REQUEST_FIELDS = ("req_id", "prompt_len", "max_gen", "priority", "deadline", "phase", "tokens_generated",
+                        "kv_slots_used", "enqueue_time", "start_time", "finish_time", "was_preempted",
+                        "preempt_count")
+SERVE_STATS_FIELDS = ("queue_size", "running_count", "swapped_count", "completed_count", "kv_used", "kv_free",
+                      "step", "total_tokens", "total_preemptions")
+SERVE_THROUGHPUT_FIELDS = ("tokens_per_step", "avg_latency", "avg_wait_time", "max_latency", "max_wait_time",
+                           "total_tokens", "total_preemptions", "total_swaps_out", "total_swaps_in",
+                           "total_requests_done")
+
+
+class ForgeServeRequest(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in SERVE_REQUEST_FIELDS]
+
+
+class ForgeServeStats(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in SERVE_STATS_FIELDS]
+
+
+class ForgeServeThroughput(C.Structure):
+    _fields_ = [(n, C.c_double) for n in SERVE_THROUGHPUT_FIELDS[:3]] + \
+               [(n, C.c_int64) for n in SERVE_THROUGHPUT_FIELDS[3:]]
+
+
 class ForgeShapeInfo(C.Structure):
     _fields_ = [("M", C.c_int64), ("N", C.c_int64), ("K", C.c_int64), ("batch", C.c_int64)]
 
@@ -154,6 +179,28 @@ def lib() -> C.CDLL:
             "forge_b200_sync": (i32, [vp]),
             "forge_b200_step_bytes": (i64, [vp, i32, i32]),
             "forge_b200_prefill": (i32, [vp, i32, vp, i32, i32, vp, vp]),
+            "forge_b200_forward_rows": (i32, [vp, i32, vp, vp, vp, i32, vp, i32, vp, vp]),
+            "forge_b200_get_kv_rows": (i32, [vp, i32, i32, vp, vp, i32]),
+            "forge_b200_get_desc": (i32, [vp, C.POINTER(ForgeModelDesc)]),
+            "forge_b200_init_synthetic_d": (i32, [vp, C.c_uint64, C.c_double]),
+            "forge_serve_create": (i32, [vp, i32, i64, C.POINTER(vp)]),
+            "forge_serve_destroy": (i32, [vp]),
+            "forge_serve_set_eos": (i32, [vp, i32]),
+            "forge_serve_add_request": (i32, [vp, i64, vp, i64, i64, i64, i64]),
+            "forge_serve_run_step": (i32, [vp, i64]),
+            "forge_serve_run_until_done": (i32, [vp, i64]),
+            "forge_serve_check_deadlines": (i32, [vp, i64]),
+            "forge_serve_preempt": (i32, [vp, i64]),
+            "forge_serve_preempt_for_room": (i32, [vp, i64]),
+            "forge_serve_swap_out": (i32, [vp, i64]),
+            "forge_serve_swap_in": (i32, [vp, i64]),
+            "forge_serve_peek_queue": (i32, [vp, C.POINTER(ForgeServeRequest)]),
+            "forge_serve_find_request": (i32, [vp, i64, C.POINTER(ForgeServeRequest)]),
+            "forge_serve_count_by_phase": (i64, [vp, i64]),
+            "forge_serve_stats": (i32, [vp, C.POINTER(ForgeServeStats)]),
+            "forge_serve_throughput": (i32, [vp, C.POINTER(ForgeServeThroughput)]),
+            "forge_serve_output": (i32, [vp, i64, vp, i64, C.POINTER(C.c_int64)]),
+            "forge_serve_engine_time": (i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
             "forge_tp_selftest_absent_peer": (i32, [i32, i32, C.c_uint64, vp, vp]),
             "forge_train_rmsnorm_rows": (i32, [vp, i64, i64, C.c_double, vp, vp]),
             "forge_train_rmsnorm_bwd_rows": (i32, [vp, vp, i64, i64, vp, vp]),
@@ -620,6 +667,17 @@ class ForgeModel:
               "prefill")
         return (nxt, lg) if want_logits else nxt
 
+    def forward_rows(self, tok, pos, seq, out_rows, exact=1, want_logits=False):
+        """One pass over ragged rows (token, position, sequence slot); the
+        argmax (and logits) of the rows out_rows."""
+        import numpy as np
+        t, p, q, o = (np.ascontiguousarray(a, dtype=np.int32) for a in (tok, pos, seq, out_rows))
+        nxt = np.zeros(len(o), np.int32)
+        lg = np.zeros((len(o), self.vocab), np.float32) if want_logits else None
+        check(lib().forge_b200_forward_rows(self.h, len(t), _ptr(t), _ptr(p), _ptr(q), len(o), _ptr(o), int(exact),
+                                            _ptr(nxt), _ptr(lg)), "forward_rows")
+        return (nxt, lg) if want_logits else nxt
+
     def generate(self, prompt, n_gen):
         import numpy as np
         p = np.ascontiguousarray(prompt, dtype=np.int32)
@@ -699,3 +757,107 @@ def bf16_pack(w_bf16_dev, stream=None):
     tiles = torch.empty(N * K * 2, dtype=torch.uint8, device=w_bf16_dev.device)
     check(lib().forge_bf16_pack_tiles(_ptr(w_bf16_dev), N, K, _ptr(tiles), stream or 0), "bf16_pack")
     return tiles
+
+
+class ForgeServe:
+    """Continuous batching (include/forge_serve.h): the cb2 scheduler of
+    self/ml/continuous_batching.hexa; with a ForgeModel every iteration runs
+    one ragged engine pass and each request generates greedy tokens, without
+    one (model=None) the scheduler keeps the books alone."""
+
+    def __init__(self, model, max_batch, max_kv_slots):
+        h = C.c_void_p()
+        self.model = model
+        check(lib().forge_serve_create(model.h if model is not None else None, max_batch, max_kv_slots,
+                                       C.byref(h)), "forge_serve_create")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib().forge_serve_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _rc(self, rc, what):
+        if rc < 0:
+            check(rc, what)
+        return rc
+
+    def set_eos(self, eos):
+        check(lib().forge_serve_set_eos(self.h, eos), "set_eos")
+
+    def add_request(self, req_id, prompt_len=None, max_gen=1, priority=0, deadline=0, prompt=None):
+        import numpy as np
+        p = None
+        if prompt is not None:
+            p = np.ascontiguousarray(prompt, dtype=np.int32)
+            prompt_len = len(p)
+        check(lib().forge_serve_add_request(self.h, req_id, _ptr(p), prompt_len, max_gen, priority, deadline),
+              "add_request")
+
+    def run_step(self, cur_time):
+        return self._rc(lib().forge_serve_run_step(self.h, cur_time), "run_step")
+
+    def run_until_done(self, max_steps):
+        return self._rc(lib().forge_serve_run_until_done(self.h, max_steps), "run_until_done")
+
+    def check_deadlines(self, cur_time):
+        return self._rc(lib().forge_serve_check_deadlines(self.h, cur_time), "check_deadlines")
+
+    def preempt(self, req_id):
+        return self._rc(lib().forge_serve_preempt(self.h, req_id), "preempt")
+
+    def preempt_for_room(self, needed):
+        return self._rc(lib().forge_serve_preempt_for_room(self.h, needed), "preempt_for_room")
+
+    def swap_out(self, req_id):
+        return self._rc(lib().forge_serve_swap_out(self.h, req_id), "swap_out")
+
+    def swap_in(self, req_id):
+        return self._rc(lib().forge_serve_swap_in(self.h, req_id), "swap_in")
+
+    @staticmethod
+    def _as_dict(st, fields):
+        return {n: getattr(st, n) for n in fields}
+
+    def peek_queue(self):
+        r = ForgeServeRequest()
+        return {} if self._rc(lib().forge_serve_peek_queue(self.h, C.byref(r)), "peek_queue") == 1 else \
+            self._as_dict(r, SERVE_REQUEST_FIELDS)
+
+    def find_request(self, req_id):
+        r = ForgeServeRequest()
+        return {} if self._rc(lib().forge_serve_find_request(self.h, req_id, C.byref(r)), "find_request") == 1 else \
+            self._as_dict(r, SERVE_REQUEST_FIELDS)
+
+    def count_by_phase(self, phase):
+        return lib().forge_serve_count_by_phase(self.h, phase)
+
+    def stats(self):
+        st = ForgeServeStats()
+        check(lib().forge_serve_stats(self.h, C.byref(st)), "stats")
+        return self._as_dict(st, SERVE_STATS_FIELDS)
+
+    def throughput(self):
+        st = ForgeServeThroughput()
+        check(lib().forge_serve_throughput(self.h, C.byref(st)), "throughput")
+        return self._as_dict(st, SERVE_THROUGHPUT_FIELDS)
+
+    def output(self, req_id):
+        import numpy as np
+        n = C.c_int64()
+        if self._rc(lib().forge_serve_output(self.h, req_id, None, 0, C.byref(n)), "output") == 1:
+            return None
+        out = np.zeros(n.value, np.int32)
+        check(lib().forge_serve_output(self.h, req_id, _ptr(out), n.value, C.byref(n)), "output")
+        return out
+
+    def engine_time(self):
+        ms, rows, passes = C.c_double(), C.c_int64(), C.c_int64()
+        check(lib().forge_serve_engine_time(self.h, C.byref(ms), C.byref(rows), C.byref(passes)), "engine_time")
+        return ms.value, rows.value, passes.value

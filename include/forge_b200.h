@@ -102,6 +102,8 @@ typedef struct ForgeLayerWeights {
 typedef struct ForgeB200 ForgeB200;
 
 int         forge_b200_create(const ForgeModelDesc* desc, int device, ForgeB200** out);
+/* The description the handle was created with. */
+int         forge_b200_get_desc(const ForgeB200* h, ForgeModelDesc* out);
 /* Tensor-parallel handle: rank desc->tp_rank of desc->tp_size, one process
  * (or thread) per GPU. Every rank passes the same 128-byte NCCL unique id
  * (made once by forge_b200_tp_unique_id and shared out of band) and calls
@@ -143,6 +145,10 @@ int forge_b200_get_kv(ForgeB200* h, int layer, int seq, uint16_t* k_out, uint16_
 /* Writes positions [0, n_pos) of one sequence's K/V cache from host
  * [n_kv_head][n_pos][head_dim] bf16 arrays (synchronous). */
 int forge_b200_set_kv(ForgeB200* h, int layer, int seq, const uint16_t* k, const uint16_t* v, int n_pos);
+/* Reads positions [0, n_pos) of one sequence's K/V cache into host
+ * [n_kv_head][n_pos][head_dim] bf16 arrays (synchronous): with set_kv, the
+ * copy that moves a sequence's cache out of HBM and back (KV swap). */
+int forge_b200_get_kv_rows(ForgeB200* h, int layer, int seq, uint16_t* k, uint16_t* v, int n_pos);
 
 /* One decode step from host buffers (H2D tokens, graph launch, D2H next
  * tokens and optional logits [batch][vocab]); synchronous. */
@@ -187,6 +193,18 @@ int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps);
  * Under tensor parallelism every rank calls it with the same prompt. */
 int forge_b200_prefill(ForgeB200* h, int batch, const int32_t* prompt, int n_prompt, int exact,
                        int32_t* next_tok, float* logits);
+/* One pass over n_rows ragged rows, the iteration of a continuous-batching
+ * scheduler (prompt chunks of new requests and one row per decoding request
+ * in the same pass): row r is token tok[r] of sequence slot seq[r] at
+ * position pos[r]; its K/V go to that slot's cache at pos[r] and it attends
+ * over positions 0..pos[r] of the slot (earlier positions cached by earlier
+ * passes or by rows of this one). Then the final norm, LM head and argmax of
+ * the n_out (1..max_batch) rows out_rows[]: next_tok [n_out] and logits
+ * [n_out][vocab] (either may be NULL). Two rows may not write the same
+ * (slot, position). exact as for forge_b200_prefill. The handle's own
+ * positions and step history are untouched. Synchronous. */
+int forge_b200_forward_rows(ForgeB200* h, int n_rows, const int32_t* tok, const int32_t* pos, const int32_t* seq,
+                            int n_out, const int32_t* out_rows, int exact, int32_t* next_tok, float* logits);
 /* Greedy generation: prompt [batch][n_prompt] prefilled in one pass (hi/lo
  * activations unless act_mode is 2), then n_gen argmax tokens into out
  * [batch][n_gen] (the first from the prefill, the rest one decode step
