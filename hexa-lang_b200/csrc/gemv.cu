@@ -75,15 +75,17 @@ __device__ __forceinline__ uint32_t sys_load_acquire(const uint32_t* p) {
 // b < batch <= 4 holds rows p / p+8 of sequence b of 16-row tile u).
 // tp_resid_post, when the CTA has reduced tile u: the tile's share goes into
 // this rank's slot on every rank (rank 0's share carries the residual, the
-// additions of its FORGE_EPI_RESID) and a flag per (rank, tile) on every rank
-// says it landed. tp_resid_finish, once the CTA has posted all its tiles:
-// when every rank's flag for the tile is in, the slots are summed in rank
-// order — the additions of the separate all-reduce, so the result is the
-// same — into the residual. Posting first and waiting at the end keeps the
-// NVLink round trip off the CTA's remaining units. The per-tile call counter
-// selects one of two buffer generations: a rank can be at most one call
-// ahead of another on a tile, because its launch ends only after every
-// rank's share of its tiles arrived. Waits are bounded (error word).
+// additions of its FORGE_EPI_RESID) with plain stores, no fence.
+// tp_resid_flags, once the CTA has stored all its tiles: one system-scope
+// fence for all of them, then a flag per (rank, tile) on every rank says
+// they landed. tp_resid_finish: when every rank's flag for the tile is in,
+// the slots are summed in rank order — the additions of the separate
+// all-reduce, so the result is the same — into the residual. One fence per
+// CTA instead of one per tile keeps the NVLink round trip of the fence off
+// the CTA's remaining units. The per-tile call counter selects one of two
+// buffer generations: a rank can be at most one call ahead of another on a
+// tile, because its launch ends only after every rank's share of its tiles
+// arrived. Waits are bounded (error word).
 __device__ __noinline__ void tp_resid_post(const ForgeGemvArgs& a, int u, int p, int b, bool act, float ylo,
                                            float yhi) {
     const ForgeTpFusedDev& f = *a.tpf;
@@ -105,10 +107,20 @@ __device__ __noinline__ void tp_resid_post(const ForgeGemvArgs& a, int u, int p,
             dst[i0] = v0;
             dst[i1] = v1;
         }
-        __threadfence_system();
     }
+}
+
+__device__ __noinline__ void tp_resid_flags(const ForgeGemvArgs& a, int units) {
+    const ForgeTpFusedDev& f = *a.tpf;
+    const int lane = threadIdx.x & 31;
+    const int T = f.T, rank = f.rank;
+    __threadfence_system();  // every lane's remote stores of every tile of this CTA
     __syncwarp();
-    if (lane < T) sys_store_release(f.flag[lane] + ((size_t)gen * T + rank) * f.max_tiles + u, ep);
+    if (lane < T)
+        for (int u = blockIdx.x; u < units; u += gridDim.x) {
+            const uint32_t ep = f.tile_epoch[u];
+            sys_store_release(f.flag[lane] + ((size_t)(ep & 1) * T + rank) * f.max_tiles + u, ep);
+        }
 }
 
 __device__ __noinline__ void tp_resid_finish(const ForgeGemvArgs& a, int u, int p, int b, bool act) {
@@ -352,9 +364,12 @@ __global__ void __maxnreg__(FORGE_GEMV_MAXNREG) k_gemv(const ForgeGemvArgs a) {
         }
     }
     if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4 + 3] = globaltimer_ns();
-    if (EPI == FORGE_EPI_RESID_TP && warp == 0 && __all_sync(0xffffffffu, ok)) {
+    if (EPI == FORGE_EPI_RESID_TP && warp == 0) {
         const int tid = threadIdx.x;
-        for (int u = blockIdx.x; u < units; u += gridDim.x) tp_resid_finish(a, u, tid & 7, tid >> 3, tid < 8 * a.batch);
+        tp_resid_flags(a, units);  // also after a failed wait: the tiles that were posted
+        if (__all_sync(0xffffffffu, ok))
+            for (int u = blockIdx.x; u < units; u += gridDim.x)
+                tp_resid_finish(a, u, tid & 7, tid >> 3, tid < 8 * a.batch);
     }
 
     if (EPI == FORGE_EPI_LOGITS && warp < 2) {
