@@ -490,6 +490,10 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-serve", action="store_true")
     ap.add_argument("--only-serve", action="store_true", help="run only the continuous-batching workload")
+    ap.add_argument("--only-step", default=None, metavar="WORKLOAD",
+                    help="run only --warmup + --steps decode steps of WORKLOAD at --batch (for profiling)")
+    ap.add_argument("--ctx", type=int, default=None, help="KV context of --only-step (default: the workload's)")
+    ap.add_argument("--layers", type=int, default=None, help="layers of --only-step (default: the workload's)")
     args = ap.parse_args()
     world, rank, local, pg = dist_setup()
     if args.impl == "reference":
@@ -512,6 +516,25 @@ def main():
         return
     if args.only_serve:
         print(json.dumps(run_serve(fb, torch, local)))
+        return
+    if args.only_step:
+        m = WORKLOADS[args.only_step]
+        ctx = args.ctx or m["ctx"]
+        fm = fb.ForgeModel(args.layers or m["n_layer"], m["d"], m["n_head"], m["n_kv"], m["hd"], m["ffn"], m["vocab"],
+                           weight_kind=fb.FORGE_WEIGHT_Q4_G128 if m["q4"] else fb.FORGE_WEIGHT_BF16,
+                           max_batch=args.batch, max_ctx=ctx + args.warmup + args.steps + 8, device=local)
+        fm.init_synthetic(1234, 0.02)
+        fm.fill_kv_synthetic(99, ctx, 0.5)
+        fm.decode_device(args.batch, args.warmup)
+        fm.sync()
+        t0 = time.perf_counter()
+        fm.decode_device(args.batch, args.steps)
+        fm.sync()
+        print(json.dumps({"workload": args.only_step, "layers": args.layers or m["n_layer"], "batch": args.batch,
+                          "ctx": ctx, "steps": args.steps,
+                          "ms_per_step_wall": (time.perf_counter() - t0) * 1e3 / max(1, args.steps),
+                          "launches_per_step": fm.launches_per_step(args.batch)}))
+        fm.close()
         return
     B, K, W = args.batch, args.steps, max(3, args.warmup)
     r = run_decode(fb, torch, pg, local, world, rank, B, K, W)

@@ -86,8 +86,8 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
             const uint32_t bytes = (uint32_t)rows * HD * 2;
             mbar_arrive_expect_tx(&full[s], 2 * bytes);
             if (!paged) {
-                bulk_g2s(dst, row(a.kc, t0), bytes, &full[s]);
-                bulk_g2s(dst + kTile * HD, row(a.vc, t0), bytes, &full[s]);
+                bulk_g2s_stream(dst, row(a.kc, t0), bytes, &full[s], l2_evict_first());
+                bulk_g2s_stream(dst + kTile * HD, row(a.vc, t0), bytes, &full[s], l2_evict_first());
             } else {
                 for (int r = t0; r < t0 + rows;) {  // one copy per page segment
                     const int seg = min(t0 + rows - r, a.page_tokens - r % a.page_tokens);

@@ -87,6 +87,20 @@ FORGE_DEV void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, ui
         ::"r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// The same copy for data a step reads once (weights, scales, cached K/V
+// rows), marked evict-first in L2: the stream then does not push out of L2
+// what is read again soon (activations, split partials, kernel code).
+FORGE_DEV uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+FORGE_DEV void bulk_g2s_stream(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
 // L2 prefetch of a global range (no smem destination).
 FORGE_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");

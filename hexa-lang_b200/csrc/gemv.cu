@@ -194,6 +194,7 @@ __global__ void __maxnreg__(FORGE_GEMV_MAXNREG) k_gemv(const ForgeGemvArgs a) {
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer
         if (lane == 0) {
+            const uint64_t pol = l2_evict_first();
             const uint8_t* wbase = static_cast<const uint8_t*>(a.w);
             const uint8_t* sbase = static_cast<const uint8_t*>(a.s);
             const int G4 = (KT / 8 + 3) / 4;
@@ -209,10 +210,11 @@ __global__ void __maxnreg__(FORGE_GEMV_MAXNREG) k_gemv(const ForgeGemvArgs a) {
                     uint32_t sb = 0;
                     if (WK == FORGE_W_Q4) sb = (uint32_t)(((nkt / 8) + 3) / 4) * 128u;
                     mbar_arrive_expect_tx(&full[s], wb + sb);
-                    bulk_g2s(stages + s * kStageBytes, wbase + ((int64_t)u * KT + kt0) * kTileBytes, wb, &full[s]);
+                    bulk_g2s_stream(stages + s * kStageBytes, wbase + ((int64_t)u * KT + kt0) * kTileBytes, wb,
+                                    &full[s], pol);
                     if (WK == FORGE_W_Q4)
-                        bulk_g2s(stages + s * kStageBytes + kStageW,
-                                 sbase + ((int64_t)u * G4 + kt0 / 32) * 128, sb, &full[s]);
+                        bulk_g2s_stream(stages + s * kStageBytes + kStageW,
+                                        sbase + ((int64_t)u * G4 + kt0 / 32) * 128, sb, &full[s], pol);
                     ++it;
                 }
             }

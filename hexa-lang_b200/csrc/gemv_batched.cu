@@ -106,9 +106,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
                     const uint32_t wb = (uint32_t)nkt * 128;
                     const uint32_t sb = (uint32_t)(((nkt / 8) + 3) / 4) * 128u;
                     mbar_arrive_expect_tx(&full[s], wb + sb);
-                    bulk_g2s(stages + s * kStageBytes, wbase + ((int64_t)u * KT + kt0) * 128, wb, &full[s]);
-                    bulk_g2s(stages + s * kStageBytes + kStageW, sbase + ((int64_t)u * G4 + kt0 / 32) * 128, sb,
-                             &full[s]);
+                    bulk_g2s_stream(stages + s * kStageBytes, wbase + ((int64_t)u * KT + kt0) * 128, wb, &full[s], l2_evict_first());
+                    bulk_g2s_stream(stages + s * kStageBytes + kStageW, sbase + ((int64_t)u * G4 + kt0 / 32) * 128, sb,
+                                    &full[s], l2_evict_first());
                     ++it;
                 }
             }
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_bf16_b(const ForgeGemvArgs
                     const int kt0 = i * kItemKT, nkt = min(kItemKT, KT - kt0);
                     const uint32_t wb = (uint32_t)nkt * 512;
                     mbar_arrive_expect_tx(&full[s], wb);
-                    bulk_g2s(stages + s * kStageBytes, wbase + ((int64_t)u * KT + kt0) * 512, wb, &full[s]);
+                    bulk_g2s_stream(stages + s * kStageBytes, wbase + ((int64_t)u * KT + kt0) * 512, wb, &full[s], l2_evict_first());
                     ++it;
                 }
             }
