@@ -207,8 +207,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv_b(const ForgeGemvArgs a, c
                     const int sq = min(cb * 4 + t, B - 1);
                     const int shi = sss[gg * 2 * B + 2 * sq], slo = sss[gg * 2 * B + 2 * sq + 1];
                     const float sx = sxs[gg * B + sq];
-                    const float v0 = (float)(c0[0] + c1[0] - 7 * shi) + (float)(c0[1] + c1[1] - 7 * slo) * (1.0f / 256.0f);
-                    const float v1 = (float)(c0[2] + c1[2] - 7 * shi) + (float)(c0[3] + c1[3] - 7 * slo) * (1.0f / 256.0f);
+                    // exact int -> float through the bits of 1.5 * 2^23 (|n| < 2^22), as in q4_group
+                    auto i2f = [](int n) { return __fsub_rn(__int_as_float(n + 0x4B400000), 12582912.0f); };
+                    const float v0 = i2f(c0[0] + c1[0] - 7 * shi) + i2f(c0[1] + c1[1] - 7 * slo) * (1.0f / 256.0f);
+                    const float v1 = i2f(c0[2] + c1[2] - 7 * shi) + i2f(c0[3] + c1[3] - 7 * slo) * (1.0f / 256.0f);
                     const float y0 = bf16_lo_f32(sc) * sx * v0;
                     const float y1 = bf16_hi_f32(sc) * sx * v1;
                     if (h == 0) { totA[cb][0] += y0; totA[cb][1] += y1; }

@@ -280,11 +280,19 @@ __device__ __forceinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, 
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const float x = e[4 * c + j];
-                    // |x| <= amax, so x * is rounds into [-127, 127]: no clamp
-                    const float hq = rintf(x * is);
-                    const float lq = fminf(fmaxf(rintf((x - sc * hq) * is256), -127.f), 127.f);
-                    hi[j] = (int)hq;
-                    lo[j] = (int)lq;
+                    // Round to the nearest integer (ties to even) by adding
+                    // 1.5 * 2^23: for |v| < 2^22 the sum's unit in the last
+                    // place is 1, so the addition rounds v and the integer is
+                    // the low mantissa bits. This is rintf(v) and (int)rintf(v)
+                    // on the FP32 pipe instead of the slower conversion pipe
+                    // (two rounds and two conversions per element); the
+                    // product is rounded first (__fmul_rn, no contraction).
+                    // |x| <= amax, so x * is rounds into [-127, 127]: no clamp.
+                    const float th = __fadd_rn(__fmul_rn(x, is), 12582912.0f);
+                    const float hq = __fsub_rn(th, 12582912.0f);
+                    const float tl = __fadd_rn(__fmul_rn(x - sc * hq, is256), 12582912.0f);
+                    hi[j] = __float_as_int(th) - 0x4B400000;
+                    lo[j] = min(max(__float_as_int(tl) - 0x4B400000, -127), 127);
                 }
                 // low bytes of four ints into one word (byte j = element j)
                 const uint32_t hw = __byte_perm(__byte_perm(hi[0], hi[1], 0x0040), __byte_perm(hi[2], hi[3], 0x0040), 0x5410);
@@ -349,8 +357,12 @@ __device__ __forceinline__ void q4_group(const uint4 w0, const uint4 w1, const u
     const int tb = t < batch ? t : batch - 1;
     const int shi = ssum[gg * 8 + 2 * tb], slo = ssum[gg * 8 + 2 * tb + 1];
     const float sx = sxf[gg * 4 + tb];
-    const float v0 = (float)(c0[0] + c1[0] - 7 * shi) + (float)(c0[1] + c1[1] - 7 * slo) * (1.0f / 256.0f);
-    const float v1 = (float)(c0[2] + c1[2] - 7 * shi) + (float)(c0[3] + c1[3] - 7 * slo) * (1.0f / 256.0f);
+    // int -> float of the group sums (|n| <= 128 * 14 * 127 < 2^22): the
+    // integer added to the bits of 1.5 * 2^23, minus 1.5 * 2^23 — exact, on
+    // the integer and FP32 pipes instead of the conversion pipe
+    auto i2f = [](int n) { return __fsub_rn(__int_as_float(n + 0x4B400000), 12582912.0f); };
+    const float v0 = i2f(c0[0] + c1[0] - 7 * shi) + i2f(c0[1] + c1[1] - 7 * slo) * (1.0f / 256.0f);
+    const float v1 = i2f(c0[2] + c1[2] - 7 * shi) + i2f(c0[3] + c1[3] - 7 * slo) * (1.0f / 256.0f);
     y0 = bf16_lo_f32(scale_pair) * sx * v0;
     y1 = bf16_hi_f32(scale_pair) * sx * v1;
 }
