@@ -275,21 +275,51 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
     if (!is_last) return;
     __threadfence();
 
-    // ---- merge all splits (log-sum-exp), write the fp32 context
+    // ---- merge all splits (log-sum-exp), write the fp32 context. Every
+    // split's (m, l) is loaded at once into shared memory (one L2 round trip
+    // instead of one per split), one thread per head forms the weights and
+    // the normaliser, then every output element sums its splits with all of
+    // its loads issued together. Same operations in the same order as one
+    // thread per element walking the splits.
+    float* mw = reinterpret_cast<float*>(smem);  // [G][nsplit] m, then the weight
+    float* lw = mw + G * nsplit;                 // [G][nsplit] l
+    float* ls = lw + G * nsplit;                 // [G] normaliser
+    for (int idx = tid; idx < G * nsplit; idx += kThreads) {
+        const int g = idx / nsplit, s2 = idx % nsplit;
+        const float* pm = a.partial + (((size_t)b * a.H + kvh * G + g) * nsplit + s2) * stride + HD;
+        mw[idx] = __ldcg(pm);
+        lw[idx] = __ldcg(pm + 1);
+    }
+    __syncthreads();
+    if (tid < G) {
+        float mg = -INFINITY;
+        for (int s2 = 0; s2 < nsplit; ++s2) mg = fmaxf(mg, mw[tid * nsplit + s2]);
+        float lsum = 0.f;
+        for (int s2 = 0; s2 < nsplit; ++s2) {
+            const float ms = mw[tid * nsplit + s2];
+            const float w = ms == -INFINITY ? 0.f : expf(ms - mg);
+            mw[tid * nsplit + s2] = w;
+            lsum = fmaf(w, lw[tid * nsplit + s2], lsum);
+        }
+        ls[tid] = lsum;
+    }
+    __syncthreads();
     for (int idx = tid; idx < G * HD; idx += kThreads) {
         const int g = idx / HD, e = idx % HD;
         const int h = kvh * G + g;
-        const float* pb = a.partial + ((size_t)b * a.H + h) * nsplit * stride;
-        float mg = -INFINITY;
-        for (int s2 = 0; s2 < nsplit; ++s2) mg = fmaxf(mg, __ldcg(pb + s2 * stride + HD));
-        float lsum = 0.f, o = 0.f;
-        for (int s2 = 0; s2 < nsplit; ++s2) {
-            const float ms = __ldcg(pb + s2 * stride + HD);
-            const float w = ms == -INFINITY ? 0.f : expf(ms - mg);
-            lsum = fmaf(w, __ldcg(pb + s2 * stride + HD + 1), lsum);
-            o = fmaf(w, __ldcg(pb + s2 * stride + e), o);
+        const float* pb = a.partial + ((size_t)b * a.H + h) * nsplit * stride + e;
+        const float* wg = mw + g * nsplit;
+        float o = 0.f;
+        int s2 = 0;
+        for (; s2 + 8 <= nsplit; s2 += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __ldcg(pb + (size_t)(s2 + j) * stride);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o = fmaf(wg[s2 + j], v[j], o);
         }
-        a.out[(size_t)b * a.H * HD + (size_t)h * HD + e] = o / lsum;
+        for (; s2 < nsplit; ++s2) o = fmaf(wg[s2], __ldcg(pb + (size_t)s2 * stride), o);
+        a.out[(size_t)b * a.H * HD + (size_t)h * HD + e] = o / ls[g];
     }
     if (tid == 0) a.counters[(size_t)b * a.Hkv + kvh] = 0u;
 }
@@ -383,6 +413,12 @@ int forge_attn_launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl) {
     if (a.table && (a.page_tokens <= 0 || a.max_pages <= 0 || a.num_pages <= 0 ||
                     (int64_t)a.max_pages * a.page_tokens != a.lmax))
         return forge_fail(-1, "flash-decode: bad page geometry");
+    // the merge keeps (m, l) of every split of the CTA's heads in the tile buffers
+    if (a.hd == 128 || a.hd == 64) {
+        const long long merge_bytes = 4LL * (2LL * (a.H / a.Hkv) * a.nsplit + a.H / a.Hkv);
+        const long long tile_bytes = a.hd == 128 ? kStages * stage_bytes<128>() : kStages * stage_bytes<64>();
+        if (merge_bytes > tile_bytes) return forge_fail(-1, "flash-decode: %d splits are too many to merge", a.nsplit);
+    }
     if (a.hd == 128) return launch_g<128>(a, stream, pdl);
     if (a.hd == 64) return launch_g<64>(a, stream, pdl);
     return forge_fail(-1, "flash-decode: head_dim must be 64 or 128 (got %d)", a.hd);
