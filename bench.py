@@ -214,6 +214,35 @@ def time_prefill(fb, torch, dev, B=8, H=32, S=4096, reps=10):
             "launches": reps}
 
 
+def time_model_prefill(fb, torch, local, n_prompt=2048, batch=1, reps=3):
+    """Model-level prompt prefill (forge_b200_prefill) of the 7B int4 model:
+    batch x n_prompt positions through all 32 layers in one pass (K/V
+    written), then the LM head of the last position; wall clock around the
+    synchronous call, best of reps. Weight bytes per 32-row chunk of the
+    batched GEMVs are the floor of this path: tokens/s and the implied
+    weight-stream rate are reported."""
+    import numpy as np
+    m = MODEL
+    fm = fb.ForgeModel(m["n_layer"], m["d"], m["n_head"], m["n_kv"], m["hd"], m["ffn"], m["vocab"],
+                       weight_kind=fb.FORGE_WEIGHT_Q4_G128, max_batch=batch, max_ctx=n_prompt + 8, device=local)
+    fm.init_synthetic(1234, 0.02)
+    prompt = np.random.default_rng(3).integers(0, m["vocab"], (batch, n_prompt)).astype(np.int32)
+    fm.prefill(prompt)  # buffers, batched paths
+    best = 1e9
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        fm.prefill(prompt)
+        best = min(best, time.perf_counter() - t0)
+    wbytes = fm.step_bytes(1, 0)
+    fm.close()
+    rows = batch * n_prompt
+    chunks = -(-rows // 32)
+    return {"workload": f"7b_int4 prompt prefill B{batch} x {n_prompt}", "ms": best * 1e3,
+            "value": rows / best, "unit": "prompt tok/s (wall clock, synchronous call)",
+            "weight_passes": chunks, "weight_gbs": chunks * wbytes / best / 1e9}
+
+
 def all_cores():
     """Host threads for the CPU legs: every core the process may run on
     (torchrun sets OMP_NUM_THREADS=1 for its workers; the CPU legs run on
@@ -516,6 +545,7 @@ def main():
         return
     if args.only_serve:
         print(json.dumps(run_serve(fb, torch, local)))
+        print(json.dumps(time_model_prefill(fb, torch, local)))
         return
     if args.only_step:
         m = WORKLOADS[args.only_step]
@@ -563,6 +593,7 @@ def main():
     achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
     prefill = None if (args.no_prefill or world > 1) else time_prefill(fb, torch, dev)
     serve = None if (args.no_serve or world > 1) else run_serve(fb, torch, local)
+    model_prefill = None if (args.no_prefill or world > 1) else time_model_prefill(fb, torch, local)
     if rank != 0:
         return
     cpu = None
@@ -590,6 +621,7 @@ def main():
         "tp_parity": parity,
         "prefill": prefill,
         "serve": serve,
+        "model_prefill": model_prefill,
         "cpu_baseline": cpu,
     }
     print(json.dumps(out))

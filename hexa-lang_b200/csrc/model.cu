@@ -78,6 +78,34 @@ __global__ void k_argmax_extract(unsigned long long* keys, int B, int32_t* tok) 
     }
 }
 
+// Prompt rows (row b * n + p of a [rows][H * hd] fp32 array) to and from
+// the [B][H][S][hd] bf16 layout of the tensor-core prefill; positions n..S-1
+// of the bf16 side are zero.
+__global__ void k_rows_to_heads_bf16(const float* __restrict__ q, int B, int n, int S, int H, int hd,
+                                     uint16_t* __restrict__ qb) {
+    const int64_t total = (int64_t)B * H * S * hd;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int e = (int)(i % hd);
+        const int64_t r = i / hd;
+        const int p = (int)(r % S);
+        const int64_t bh = r / S;
+        const int hh = (int)(bh % H), b = (int)(bh / H);
+        qb[i] = p < n ? f32_to_bf16_bits(q[(((int64_t)b * n + p) * H + hh) * hd + e]) : (uint16_t)0;
+    }
+}
+__global__ void k_heads_bf16_to_rows(const uint16_t* __restrict__ ob, int B, int n, int S, int H, int hd,
+                                     float* __restrict__ ctx) {
+    const int64_t total = (int64_t)B * n * H * hd;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int e = (int)(i % hd);
+        const int64_t t = i / hd;
+        const int hh = (int)(t % H);
+        const int64_t r = t / H;
+        const int p = (int)(r % n), b = (int)(r / n);
+        ctx[i] = bf16_bits_to_f32(ob[(((int64_t)b * H + hh) * S + p) * hd + e]);
+    }
+}
+
 // dst[r] = src[rows[r]] for r < n, rows of d floats (one CTA per row).
 __global__ void k_gather_rows(const float* __restrict__ src, const int32_t* __restrict__ rows, int d,
                               float* __restrict__ dst) {
@@ -142,6 +170,9 @@ struct ForgeB200 {
         int32_t *tok = nullptr, *pos = nullptr, *seq = nullptr;
         int32_t* sel = nullptr;  // [2][Bmax]: rows that take the LM head, their tokens
         uint32_t* counters = nullptr;
+        // tensor-core prompt attention: Q and O as [B][H][S][hd] bf16
+        uint16_t *qb = nullptr, *ob = nullptr;
+        int64_t qb_cap = 0;
     } pre;
     // multi-kernel step timeline (FORGE_GRAPH_TRACE): [node][grid][4] stamps
     unsigned long long* gtrace = nullptr;
@@ -877,7 +908,8 @@ FORGE_API void forge_b200_destroy(ForgeB200* h) {
     if (h->comm) forge_tp_comm_destroy(h->comm);  // after the graphs that hold its collectives
     for (void* p : h->allocs) cudaFree(p);
     for (void* p : {(void*)h->pre.x, (void*)h->pre.q, (void*)h->pre.ctx, (void*)h->pre.s, (void*)h->pre.partial,
-                    (void*)h->pre.tok, (void*)h->pre.pos, (void*)h->pre.seq, (void*)h->pre.counters})
+                    (void*)h->pre.tok, (void*)h->pre.pos, (void*)h->pre.seq, (void*)h->pre.sel, (void*)h->pre.counters,
+                    (void*)h->pre.qb, (void*)h->pre.ob})
         if (p) cudaFree(p);
     if (h->h_tok) cudaFreeHost(h->h_tok);
     if (h->stream) cudaStreamDestroy(h->stream);
@@ -1156,6 +1188,17 @@ FORGE_API int forge_b200_decode_device(ForgeB200* h, int batch, int n_steps) {
 }
 
 namespace {
+// Shortest prompt that takes the tensor-core attention in prefill
+// (FORGE_PREFILL_FLASH_MIN; default 256).
+int prefill_flash_min() {
+    static const int v = [] {
+        const char* e = getenv("FORGE_PREFILL_FLASH_MIN");
+        const int x = e ? atoi(e) : 256;
+        return x > 0 ? x : 256;
+    }();
+    return v;
+}
+
 // Grows the prefill buffers to R rows (outside any stream capture).
 int prefill_reserve(ForgeB200* h, int64_t R) {
     auto& P = h->pre;
@@ -1164,7 +1207,12 @@ int prefill_reserve(ForgeB200* h, int64_t R) {
     for (void* p : {(void*)P.x, (void*)P.q, (void*)P.ctx, (void*)P.s, (void*)P.partial, (void*)P.tok, (void*)P.pos,
                     (void*)P.seq, (void*)P.sel, (void*)P.counters})
         if (p) cudaFree(p);
+    uint16_t *qb = P.qb, *ob = P.ob;
+    const int64_t qb_cap = P.qb_cap;
     P = {};
+    P.qb = qb;
+    P.ob = ob;
+    P.qb_cap = qb_cap;
     int64_t part = 0;  // split partials for any row count up to R
     for (int64_t r = 1; r <= R; ++r)
         part = std::max(part, r * forge_attn_pick_splits((int)r, h->Hkv, h->lmax));
@@ -1211,10 +1259,47 @@ int prefill_impl(ForgeB200* h, int batch, const int32_t* prompt, int n, int exac
     // exact_mode: 1 hi/lo activations for bf16 weights at any row count,
     // 0 the model's own activation policy (bf16 activations above 4 rows)
     const RowMap rm{P.pos, P.seq, P.partial, P.counters, exact_mode == 1};
+    // Long prompts take the tensor-core causal prefill for attention (bf16 Q,
+    // P and O; K / V read in place from the cache); short ones, and shapes
+    // it does not cover, the split flash-decode per row (fp32 Q and O).
+    const int S = (n + 127) / 128 * 128;
+    const bool flash = h->hd == 128 && n >= prefill_flash_min() && S <= h->lmax && h->H % h->Hkv == 0;
+    if (flash) {
+        const int64_t need = (int64_t)batch * h->H * S * h->hd;
+        if (need > P.qb_cap) {
+            cudaStreamSynchronize(st);
+            if (P.qb) cudaFree(P.qb);
+            if (P.ob) cudaFree(P.ob);
+            P.qb = P.ob = nullptr;
+            P.qb_cap = 0;
+            if (cudaMalloc(&P.qb, 2 * need) != cudaSuccess || cudaMalloc(&P.ob, 2 * need) != cudaSuccess) {
+                cudaGetLastError();
+                return forge_fail(-1, "forge_b200_prefill: out of device memory for %lld attention rows", (long long)need);
+            }
+            P.qb_cap = need;
+        }
+        // cache rows n..S-1 of these sequences are read (masked) by the last
+        // key block: zero them so that no stale value can reach the sums
+        if (S > n)
+            for (int l = 0; l < h->L; ++l)
+                for (uint16_t* c : {h->kc + (size_t)l * h->kv_layer, h->vc + (size_t)l * h->kv_layer})
+                    cudaMemset2DAsync(c + (size_t)n * h->hd, (size_t)h->lmax * h->hd * 2, 0, (size_t)(S - n) * h->hd * 2,
+                                      (size_t)batch * h->Hkv, st);
+    }
+    const int cgrid = 4 * forge_sm_count();
     int rc = forge_embed_launch(h->emb, h->d, h->Vfull, P.tok, (int)R, P.x, h->err, st, false);
-    for (int l = 0; l < h->L && !rc; ++l)
-        rc = enqueue_qkv(h, l, (int)R, P.x, P.q, true, &rm) || enqueue_attn(h, l, (int)R, P.q, P.ctx, false, &rm) ||
-             enqueue_oproj(h, l, (int)R, P.ctx, P.x, true, &rm) || enqueue_mlp(h, l, (int)R, P.x, true, &rm, P.s);
+    for (int l = 0; l < h->L && !rc; ++l) {
+        rc = enqueue_qkv(h, l, (int)R, P.x, P.q, true, &rm);
+        if (!rc && flash) {
+            k_rows_to_heads_bf16<<<cgrid, 256, 0, st>>>(P.q, batch, n, S, h->H, h->hd, P.qb);
+            rc = forge_flash_prefill_kv(P.qb, h->kc + (size_t)l * h->kv_layer, h->vc + (size_t)l * h->kv_layer, P.ob,
+                                        batch, h->H, h->Hkv, S, h->lmax, (int64_t)h->Bmax * h->Hkv * h->lmax, st);
+            if (!rc) k_heads_bf16_to_rows<<<cgrid, 256, 0, st>>>(P.ob, batch, n, S, h->H, h->hd, P.ctx);
+        } else if (!rc) {
+            rc = enqueue_attn(h, l, (int)R, P.q, P.ctx, false, &rm);
+        }
+        rc = rc || enqueue_oproj(h, l, (int)R, P.ctx, P.x, true, &rm) || enqueue_mlp(h, l, (int)R, P.x, true, &rm, P.s);
+    }
     if (rc) return -1;
     // last position of every sequence: final norm, LM head, argmax; the
     // finaliser records the token as step n-1 and moves the positions to n
@@ -1274,6 +1359,7 @@ FORGE_API int forge_b200_prefill(ForgeB200* h, int batch, const int32_t* prompt,
     if (cudaStreamSynchronize(h->stream) != cudaSuccess)
         return forge_fail(-1, "forge_b200_prefill: %s", cudaGetErrorString(cudaGetLastError()));
     if (int e = read_err(h)) return e;
+    if (forge_ops_check()) return -1;  // the tensor-core attention's error word
     if (next_tok && cudaMemcpy(next_tok, h->tok, 4 * (size_t)batch, cudaMemcpyDeviceToHost) != cudaSuccess)
         return forge_fail(-1, "forge_b200_prefill: D2H of the next tokens failed");
     if (logits) {
@@ -1312,6 +1398,7 @@ FORGE_API int forge_b200_generate(ForgeB200* h, int batch, const int32_t* prompt
         rc = forge_fail(-1, "forge_b200_generate: %s", cudaGetErrorString(cudaGetLastError()));
     if (rc) return rc;
     if (int e = read_err(h)) return e;
+    if (forge_ops_check()) return -1;
     std::vector<int32_t> hist((size_t)n_gen * batch);
     if (cudaMemcpy2D(hist.data(), 4 * batch, h->hist + (size_t)(n_prompt - 1) * batch, 4 * batch, 4 * batch, n_gen,
                      cudaMemcpyDeviceToHost) != cudaSuccess)

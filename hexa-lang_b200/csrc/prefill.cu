@@ -46,6 +46,9 @@ struct PrefillArgs {
     int B, H, S, causal;
     float scale_log2;  // log2(e) / sqrt(hd)
     uint32_t* err;
+    // K/V rows: (b * Hkv + h / (H / Hkv)) * kv_ld + position, so K and V can
+    // be a decode KV cache ([B][Hkv][kv_ld][hd], GQA) rather than [B][H][S][hd]
+    int Hkv, kv_ld;
 };
 
 // 2^x with the hardware approximation (ex2.approx, relative error ~2^-22;
@@ -139,6 +142,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int nB = hasB ? (a.causal ? tB + 1 : ntile) : 0;
     const int nblk = nA > nB ? nA : nB;
     const int row0 = (b * a.H + h) * a.S;
+    const int row0kv = (b * a.Hkv + h / (a.H / a.Hkv)) * a.kv_ld;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 if (!mbar_wait(&kv_empty[st], ((it / kPStages) & 1) ^ 1, a.err)) break;
                 uint8_t* dst = base + kPOffKV + st * kTile;
                 const CUtensorMap* map = (it & 1) ? &tv : &tk;
-                const int y = row0 + (it >> 1) * kBN;
+                const int y = row0kv + (it >> 1) * kBN;
                 mbar_arrive_expect_tx(&kv_full[st], kTile);
                 tma_load_2d(dst, map, 0, y, &kv_full[st]);
                 tma_load_2d(dst + kHalf, map, 64, y, &kv_full[st]);
@@ -452,10 +456,32 @@ extern "C" FORGE_API int forge_flash_prefill(const uint16_t* q, const uint16_t* 
     const int64_t rows = (int64_t)B * H * S;
     CUtensorMap mq, mk, mv;
     if (make_map(&mq, q, rows) || make_map(&mk, k, rows) || make_map(&mv, v, rows)) return -1;
-    PrefillArgs a{o, B, H, S, causal ? 1 : 0, (float)(1.4426950408889634 / 11.313708498984761), err};
+    PrefillArgs a{o, B, H, S, causal ? 1 : 0, (float)(1.4426950408889634 / 11.313708498984761), err, H, S};
     dim3 grid((unsigned)((S / kBM + 1) / 2), (unsigned)H, (unsigned)B);
     k_flash_prefill_pp<<<grid, kPThreads, kPSmem, (cudaStream_t)stream>>>(mq, mk, mv, a);
     return forge_check_launch("forge_flash_prefill");
+}
+
+// Causal prefill of B sequences of S positions (S a multiple of 128) with
+// Q and O as [B][H][S][hd] bf16 and K / V read in place from a decode KV
+// cache layer [.. B ..][Hkv][kv_ld][hd] (kv_rows rows in all), GQA heads
+// h -> h / (H / Hkv). Used by the engine's prompt prefill.
+int forge_flash_prefill_kv(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* o, int B, int H,
+                           int Hkv, int S, int kv_ld, int64_t kv_rows, cudaStream_t stream) {
+    if (!q || !kc || !vc || !o || B <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || S <= 0 || S % kBM || kv_ld < S ||
+        (int64_t)B * Hkv * kv_ld > kv_rows || kv_rows > (1ll << 31) - 1 || (int64_t)B * H * S > (1ll << 31) - 1)
+        return forge_fail(FORGE_INVALID_ARGS, "flash prefill (cache): bad shape");
+    if (((uintptr_t)q | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)o) & 15)
+        return forge_fail(FORGE_INVALID_ARGS, "flash prefill (cache): arrays must be 16-byte aligned");
+    if (configure()) return -1;
+    uint32_t* err = forge_ops_err_word();
+    if (!err) return forge_fail(-1, "flash prefill (cache): no device");
+    CUtensorMap mq, mk, mv;
+    if (make_map(&mq, q, (int64_t)B * H * S) || make_map(&mk, kc, kv_rows) || make_map(&mv, vc, kv_rows)) return -1;
+    PrefillArgs a{o, B, H, S, 1, (float)(1.4426950408889634 / 11.313708498984761), err, Hkv, kv_ld};
+    dim3 grid((unsigned)((S / kBM + 1) / 2), (unsigned)H, (unsigned)B);
+    k_flash_prefill_pp<<<grid, kPThreads, kPSmem, stream>>>(mq, mk, mv, a);
+    return forge_check_launch("forge_flash_prefill_kv");
 }
 
 // FLASH_PREFILL family: in = [Q, K, V (HexaFarrBf16, [B][H][S][hd]), causal],

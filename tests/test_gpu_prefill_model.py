@@ -114,3 +114,41 @@ def test_prefill_bf16_activations_close_to_exact(forge, cuda):
     _, fast = fm.prefill(prompt, exact=0, want_logits=True)
     assert np.abs(exact - fast).max() < 2e-2 * max(1.0, np.abs(exact).max())
     fm.close()
+
+
+HD128 = {
+    "mha_hd128_q4": dict(n_layer=2, d=512, n_head=4, n_kv=4, hd=128, ffn=1024, vocab=2048, q4=True, tied=False),
+    "gqa_hd128_bf16": dict(n_layer=2, d=512, n_head=4, n_kv=2, hd=128, ffn=1024, vocab=2048, q4=False, tied=False),
+}
+
+
+@pytest.mark.parametrize("name", list(HD128))
+@pytest.mark.parametrize("n,batch", [(300, 1), (260, 2), (512, 1)])
+def test_long_prompt_tensor_core_attention(forge, oracle, cuda, name, n, batch):
+    """Prompts of 256 positions or more take the tensor-core causal prefill
+    for attention (bf16 Q, P and O, K / V read from the cache, positions
+    padded to a multiple of 128): last-position logits against flame's full
+    recompute in float64 within the bf16 bound, then decode steps on top of
+    the cache the prefill wrote, against the oracle's KV decode."""
+    cfg = HD128[name]
+    om, fm = _models(oracle, forge, cfg, batch, 640)
+    rng = np.random.default_rng(n + batch)
+    prompt = rng.integers(0, cfg["vocab"], (batch, n)).astype(np.int32)
+    nxt, lg = fm.prefill(prompt, exact=1, want_logits=True)
+    for b in range(batch):
+        ref = om.full_forward(prompt[b])
+        err = float(np.abs(lg[b] - ref).max())
+        assert err < 2e-2, f"seq {b}: max |dlogit| {err}"
+        assert np.median(np.abs(lg[b] - ref)) < 3e-3
+    # decode 4 steps after the prefill, sequence 0 against the oracle
+    kc, vc = om.new_cache(1, 640)
+    for p in range(n):
+        ref_lg, ref_am = om.decode_step(kc, vc, [prompt[0, p]], [p], oracle.OR_KV_BF16)
+    tok = [int(ref_am[0])] * batch
+    for s in range(4):
+        got, glg = fm.step(tok, want_logits=True)
+        ref_lg, ref_am = om.decode_step(kc, vc, [tok[0]], [n + s], oracle.OR_KV_BF16)
+        err = float(np.abs(glg[0] - ref_lg[0]).max())
+        assert err < 2e-2, (s, err)
+        tok = [int(ref_am[0])] * batch
+    fm.close()
