@@ -22,7 +22,12 @@
 //
 // The v1 kernels run on the legacy default stream, so the synchronous
 // hexa_farr_*_to_host copies order after them without an explicit sync.
+#include <cublas_v2.h>
+#include <dlfcn.h>
+#include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include "common.cuh"
 #include "forge_internal.h"
@@ -89,6 +94,73 @@ __global__ void __launch_bounds__(256) k_matmul_bf16(const uint16_t* __restrict_
             C[gm * N + gn] = f32_to_bf16_bits(v);
         }
     }
+}
+
+// h = bf16(silu(h)) in place: the FFN's activation on the rounded product.
+__global__ void k_silu_bf16_inplace(uint16_t* __restrict__ h, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = bf16_bits_to_f32(h[i]);
+        h[i] = f32_to_bf16_bits(v / (1.0f + expf(-v)));
+    }
+}
+
+// cuBLAS, opened at run time as the reference reaches it (cublasGemmEx with
+// bf16 operands and fp32 compute, runtime_bf16_emit.hexa:487-540): the
+// tensor-core GEMM for the v1 MATMUL and FFN_FUSED families. One handle per
+// device on the legacy default stream. When the library cannot be opened
+// the 64 x 64 tile kernel above runs instead (one line on stderr).
+struct Blas {
+    void* lib = nullptr;
+    decltype(&cublasCreate_v2) create = nullptr;
+    cublasStatus_t (*gemm)(cublasHandle_t, cublasOperation_t, cublasOperation_t, int, int, int, const void*,
+                           const void*, cudaDataType, int, const void*, cudaDataType, int, const void*, void*,
+                           cudaDataType, int, cublasComputeType_t, cublasGemmAlgo_t) = nullptr;
+    cublasHandle_t handle[64] = {};
+};
+std::mutex g_blas_mu;
+Blas g_blas;
+bool g_blas_tried = false;
+
+// The handle of the current device, or nullptr when cuBLAS is unavailable.
+cublasHandle_t blas_handle() {
+    std::lock_guard<std::mutex> lk(g_blas_mu);
+    if (!g_blas_tried) {
+        g_blas_tried = true;
+        const char* path = getenv("FORGE_CUBLAS_LIB");
+        g_blas.lib = dlopen(path && *path ? path : "libcublas.so.12", RTLD_NOW | RTLD_GLOBAL);
+        if (g_blas.lib) {
+            g_blas.create = (decltype(g_blas.create))dlsym(g_blas.lib, "cublasCreate_v2");
+            g_blas.gemm = (decltype(g_blas.gemm))dlsym(g_blas.lib, "cublasGemmEx");
+        }
+        if (!g_blas.create || !g_blas.gemm)
+            fprintf(stderr, "[forge_b200] cuBLAS not available (%s): v1 MATMUL / FFN_FUSED use the tile kernel\n",
+                    g_blas.lib ? "missing symbols" : dlerror());
+    }
+    if (!g_blas.create || !g_blas.gemm) return nullptr;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!g_blas.handle[dev] && g_blas.create(&g_blas.handle[dev]) != CUBLAS_STATUS_SUCCESS) {
+        g_blas.handle[dev] = nullptr;
+        return nullptr;
+    }
+    return g_blas.handle[dev];
+}
+
+// C[M][N] = A[M][K] B[K][N] (row-major bf16, fp32 accumulation, bf16 RNE
+// result): the column-major product C^T = B^T A^T. Returns 1 when cuBLAS is
+// unavailable or a dimension exceeds its int range.
+int matmul_bf16(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N, int64_t K) {
+    const int64_t lim = (1ll << 31) - 1;
+    cublasHandle_t hd = (M <= lim && N <= lim && K <= lim) ? blas_handle() : nullptr;
+    if (!hd) {
+        k_matmul_bf16<0><<<dim3((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64)), 256>>>(A, B, C, M, N, K);
+        return 0;
+    }
+    const float one = 1.0f, zero = 0.0f;
+    const cublasStatus_t st = g_blas.gemm(hd, CUBLAS_OP_N, CUBLAS_OP_N, (int)N, (int)M, (int)K, &one, B, CUDA_R_16BF,
+                                          (int)N, A, CUDA_R_16BF, (int)K, &zero, C, CUDA_R_16BF, (int)N,
+                                          CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    return st == CUBLAS_STATUS_SUCCESS ? 0 : forge_fail(FORGE_KERNEL_UNSUPPORTED, "cublasGemmEx failed (%d)", (int)st);
 }
 
 // Row RMSNorm (reference _hx_cuda_kern_rmsnorm_mh, runtime_cuda_emit.hexa:
@@ -214,8 +286,7 @@ int v1_matmul(const ForgeShapeInfo* s, const ForgeArgs* in, const ForgeArgs* out
     const uint16_t* B = bf16_in(slot<HexaFarrBf16>(in, 1), s->K * s->N);
     uint16_t* C = bf16_out(slot<HexaFarrBf16>(out, 0), s->M * s->N);
     if (!A || !B || !C) return FORGE_INVALID_ARGS;
-    dim3 grid((unsigned)((s->N + 63) / 64), (unsigned)((s->M + 63) / 64));
-    k_matmul_bf16<0><<<grid, 256>>>(A, B, C, s->M, s->N, s->K);
+    if (matmul_bf16(A, B, C, s->M, s->N, s->K)) return FORGE_KERNEL_UNSUPPORTED;
     return launched("v1 MATMUL");
 }
 
@@ -254,8 +325,10 @@ int v1_ffn(const ForgeShapeInfo* s, const ForgeArgs* in, const ForgeArgs* out) {
         }
         Hd = hbuf[dev];
     }
-    k_matmul_bf16<1><<<dim3((unsigned)((FD + 63) / 64), (unsigned)((M + 63) / 64)), 256>>>(X, W1, Hd, M, FD, D);
-    k_matmul_bf16<0><<<dim3((unsigned)((D + 63) / 64), (unsigned)((M + 63) / 64)), 256>>>(Hd, W2, Y, M, D, FD);
+    if (matmul_bf16(X, W1, Hd, M, FD, D)) return FORGE_KERNEL_UNSUPPORTED;
+    const int64_t nh = M * FD;
+    k_silu_bf16_inplace<<<(unsigned)std::min<int64_t>((nh + 255) / 256, 4 * 148), 256>>>(Hd, nh);
+    if (matmul_bf16(Hd, W2, Y, M, D, FD)) return FORGE_KERNEL_UNSUPPORTED;
     return launched("v1 FFN_FUSED");
 }
 

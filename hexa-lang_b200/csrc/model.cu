@@ -895,6 +895,16 @@ FORGE_API int forge_b200_create_tp(const ForgeModelDesc* desc, int device, const
                                    ForgeB200** out) {
     if (!desc || !nccl_unique_id || desc->tp_size < 1)
         return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create_tp: bad args");
+    if (desc->tp_rank < 0 || desc->tp_rank >= desc->tp_size)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create_tp: rank %d outside 0..%d", desc->tp_rank,
+                          desc->tp_size - 1);
+    // an id that forge_b200_tp_unique_id never wrote (all zero bytes) would
+    // leave every rank waiting in NCCL's bootstrap: refuse it up front
+    const unsigned char* idb = static_cast<const unsigned char*>(nccl_unique_id);
+    bool any = false;
+    for (int i = 0; i < 128; ++i) any |= idb[i] != 0;
+    if (desc->tp_size > 1 && !any)
+        return forge_fail(FORGE_INVALID_ARGS, "forge_b200_create_tp: empty NCCL unique id (all zero bytes)");
     return create_impl(desc, device, nccl_unique_id, out);
 }
 

@@ -92,3 +92,26 @@ def test_gloo_collective_with_a_departed_rank_fails():
         p.join(timeout=60)
     assert msg != "no error", msg
     assert dt < 30.0, dt
+
+
+def test_bad_nccl_unique_id_is_refused_before_any_nccl_call(forge):
+    """An all-zero id (never written by forge_b200_tp_unique_id) and a rank
+    outside 0..tp_size-1 are refused before the device or NCCL is touched,
+    so no rank is left waiting in NCCL's bootstrap; a well-formed id gets as
+    far as the device check (no GPU here)."""
+    import ctypes as C
+    fb = forge
+    d = fb.ForgeModelDesc(2, 256, 4, 4, 64, 512, 1000, 1e-5, 10000.0, 0, 0, 1, 64, 0, 2, 0)
+    h = C.c_void_p()
+    zero = (C.c_ubyte * 128)()
+    rc = fb.lib().forge_b200_create_tp(C.byref(d), 0, zero, C.byref(h))
+    assert rc == fb.FORGE_INVALID_ARGS and b"empty NCCL unique id" in fb.lib().forge_b200_last_error()
+    d.tp_rank = 2
+    some = (C.c_ubyte * 128)(*([7] * 128))
+    rc = fb.lib().forge_b200_create_tp(C.byref(d), 0, some, C.byref(h))
+    assert rc == fb.FORGE_INVALID_ARGS and b"rank 2 outside 0..1" in fb.lib().forge_b200_last_error()
+    import torch
+    if not torch.cuda.is_available():
+        d.tp_rank = 0
+        rc = fb.lib().forge_b200_create_tp(C.byref(d), 0, some, C.byref(h))
+        assert rc != 0 and b"unique id" not in fb.lib().forge_b200_last_error()
