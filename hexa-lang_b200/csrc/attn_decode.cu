@@ -23,6 +23,7 @@
 #include <cmath>
 #include "common.cuh"
 #include "forge_internal.h"
+#include "gemv_core.cuh"
 
 namespace {
 constexpr int kWarps = 4;
@@ -284,6 +285,7 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
     float* mw = reinterpret_cast<float*>(smem);  // [G][nsplit] m, then the weight
     float* lw = mw + G * nsplit;                 // [G][nsplit] l
     float* ls = lw + G * nsplit;                 // [G] normaliser
+    float* vals = mw + ((2 * G * nsplit + G + 3) & ~3);  // [G][HD] merged context (handoff), 16-byte aligned
     for (int idx = tid; idx < G * nsplit; idx += kThreads) {
         const int g = idx / nsplit, s2 = idx % nsplit;
         const float* pm = a.partial + (((size_t)b * a.H + kvh * G + g) * nsplit + s2) * stride + HD;
@@ -319,7 +321,18 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
             for (int j = 0; j < 8; ++j) o = fmaf(wg[s2 + j], v[j], o);
         }
         for (; s2 < nsplit; ++s2) o = fmaf(wg[s2], __ldcg(pb + (size_t)s2 * stride), o);
-        a.out[(size_t)b * a.H * HD + (size_t)h * HD + e] = o / ls[g];
+        const float val = o / ls[g];
+        a.out[(size_t)b * a.H * HD + (size_t)h * HD + e] = val;
+        if (HD == 128 && a.pq_out) vals[idx] = val;
+    }
+    if (HD == 128 && a.pq_out) {
+        // each head's context is one 128-group of the O projection's input:
+        // hand it over staged (one warp per head)
+        __syncthreads();
+        for (int g = warp; g < G; g += kWarps) {
+            const float4 v = reinterpret_cast<const float4*>(vals + g * HD)[lane];
+            pq_group_warp(v, kvh * G + g, b, 2 * a.B, a.H, a.pq_out);
+        }
     }
     if (tid == 0) a.counters[(size_t)b * a.Hkv + kvh] = 0u;
 }
@@ -415,10 +428,13 @@ int forge_attn_launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl) {
         return forge_fail(-1, "flash-decode: bad page geometry");
     // the merge keeps (m, l) of every split of the CTA's heads in the tile buffers
     if (a.hd == 128 || a.hd == 64) {
-        const long long merge_bytes = 4LL * (2LL * (a.H / a.Hkv) * a.nsplit + a.H / a.Hkv);
+        const long long merge_bytes = 4LL * (2LL * (a.H / a.Hkv) * a.nsplit + a.H / a.Hkv + 3 +
+                                             (a.pq_out ? (long long)(a.H / a.Hkv) * a.hd : 0));
         const long long tile_bytes = a.hd == 128 ? kStages * stage_bytes<128>() : kStages * stage_bytes<64>();
         if (merge_bytes > tile_bytes) return forge_fail(-1, "flash-decode: %d splits are too many to merge", a.nsplit);
     }
+    if (a.pq_out && (a.hd != 128 || a.B > 4 || a.table || a.seq_of))
+        return forge_fail(-1, "flash-decode: the staged handoff needs head_dim 128, batch <= 4, contiguous decode");
     if (a.hd == 128) return launch_g<128>(a, stream, pdl);
     if (a.hd == 64) return launch_g<64>(a, stream, pdl);
     return forge_fail(-1, "flash-decode: head_dim must be 64 or 128 (got %d)", a.hd);

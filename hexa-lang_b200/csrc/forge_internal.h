@@ -78,7 +78,18 @@ struct ForgeGemvArgs {
     // Prompt prefill: row b of the launch is position pos[b] of cache
     // sequence seq_of[b] (null: row b is sequence b).
     const int32_t* seq_of;
+    // Quantised-activation handoff (int4 weights, plain prologue, batch <= 4):
+    // pq_in, when set, is the staged block of this GEMV's input, written by
+    // the kernel before it — [K/128][4] f32 scales, [K/128][8] s32 column
+    // sums, [K][2 batch] int8 hi/lo in the shared-memory layout of the
+    // staging — and is copied instead of staged.
+    const uint8_t* pq_in;
 };
+
+// Bytes of a handoff block for K inputs and `batch` sequences.
+__host__ __device__ inline int64_t forge_pq_bytes(int K, int batch) {
+    return (int64_t)(K / 128) * 48 + (int64_t)K * 2 * batch;
+}
 
 // Launches the decode GEMV (one or more launches when the batch exceeds one
 // mma column block). pdl: launch with programmatic stream serialization.
@@ -130,6 +141,10 @@ struct ForgeAttnArgs {
     // Prompt prefill (split kernel, contiguous cache): query row b attends
     // to rows 0..pos[b] of cache sequence seq_of[b] (null: sequence b).
     const int32_t* seq_of;
+    // Handoff (hd 128, B <= 4): the merged context of every head, one
+    // 128-group of the O projection's input, also written staged into this
+    // block (layout of ForgeGemvArgs::pq_in for K = H * hd).
+    uint8_t* pq_out;
 };
 int forge_attn_launch(const ForgeAttnArgs& a, cudaStream_t stream, bool pdl);
 // Flat small-batch flash-decode (attn_flat.cu).

@@ -59,7 +59,7 @@ constexpr int kStageS = 512;                          // q4 scale bytes per piec
 constexpr int kStageBytes = kStageW + kStageS;
 constexpr int kRedFloats = 2 * kConsumerWarps * 16 * 8;  // two unit slots
 constexpr int kMaxG = 128;                            // K <= 16384 (staging keeps K/4/threads float4 in registers)
-constexpr int kFixedSmem = kStages * kStageBytes + 2 * kStages * 8 + kRedFloats * 4;
+constexpr int kFixedSmem = kStages * kStageBytes + 2 * kStages * 8 + 16 + kRedFloats * 4;
 constexpr int kMaxSmem = 227 * 1024;
 
 __device__ __forceinline__ void sys_store_release(uint32_t* p, uint32_t v) {
@@ -165,7 +165,8 @@ __global__ void __maxnreg__(FORGE_GEMV_MAXNREG) k_gemv(const ForgeGemvArgs a) {
     uint8_t* stages = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
     uint64_t* empty = full + kStages;
-    float* red = reinterpret_cast<float*>(empty + kStages);
+    uint64_t* pq_bar = empty + kStages;  // the handoff copy (16 bytes with padding)
+    float* red = reinterpret_cast<float*>(pq_bar + 2);
     // int4: per-group activation scales [G][4] and column sums [G][8], then
     // the int8 activations; bf16: the bf16 hi/lo activations
     float* sxf = red + kRedFloats;
@@ -186,6 +187,7 @@ __global__ void __maxnreg__(FORGE_GEMV_MAXNREG) k_gemv(const ForgeGemvArgs a) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
+        mbar_init(pq_bar, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -230,7 +232,15 @@ __global__ void __maxnreg__(FORGE_GEMV_MAXNREG) k_gemv(const ForgeGemvArgs a) {
     // ---------------------------------------------------------- consumers
     pdl_wait();
     if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4 + 1] = globaltimer_ns();
-    if (WK == FORGE_W_Q4) {
+    if (WK == FORGE_W_Q4 && PRO == FORGE_PRO_PLAIN && a.pq_in) {
+        // the previous kernel staged the activations: one copy of its block
+        if (threadIdx.x == 0) {
+            const uint32_t bytes = (uint32_t)forge_pq_bytes(a.K, a.batch);
+            mbar_arrive_expect_tx(pq_bar, bytes);
+            bulk_g2s(sxf, a.pq_in, bytes, pq_bar);
+        }
+        mbar_wait(pq_bar, 0, a.err);
+    } else if (WK == FORGE_W_Q4) {
         stage_x_q8<PRO, 256>(a, xq, sxf, ssum, red);
     } else {
         stage_x<PRO, 256>(a, xf, red);

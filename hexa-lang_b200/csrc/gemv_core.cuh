@@ -178,6 +178,32 @@ __device__ __forceinline__ int xq_index(int k, int col, int ncols) {
     return (((kp * ncols + col) * 4 + t) * 16) + which * 8 + half * 4 + i;
 }
 
+// The int8 hi/lo arithmetic of one group (shared by the staging below and
+// the kernels that hand staged activations to the next GEMV, so every path
+// writes the same bytes): s = max|x| / 127 (1 for an all-zero group), then
+// per element hi = rint(x / s), lo = rint((x - s hi) 256 / s) clamped to
+// +-127. Rounding to the nearest integer (ties to even) adds 1.5 * 2^23: for
+// |v| < 2^22 the sum's unit in the last place is 1, so the addition rounds v
+// and the integer is the low mantissa bits — rintf and (int)rintf on the
+// FP32 pipe instead of the slower conversion pipe. Products are rounded first
+// (__fmul_rn) and x - s hi is one fused multiply-add.
+__device__ __forceinline__ void quant_scales(float amax, float& sc, float& is, float& is256) {
+    sc = amax > 0.f ? amax / 127.0f : 1.0f;
+    is = amax > 0.f ? 127.0f / amax : 0.0f;
+    is256 = 256.0f * is;
+}
+__device__ __forceinline__ void quant_elem(float x, float sc, float is, float is256, int& hi, int& lo) {
+    // |x| <= amax, so x * is rounds into [-127, 127]: no clamp for hi
+    const float th = __fadd_rn(__fmul_rn(x, is), 12582912.0f);
+    const float hq = __fsub_rn(th, 12582912.0f);
+    const float tl = __fadd_rn(__fmul_rn(__fmaf_rn(-sc, hq, x), is256), 12582912.0f);
+    hi = __float_as_int(th) - 0x4B400000;
+    lo = min(max(__float_as_int(tl) - 0x4B400000, -127), 127);
+}
+__device__ __forceinline__ uint32_t pack4_low_bytes(const int (&v)[4]) {  // byte j = v[j]
+    return __byte_perm(__byte_perm(v[0], v[1], 0x0040), __byte_perm(v[2], v[3], 0x0040), 0x5410);
+}
+
 // int4-weight prologue: activations become int8 pairs per 128-group and
 // sequence b: s = max|x| / 127, hi = rint(x / s), lo = rint((x - s*hi)*256/s)
 // (both clamped to +-127), so x = s*(hi + lo/256) to ~2^-16 of the group
@@ -270,33 +296,17 @@ __device__ __forceinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, 
             for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(e[j]));
 #pragma unroll
             for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
-            const float is = amax > 0.f ? 127.0f / amax : 0.0f;
-            const float is256 = 256.0f * is;
+            float sc, is, is256;
+            quant_scales(amax, sc, is, is256);
             int shi = 0, slo = 0;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 int hi[4], lo[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float x = e[4 * c + j];
-                    // Round to the nearest integer (ties to even) by adding
-                    // 1.5 * 2^23: for |v| < 2^22 the sum's unit in the last
-                    // place is 1, so the addition rounds v and the integer is
-                    // the low mantissa bits. This is rintf(v) and (int)rintf(v)
-                    // on the FP32 pipe instead of the slower conversion pipe
-                    // (two rounds and two conversions per element); the
-                    // product is rounded first (__fmul_rn, no contraction).
-                    // |x| <= amax, so x * is rounds into [-127, 127]: no clamp.
-                    const float th = __fadd_rn(__fmul_rn(x, is), 12582912.0f);
-                    const float hq = __fsub_rn(th, 12582912.0f);
-                    const float tl = __fadd_rn(__fmul_rn(x - sc * hq, is256), 12582912.0f);
-                    hi[j] = __float_as_int(th) - 0x4B400000;
-                    lo[j] = min(max(__float_as_int(tl) - 0x4B400000, -127), 127);
-                }
+                for (int j = 0; j < 4; ++j) quant_elem(e[4 * c + j], sc, is, is256, hi[j], lo[j]);
                 // low bytes of four ints into one word (byte j = element j)
-                const uint32_t hw = __byte_perm(__byte_perm(hi[0], hi[1], 0x0040), __byte_perm(hi[2], hi[3], 0x0040), 0x5410);
-                const uint32_t lw = __byte_perm(__byte_perm(lo[0], lo[1], 0x0040), __byte_perm(lo[2], lo[3], 0x0040), 0x5410);
+                const uint32_t hw = pack4_low_bytes(hi);
+                const uint32_t lw = pack4_low_bytes(lo);
                 shi = __dp4a((int)hw, 0x01010101, shi);  // sum of the four signed bytes
                 slo = __dp4a((int)lw, 0x01010101, slo);
                 if (k0 < K) {
@@ -330,6 +340,42 @@ __device__ __forceinline__ void stage_x_q8(const ForgeGemvArgs& a, uint8_t* xq, 
             }
             quantise(p, v);
         }
+    }
+}
+
+// The staged form of 128-group g of sequence b, from its 128 values held
+// four per lane (lane l: elements 4l .. 4l+3), into a handoff block
+// (ForgeGemvArgs::pq_in layout, G groups, ncols = 2 x batch). Every lane of
+// the warp calls it; the bytes equal stage_x_q8's for the same values.
+__device__ __forceinline__ void pq_group_warp(float4 v, int g, int b, int ncols, int G, uint8_t* blk) {
+    float* sxf = reinterpret_cast<float*>(blk);
+    int* ssum = reinterpret_cast<int*>(sxf + G * 4);
+    uint8_t* xq = reinterpret_cast<uint8_t*>(ssum + G * 8);
+    const int lane = threadIdx.x & 31;
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float sc, is, is256;
+    quant_scales(amax, sc, is, is256);
+    int hi[4], lo[4];
+    quant_elem(v.x, sc, is, is256, hi[0], lo[0]);
+    quant_elem(v.y, sc, is, is256, hi[1], lo[1]);
+    quant_elem(v.z, sc, is, is256, hi[2], lo[2]);
+    quant_elem(v.w, sc, is, is256, hi[3], lo[3]);
+    const uint32_t hw = pack4_low_bytes(hi), lw = pack4_low_bytes(lo);
+    const int k = g * 128 + 4 * lane;
+    *reinterpret_cast<uint32_t*>(xq + xq_index(k, 2 * b, ncols)) = hw;
+    *reinterpret_cast<uint32_t*>(xq + xq_index(k, 2 * b + 1, ncols)) = lw;
+    int shi = __dp4a((int)hw, 0x01010101, 0), slo = __dp4a((int)lw, 0x01010101, 0);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        shi += __shfl_xor_sync(0xffffffffu, shi, o);
+        slo += __shfl_xor_sync(0xffffffffu, slo, o);
+    }
+    if (lane == 0) {
+        sxf[g * 4 + b] = sc;
+        ssum[g * 8 + 2 * b] = shi;
+        ssum[g * 8 + 2 * b + 1] = slo;
     }
 }
 

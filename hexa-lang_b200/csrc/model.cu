@@ -147,6 +147,12 @@ struct ForgeB200 {
     uint32_t* counters = nullptr;
     int nsplit = 1;
     bool flat_attn = false;  // small batches on attn_flat.cu (FORGE_ATTN=flat)
+    // Staged-context handoff for batch <= 4 (int4 weights, head dim 128, one
+    // GPU): the flash-decode merge stages each head's context for the O
+    // projection, which copies the block instead of staging (FORGE_PREQUANT=0
+    // turns it off)
+    bool prequant = false;
+    uint8_t* pq_ctx = nullptr;
     uint32_t* err = nullptr;
     uint16_t *stA = nullptr, *stB = nullptr;
     uint8_t* codes = nullptr;
@@ -414,6 +420,10 @@ int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl, 
     return forge_gemv_launch(g, h->stream, pdl);
 }
 
+// Whether the decode step at batch B hands the staged context from the
+// flash-decode merge to the O projection.
+bool pq_ctx_on(const ForgeB200* h, int B) { return h->prequant && B <= 4 && h->hd == 128 && !h->flat_attn; }
+
 // Split-K flash-decode over positions 0..pos of every sequence.
 int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pdl, const RowMap* rm = nullptr) {
     ForgeAttnArgs at{};
@@ -432,6 +442,7 @@ int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pd
         at.flat_slots = forge_attn_flat_slots(h->hd, h->lmax);
         return forge_attn_flat_launch(at, h->stream, pdl);
     }
+    if (pq_ctx_on(h, B)) at.pq_out = h->pq_ctx;
     at.nsplit = forge_attn_pick_splits(B, h->Hkv, h->lmax);
     return forge_attn_launch(at, h->stream, pdl);
 }
@@ -444,6 +455,7 @@ int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool p
     g.w = Ld.o_w; g.s = Ld.o_s; g.N = h->d; g.K = h->qd; g.x = ctx; g.x_stride = h->qd;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
     g.trace = trace_slot(h);
+    if (!rm && pq_ctx_on(h, B)) g.pq_in = h->pq_ctx;
     return resid_gemv(h, g, x, B, pdl);
 }
 
@@ -798,6 +810,14 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
                 partial_floats = std::max(partial_floats, (size_t)forge_attn_flat_partial_floats(B, h->H, h->hd, h->lmax));
     }
     h->partial = (float*)h->alloc(sizeof(float) * partial_floats);
+    {
+        const char* e = getenv("FORGE_PREQUANT");
+        h->prequant = h->q4 && T == 1 && !(e && strcmp(e, "0") == 0);
+        if (h->prequant) {
+            h->pq_ctx = (uint8_t*)h->alloc((size_t)forge_pq_bytes(h->qd, 4));
+            if (!h->pq_ctx) h->prequant = false;
+        }
+    }
     h->bar = (unsigned long long*)h->alloc(16);
     h->epoch = (uint32_t*)h->alloc(16);
     {

@@ -139,3 +139,28 @@ def test_fused_and_graph_paths_agree(forge, oracle, cuda, name, monkeypatch):
         outs.append(np.array(lgs))
         fm.close()
     assert np.abs(outs[0] - outs[1]).max() < 2e-3
+
+
+@pytest.mark.parametrize("batch", [1, 2, 4])
+def test_context_handoff_bit_identical(forge, oracle, cuda, batch, monkeypatch):
+    """int4, head dim 128, up to 4 sequences: the flash-decode merge hands
+    each head's context to the O projection already staged (int8 hi/lo
+    groups, scales, column sums), which copies it instead of staging. The
+    bytes equal the staging's, so logits and tokens are bit-identical with
+    the handoff off (FORGE_PREQUANT=0, read at handle creation)."""
+    cfg = CONFIGS["mha_q4"]
+    monkeypatch.setenv("FORGE_DECODE_PATH", "graph")
+    runs = []
+    for pq in ("1", "0"):
+        monkeypatch.setenv("FORGE_PREQUANT", pq)
+        _, fm = _models(oracle, forge, cfg, batch, 64)
+        fm.init_synthetic(1234, 0.02)
+        fm.fill_kv_synthetic(5, 20, 0.5)
+        toks = np.arange(batch, dtype=np.int32) * 37 + 3
+        lgs = []
+        for _ in range(6):
+            toks, lg = fm.step(toks, want_logits=True)
+            lgs.append(lg)
+        fm.close()
+        runs.append(np.stack(lgs))
+    assert np.array_equal(runs[0], runs[1])
