@@ -356,13 +356,8 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
                 uint32_t acc[2][16];  // columns past 2 x batch hold stale values, never stored
                 tmem_ld16(tl_addr + (uint32_t)((tb * kGU + h) * 64), acc[0]);
                 tmem_ld16(tl_addr + (uint32_t)((tb * kGU + h) * 64 + 16), acc[1]);
-                tmem_wait_ld();
-                if (h == nh - 1) {  // every accumulator of the unit read
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[tb]);
-                }
-                // this warp's scales and bias terms of group 2 g + h
+                // this warp's scales and bias terms of group 2 g + h, loaded
+                // while the accumulator load is in flight
                 const int aux = (h ? kSlotAct1 : kSlotAct0) + kActTile;
                 const float4* sx4 = reinterpret_cast<const float4*>(slot + aux);
                 const int4* bias4 = reinterpret_cast<const int4*>(slot + aux + 128);
@@ -382,6 +377,12 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
                         const int4 bj = bias4[4 * cc + j];
                         bias[c][4 * j] = bj.x; bias[c][4 * j + 1] = bj.y; bias[c][4 * j + 2] = bj.z; bias[c][4 * j + 3] = bj.w;
                     }
+                }
+                tmem_wait_ld();
+                if (h == nh - 1) {  // every accumulator of the unit read
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[tb]);
                 }
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
