@@ -425,7 +425,11 @@ int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl, 
 bool pq_ctx_on(const ForgeB200* h, int B) { return h->prequant && B <= 4 && h->hd == 128 && !h->flat_attn; }
 
 // Split-K flash-decode over positions 0..pos of every sequence.
-int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pdl, const RowMap* rm = nullptr) {
+// handoff: the decode step's own chain (attention then O projection of the
+// same context); block-level callers pass their own context to the O
+// projection, so they never take it.
+int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pdl, const RowMap* rm = nullptr,
+                 bool handoff = false) {
     ForgeAttnArgs at{};
     at.q = q; at.kc = h->kc + (size_t)l * h->kv_layer; at.vc = h->vc + (size_t)l * h->kv_layer; at.pos = h->pos;
     at.B = B; at.H = h->H; at.Hkv = h->Hkv; at.hd = h->hd; at.lmax = h->lmax;
@@ -442,20 +446,21 @@ int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pd
         at.flat_slots = forge_attn_flat_slots(h->hd, h->lmax);
         return forge_attn_flat_launch(at, h->stream, pdl);
     }
-    if (pq_ctx_on(h, B)) at.pq_out = h->pq_ctx;
+    if (handoff && pq_ctx_on(h, B)) at.pq_out = h->pq_ctx;
     at.nsplit = forge_attn_pick_splits(B, h->Hkv, h->lmax);
     return forge_attn_launch(at, h->stream, pdl);
 }
 
 // x += Wo ctx
-int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool pdl, const RowMap* rm = nullptr) {
+int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool pdl, const RowMap* rm = nullptr,
+                  bool handoff = false) {
     const LayerDev& Ld = h->layers[l];
     ForgeGemvArgs g = gemv_base(h, B);
     if (rm && rm->exact) g.split = 1;
     g.w = Ld.o_w; g.s = Ld.o_s; g.N = h->d; g.K = h->qd; g.x = ctx; g.x_stride = h->qd;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
     g.trace = trace_slot(h);
-    if (!rm && pq_ctx_on(h, B)) g.pq_in = h->pq_ctx;
+    if (handoff && !rm && pq_ctx_on(h, B)) g.pq_in = h->pq_ctx;
     return resid_gemv(h, g, x, B, pdl);
 }
 
@@ -496,8 +501,8 @@ int enqueue_step(ForgeB200* h, int B) {
     cudaStream_t st = h->stream;
     if (forge_embed_launch(h->emb, h->d, h->Vfull, h->tok, B, h->x, h->err, st, false)) return -1;
     for (int l = 0; l < h->L; ++l) {
-        if (enqueue_qkv(h, l, B, h->x, h->q, true) || enqueue_attn(h, l, B, h->q, h->ctx, true) ||
-            enqueue_oproj(h, l, B, h->ctx, h->x, true) || enqueue_mlp(h, l, B, h->x, true))
+        if (enqueue_qkv(h, l, B, h->x, h->q, true) || enqueue_attn(h, l, B, h->q, h->ctx, true, nullptr, true) ||
+            enqueue_oproj(h, l, B, h->ctx, h->x, true, nullptr, true) || enqueue_mlp(h, l, B, h->x, true))
             return -1;
     }
     if (enqueue_head(h, B, h->x, true)) return -1;

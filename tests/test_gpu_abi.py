@@ -281,3 +281,50 @@ def test_block_entries_chain_equals_decode_step(forge, cuda, q4):
     for f in (LG, X):
         L.hexa_farr_f32_free(f)
     m.close()
+
+
+@pytest.mark.parametrize("B", [1, 4])
+def test_block_entries_with_context_handoff(forge, cuda, B):
+    """Head dim 128, int4, up to 4 sequences: the decode step hands the
+    staged context from the flash-decode merge to the O projection; the
+    block-level chain (which stages the context it is given) still equals
+    the step bit for bit, and o_proj on a context of the caller's own after
+    an attention call uses that context, not the step's handoff block."""
+    import torch
+    F = forge
+    nl, d, H, Hkv, hd, ffn, V, P0 = 2, 512, 4, 4, 128, 1024, 1000, 20
+    m = F.ForgeModel(nl, d, H, Hkv, hd, ffn, V, weight_kind=F.FORGE_WEIGHT_Q4_G128, max_batch=4, max_ctx=64)
+    m.init_synthetic(99, 0.05)
+    m.fill_kv_synthetic(3, P0, 0.5)
+    tok = (np.arange(B, dtype=np.int32) * 211 + 5) % V
+    nxt, lg = m.step(tok, want_logits=True)
+    m.set_positions([P0] * B)
+    x = torch.empty((B, d), device=cuda)
+    q = torch.empty((B, H * hd), device=cuda)
+    ctx = torch.empty((B, H * hd), device=cuda)
+    out_tok = torch.empty(B, dtype=torch.int32, device=cuda)
+    logits = torch.empty((B, V), device=cuda)
+    torch.cuda.synchronize()
+    m.embed(B, torch.from_numpy(tok).to(cuda), x)
+    for layer in range(nl):
+        m.qkv_rope(layer, B, x, q)
+        m.attention(layer, B, q, ctx)
+        m.o_proj(layer, B, ctx, x)
+        m.mlp(layer, B, x, x)
+    m.lm_head(B, x, out_tok, logits)
+    m.sync()
+    assert np.array_equal(logits.cpu().numpy(), lg) and np.array_equal(out_tok.cpu().numpy(), nxt)
+
+    # a context of the caller's own, right after an attention call
+    own = torch.randn((B, H * hd), device=cuda) * 0.3
+    x0 = torch.randn((B, d), device=cuda)
+    x1, x2 = x0.clone(), x0.clone()
+    m.attention(0, B, q, ctx)
+    m.o_proj(0, B, own, x1)
+    m.sync()
+    m2 = F.ForgeModel(nl, d, H, Hkv, hd, ffn, V, weight_kind=F.FORGE_WEIGHT_Q4_G128, max_batch=4, max_ctx=64)
+    m2.init_synthetic(99, 0.05)
+    m2.o_proj(0, B, own, x2)
+    m2.sync()
+    assert torch.equal(x1, x2)
+    m.close(); m2.close()
