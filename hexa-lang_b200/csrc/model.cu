@@ -147,10 +147,10 @@ struct ForgeB200 {
     uint32_t* counters = nullptr;
     int nsplit = 1;
     bool flat_attn = false;  // small batches on attn_flat.cu (FORGE_ATTN=flat)
-    // Staged-context handoff for batch <= 4 (int4 weights, head dim 128, one
-    // GPU): the flash-decode merge stages each head's context for the O
-    // projection, which copies the block instead of staging (FORGE_PREQUANT=0
-    // turns it off)
+    // Staged-context handoff for batch <= 4 (int4 weights, head dim 128; a
+    // rank's own heads under tensor parallelism): the flash-decode merge
+    // stages each head's context for the O projection, which copies the
+    // block instead of staging (FORGE_PREQUANT=0 turns it off)
     bool prequant = false;
     uint8_t* pq_ctx = nullptr;
     uint32_t* err = nullptr;
@@ -817,7 +817,7 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
     h->partial = (float*)h->alloc(sizeof(float) * partial_floats);
     {
         const char* e = getenv("FORGE_PREQUANT");
-        h->prequant = h->q4 && T == 1 && !(e && strcmp(e, "0") == 0);
+        h->prequant = h->q4 && !(e && strcmp(e, "0") == 0);
         if (h->prequant) {
             h->pq_ctx = (uint8_t*)h->alloc((size_t)forge_pq_bytes(h->qd, 4));
             if (!h->pq_ctx) h->prequant = false;
