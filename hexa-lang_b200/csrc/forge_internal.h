@@ -231,6 +231,6 @@ int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStrea
 // Per-device error word of the per-op entries (created on first use).
 uint32_t* forge_ops_err_word();
 int forge_flash_prefill_kv(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* o, int B, int H,
-                           int Hkv, int S, int kv_ld, int64_t kv_rows, cudaStream_t stream);
+                           int Hkv, int S, int hd, int kv_ld, int64_t kv_rows, cudaStream_t stream);
 // v2 FLASH_PREFILL family.
 int forge_prefill_dispatch(const ForgeShapeInfo* s, const ForgeArgs* in, const ForgeArgs* out);

@@ -1298,7 +1298,7 @@ int prefill_impl(ForgeB200* h, int batch, const int32_t* prompt, int n, int exac
     // P and O; K / V read in place from the cache); short ones, and shapes
     // it does not cover, the split flash-decode per row (fp32 Q and O).
     const int S = (n + 127) / 128 * 128;
-    const bool flash = h->hd == 128 && n >= prefill_flash_min() && S <= h->lmax && h->H % h->Hkv == 0;
+    const bool flash = (h->hd == 128 || h->hd == 64) && n >= prefill_flash_min() && S <= h->lmax && h->H % h->Hkv == 0;
     if (flash) {
         const int64_t need = (int64_t)batch * h->H * S * h->hd;
         if (need > P.qb_cap) {
@@ -1328,7 +1328,7 @@ int prefill_impl(ForgeB200* h, int batch, const int32_t* prompt, int n, int exac
         if (!rc && flash) {
             k_rows_to_heads_bf16<<<cgrid, 256, 0, st>>>(P.q, batch, n, S, h->H, h->hd, P.qb);
             rc = forge_flash_prefill_kv(P.qb, h->kc + (size_t)l * h->kv_layer, h->vc + (size_t)l * h->kv_layer, P.ob,
-                                        batch, h->H, h->Hkv, S, h->lmax, (int64_t)h->Bmax * h->Hkv * h->lmax, st);
+                                        batch, h->H, h->Hkv, S, h->hd, h->lmax, (int64_t)h->Bmax * h->Hkv * h->lmax, st);
             if (!rc) k_heads_bf16_to_rows<<<cgrid, 256, 0, st>>>(P.ob, batch, n, S, h->H, h->hd, P.ctx);
         } else if (!rc) {
             rc = enqueue_attn(h, l, (int)R, P.q, P.ctx, false, &rm);

@@ -1,6 +1,6 @@
 // prefill.cu — causal flash-attention prefill on the 5th-generation tensor
-// cores (tcgen05 + TMEM, TMA-fed), head_dim 128, bf16 in / bf16 out, fp32
-// accumulation.
+// cores (tcgen05 + TMEM, TMA-fed), head_dim 128 or 64, bf16 in / bf16 out,
+// fp32 accumulation.
 //
 // Semantics follow nn_attn_core_fwd (stdlib/flame/nn_lib.hexa:221-278):
 // O = softmax(Q K^T / sqrt(hd) + causal mask) V per (batch, head), the mask
@@ -25,6 +25,7 @@
 //                      and finally O / l to global memory.
 // Every wait is bounded (error word, then the CTA drains its copies and
 // tensor-core work and frees its TMEM).
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include "tcgen05.cuh"
@@ -33,13 +34,12 @@
 #include "../../include/forge_farr.h"
 
 namespace {
-constexpr int kHD = 128;                  // head dim (the K of S = Q K^T)
 constexpr int kBM = 128;                  // query rows per CTA
 constexpr int kBN = 128;                  // keys per block
-constexpr int kTile = kBM * kHD * 2;      // 32 KB: one Q / K / V / P tile
-constexpr int kHalf = kTile / 2;          // 16 KB: 64 columns x 128 rows, swizzled
+constexpr int kHalf = 128 * 64 * 2;       // 16 KB: 64 columns x 128 rows, swizzled
+// one Q / K / V tile: HD / 64 such halves (32 KB at head dim 128, 16 KB at 64)
+template <int HD> constexpr int tile_bytes() { return kBM * HD * 2; }
 constexpr uint32_t kIdescS = umma_idesc_bf16_f32(kBM, kBN, false);  // B = K rows, K-major
-constexpr uint32_t kIdescO = umma_idesc_bf16_f32(kBM, kHD, true);   // B = V rows, MN-major
 
 struct PrefillArgs {
     uint16_t* o;
@@ -104,10 +104,13 @@ constexpr int kPThreads = 320;            // warps 0-3 softmax A, 4-7 softmax B,
 #define FORGE_PREFILL_STAGES 4
 #endif
 constexpr int kPStages = FORGE_PREFILL_STAGES;  // K/V ring slots (4 or 5 fit)
-constexpr int kPOffQ = 0, kPOffKV = 2 * kTile, kPOffBar = (2 + kPStages) * kTile;
-constexpr int kPSmem = kPOffBar + 256 + 1024;
+constexpr int kPOffQ = 0;
+template <int HD> constexpr int off_kv() { return 2 * tile_bytes<HD>(); }
+template <int HD> constexpr int off_bar() { return (2 + kPStages) * tile_bytes<HD>(); }
+template <int HD> constexpr int psmem() { return off_bar<HD>() + 256 + 1024; }
 constexpr uint32_t kPTmemCols = 512;
 
+template <int HD>
 __global__ void __launch_bounds__(kPThreads, 1)
     k_flash_prefill_pp(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const PrefillArgs a) {
@@ -115,7 +118,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
     const uint32_t sbase = smem_u32(base);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(base + kPOffBar);
+    constexpr int kTile = tile_bytes<HD>();
+    constexpr int kNH = HD / 64;  // 64-column halves of a tile
+    constexpr int kPOffKV = off_kv<HD>();
+    constexpr uint32_t kIdescO = umma_idesc_bf16_f32(kBM, HD, true);  // B = V rows, MN-major
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + off_bar<HD>());
     uint64_t* q_full = bars + 0;
     uint64_t* s_full = bars + 1;    // [2] per tile
     uint64_t* p_full = bars + 3;    // [2]
@@ -173,11 +180,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (lane == 0) {
             // Q of both tiles, then the K ring
             mbar_arrive_expect_tx(q_full, hasB ? 2 * kTile : kTile);
-            tma_load_2d(base + kPOffQ, &tq, 0, row0 + tA * kBM, q_full);
-            tma_load_2d(base + kPOffQ + kHalf, &tq, 64, row0 + tA * kBM, q_full);
-            if (hasB) {
-                tma_load_2d(base + kPOffQ + kTile, &tq, 0, row0 + tB * kBM, q_full);
-                tma_load_2d(base + kPOffQ + kTile + kHalf, &tq, 64, row0 + tB * kBM, q_full);
+#pragma unroll
+            for (int h2 = 0; h2 < kNH; ++h2) {
+                tma_load_2d(base + kPOffQ + h2 * kHalf, &tq, 64 * h2, row0 + tA * kBM, q_full);
+                if (hasB) tma_load_2d(base + kPOffQ + kTile + h2 * kHalf, &tq, 64 * h2, row0 + tB * kBM, q_full);
             }
             // item i of the ring: block i / 2, K when i is even, V when odd
             const int nitem = 2 * nblk;
@@ -189,8 +195,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const CUtensorMap* map = (it & 1) ? &tv : &tk;
                 const int y = row0kv + (it >> 1) * kBN;
                 mbar_arrive_expect_tx(&kv_full[st], kTile);
-                tma_load_2d(dst, map, 0, y, &kv_full[st]);
-                tma_load_2d(dst + kHalf, map, 64, y, &kv_full[st]);
+#pragma unroll
+                for (int h2 = 0; h2 < kNH; ++h2) tma_load_2d(dst + h2 * kHalf, map, 64 * h2, y, &kv_full[st]);
                 issued = it + 1;
             }
             // every copy issued has landed before the CTA may exit
@@ -210,7 +216,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const uint32_t kb = slot_addr(2 * j);
                 const uint32_t qb = sbase + (uint32_t)(kPOffQ + t * kTile);
 #pragma unroll
-                for (int s = 0; s < kHD / 16; ++s) {
+                for (int s = 0; s < HD / 16; ++s) {
                     const uint32_t off = (uint32_t)((s >> 2) * kHalf + (s & 3) * 32);
                     umma_bf16(tS[t], umma_desc_sw128(qb + off, 16, 1024), umma_desc_sw128(kb + off, 16, 1024),
                               kIdescS, s > 0 ? 1u : 0u);
@@ -315,7 +321,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, raise)) {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
+                    for (int q = 0; q < HD / 32; ++q) {
                         uint32_t ov[32];
                         tmem_ld32(tOm + lrow + 32 * q, ov);
                         tmem_wait_ld();
@@ -364,9 +370,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (ok && __all_sync(0xffffffffu, mbar_wait(&o_done[t], (nmine - 1) & 1, a.err))) {
             tc_fence_after();
             const float inv = 1.0f / l;
-            uint16_t* orow = a.o + ((size_t)row0 + (size_t)qt * kBM + r) * kHD;
+            uint16_t* orow = a.o + ((size_t)row0 + (size_t)qt * kBM + r) * HD;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < HD / 32; ++q) {
                 uint32_t ov[32];
                 tmem_ld32(tOm + lrow + 32 * q, ov);
                 tmem_wait_ld();
@@ -398,11 +404,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
 // ---- host ------------------------------------------------------------------------
 // [rows][128] bf16 viewed as 64-column x 128-row boxes, 128-byte swizzle.
-int make_map(CUtensorMap* m, const void* ptr, int64_t rows) {
+int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int hd) {
     ForgeEncodeTiled enc = forge_tensor_map_encoder();
     if (!enc) return forge_fail(-1, "flash prefill: cuTensorMapEncodeTiled unavailable");
-    const cuuint64_t dims[2] = {(cuuint64_t)kHD, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)kHD * 2};
+    const cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)hd * 2};
     const cuuint32_t box[2] = {64, 128};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
@@ -418,7 +424,9 @@ int configure() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return forge_fail(-1, "flash prefill: no device");
     if (done[dev]) return 0;
-    cudaError_t e = cudaFuncSetAttribute(k_flash_prefill_pp, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
+    cudaError_t e = cudaFuncSetAttribute(k_flash_prefill_pp<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, psmem<128>());
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_flash_prefill_pp<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, psmem<64>());
     if (e != cudaSuccess) return forge_fail(-1, "flash prefill: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done[dev] = true;
     return 0;
@@ -444,7 +452,8 @@ extern "C" FORGE_API int forge_flash_prefill(const uint16_t* q, const uint16_t* 
                                              int B, int H, int S, int hd, int causal, void* stream) {
     if (!q || !k || !v || !o || B <= 0 || H <= 0 || S <= 0)
         return forge_fail(FORGE_INVALID_ARGS, "forge_flash_prefill: bad args");
-    if (hd != kHD) return forge_fail(FORGE_KERNEL_UNSUPPORTED, "forge_flash_prefill: head_dim %d (only 128)", hd);
+    if (hd != 128 && hd != 64)
+        return forge_fail(FORGE_KERNEL_UNSUPPORTED, "forge_flash_prefill: head_dim %d (128 or 64)", hd);
     if (S % kBM) return forge_fail(FORGE_KERNEL_UNSUPPORTED, "forge_flash_prefill: seq_len %d not a multiple of 128", S);
     if ((int64_t)B * H * S > (1ll << 31) - 1 || H > 65535 || B > 65535)
         return forge_fail(FORGE_INVALID_ARGS, "forge_flash_prefill: shape too large");
@@ -455,10 +464,13 @@ extern "C" FORGE_API int forge_flash_prefill(const uint16_t* q, const uint16_t* 
     if (!err) return forge_fail(-1, "forge_flash_prefill: no device");
     const int64_t rows = (int64_t)B * H * S;
     CUtensorMap mq, mk, mv;
-    if (make_map(&mq, q, rows) || make_map(&mk, k, rows) || make_map(&mv, v, rows)) return -1;
-    PrefillArgs a{o, B, H, S, causal ? 1 : 0, (float)(1.4426950408889634 / 11.313708498984761), err, H, S};
+    if (make_map(&mq, q, rows, hd) || make_map(&mk, k, rows, hd) || make_map(&mv, v, rows, hd)) return -1;
+    PrefillArgs a{o, B, H, S, causal ? 1 : 0, (float)(1.4426950408889634 / std::sqrt((double)hd)), err, H, S};
     dim3 grid((unsigned)((S / kBM + 1) / 2), (unsigned)H, (unsigned)B);
-    k_flash_prefill_pp<<<grid, kPThreads, kPSmem, (cudaStream_t)stream>>>(mq, mk, mv, a);
+    if (hd == 128)
+        k_flash_prefill_pp<128><<<grid, kPThreads, psmem<128>(), (cudaStream_t)stream>>>(mq, mk, mv, a);
+    else
+        k_flash_prefill_pp<64><<<grid, kPThreads, psmem<64>(), (cudaStream_t)stream>>>(mq, mk, mv, a);
     return forge_check_launch("forge_flash_prefill");
 }
 
@@ -467,8 +479,9 @@ extern "C" FORGE_API int forge_flash_prefill(const uint16_t* q, const uint16_t* 
 // cache layer [.. B ..][Hkv][kv_ld][hd] (kv_rows rows in all), GQA heads
 // h -> h / (H / Hkv). Used by the engine's prompt prefill.
 int forge_flash_prefill_kv(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, uint16_t* o, int B, int H,
-                           int Hkv, int S, int kv_ld, int64_t kv_rows, cudaStream_t stream) {
+                           int Hkv, int S, int hd, int kv_ld, int64_t kv_rows, cudaStream_t stream) {
     if (!q || !kc || !vc || !o || B <= 0 || H <= 0 || Hkv <= 0 || H % Hkv || S <= 0 || S % kBM || kv_ld < S ||
+        (hd != 128 && hd != 64) ||
         (int64_t)B * Hkv * kv_ld > kv_rows || kv_rows > (1ll << 31) - 1 || (int64_t)B * H * S > (1ll << 31) - 1)
         return forge_fail(FORGE_INVALID_ARGS, "flash prefill (cache): bad shape");
     if (((uintptr_t)q | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)o) & 15)
@@ -477,10 +490,14 @@ int forge_flash_prefill_kv(const uint16_t* q, const uint16_t* kc, const uint16_t
     uint32_t* err = forge_ops_err_word();
     if (!err) return forge_fail(-1, "flash prefill (cache): no device");
     CUtensorMap mq, mk, mv;
-    if (make_map(&mq, q, (int64_t)B * H * S) || make_map(&mk, kc, kv_rows) || make_map(&mv, vc, kv_rows)) return -1;
-    PrefillArgs a{o, B, H, S, 1, (float)(1.4426950408889634 / 11.313708498984761), err, Hkv, kv_ld};
+    if (make_map(&mq, q, (int64_t)B * H * S, hd) || make_map(&mk, kc, kv_rows, hd) || make_map(&mv, vc, kv_rows, hd))
+        return -1;
+    PrefillArgs a{o, B, H, S, 1, (float)(1.4426950408889634 / std::sqrt((double)hd)), err, Hkv, kv_ld};
     dim3 grid((unsigned)((S / kBM + 1) / 2), (unsigned)H, (unsigned)B);
-    k_flash_prefill_pp<<<grid, kPThreads, kPSmem, stream>>>(mq, mk, mv, a);
+    if (hd == 128)
+        k_flash_prefill_pp<128><<<grid, kPThreads, psmem<128>(), stream>>>(mq, mk, mv, a);
+    else
+        k_flash_prefill_pp<64><<<grid, kPThreads, psmem<64>(), stream>>>(mq, mk, mv, a);
     return forge_check_launch("forge_flash_prefill_kv");
 }
 

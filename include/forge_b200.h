@@ -293,7 +293,7 @@ int forge_sample(const float* logits, int64_t ld, int batch, int vocab, double t
                  double top_p, int64_t* rng_state, float* probs, int32_t* tokens, void* stream);
 
 /* Causal (or full) flash-attention prefill on the tcgen05 tensor cores:
- * q, k, v, o [B][H][S][hd] bf16 device arrays (16-byte aligned), hd = 128,
+ * q, k, v, o [B][H][S][hd] bf16 device arrays (16-byte aligned), hd = 128 or 64,
  * S a multiple of 128; O = softmax(Q K^T / sqrt(hd) + mask) V with fp32
  * accumulation. Asynchronous on `stream`; kernel errors (a wait that ran
  * out) show in forge_ops_check(). */

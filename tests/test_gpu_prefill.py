@@ -1,5 +1,6 @@
 """Flash-attention prefill on the tcgen05 tensor cores against a PyTorch
-fp32 reference of the same op: O = softmax(Q K^T / sqrt(128) + causal mask) V
+fp32 reference of the same op: O = softmax(Q K^T / sqrt(hd) + causal mask) V
+(head dim 128 and 64)
 (nn_attn_core_fwd, stdlib/flame/nn_lib.hexa:221-278), bf16 inputs ~ N(0, 1).
 
 Tolerance: the kernel rounds P to bf16 before P V and O to bf16 on output,
@@ -22,20 +23,23 @@ def _ref(torch, q, k, v, causal):
     return torch.softmax(s, -1) @ vf
 
 
-@pytest.mark.parametrize("B,H,S,causal", [
-    (1, 1, 128, True),
-    (1, 1, 128, False),
-    (1, 2, 256, True),
-    (1, 2, 512, False),
-    (2, 3, 1024, True),
+@pytest.mark.parametrize("B,H,S,causal,hd", [
+    (1, 1, 128, True, 128),
+    (1, 1, 128, False, 128),
+    (1, 2, 256, True, 128),
+    (1, 2, 512, False, 128),
+    (2, 3, 1024, True, 128),
+    (1, 1, 128, True, 64),
+    (1, 2, 384, False, 64),
+    (2, 4, 1024, True, 64),
 ])
-def test_flash_prefill(forge, cuda, B, H, S, causal):
+def test_flash_prefill(forge, cuda, B, H, S, causal, hd):
     import torch
-    g = torch.Generator(device=cuda).manual_seed(B * 100 + H * 10 + S + causal)
-    q, k, v = (torch.randn(B, H, S, 128, generator=g, device=cuda).to(torch.bfloat16) for _ in range(3))
+    g = torch.Generator(device=cuda).manual_seed(B * 100 + H * 10 + S + causal + hd)
+    q, k, v = (torch.randn(B, H, S, hd, generator=g, device=cuda).to(torch.bfloat16) for _ in range(3))
     o = torch.full_like(q, float("nan"))
     torch.cuda.synchronize()
-    forge.check(forge.lib().forge_flash_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S, 128,
+    forge.check(forge.lib().forge_flash_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S, hd,
                                                 int(causal), torch.cuda.current_stream().cuda_stream), "prefill")
     torch.cuda.synchronize()
     forge.check(forge.lib().forge_ops_check(), "prefill error word")

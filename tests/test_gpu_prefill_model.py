@@ -119,6 +119,8 @@ def test_prefill_bf16_activations_close_to_exact(forge, cuda):
 HD128 = {
     "mha_hd128_q4": dict(n_layer=2, d=512, n_head=4, n_kv=4, hd=128, ffn=1024, vocab=2048, q4=True, tied=False),
     "gqa_hd128_bf16": dict(n_layer=2, d=512, n_head=4, n_kv=2, hd=128, ffn=1024, vocab=2048, q4=False, tied=False),
+    # the 1B config's head dim (64) and GQA 4:1, scaled down
+    "gqa_hd64_bf16": dict(n_layer=2, d=512, n_head=8, n_kv=2, hd=64, ffn=1024, vocab=2048, q4=False, tied=False),
 }
 
 
