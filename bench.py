@@ -187,15 +187,15 @@ def time_dominant_gemv(fb, torch, dev, K=4096, N=2 * 11008, copies=4, reps=20, b
     return ms, nbytes
 
 
-def time_prefill(fb, torch, dev, B=8, H=32, S=4096, reps=10):
+def time_prefill(fb, torch, dev, B=8, H=32, S=4096, reps=10, hd=128):
     """Causal flash-attention prefill on the tcgen05 kernel: bf16 Q/K/V
-    ~N(0,1) [B][H][S][128] (805 MB, larger than L2). Algorithmic FLOPs:
-    4 * B * H * S^2 * hd / 2 (causal half)."""
-    q, k, v = (torch.randn(B, H, S, 128, device=dev).to(torch.bfloat16) for _ in range(3))
+    ~N(0,1) [B][H][S][hd] (805 MB at hd 128, larger than L2). Algorithmic
+    FLOPs: 4 * B * H * S^2 * hd / 2 (causal half)."""
+    q, k, v = (torch.randn(B, H, S, hd, device=dev).to(torch.bfloat16) for _ in range(3))
     o = torch.empty_like(q)
     lib = fb.lib()
     stream = torch.cuda.current_stream().cuda_stream
-    run = lambda: lib.forge_flash_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S, 128, 1,
+    run = lambda: lib.forge_flash_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, S, hd, 1,
                                           stream)
     for _ in range(3):
         fb.check(run(), "prefill")
@@ -208,8 +208,8 @@ def time_prefill(fb, torch, dev, B=8, H=32, S=4096, reps=10):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    flops = 4.0 * B * H * S * S * 128 / 2
-    return {"workload": f"flash prefill B{B} H{H} S{S} hd128 causal bf16", "ms": ms, "tflops": flops / ms / 1e9,
+    flops = 4.0 * B * H * S * S * hd / 2
+    return {"workload": f"flash prefill B{B} H{H} S{S} hd{hd} causal bf16", "ms": ms, "tflops": flops / ms / 1e9,
             "peak_tflops": TC_PEAK, "frac": flops / ms / 1e9 / TC_PEAK, "peak_kind": "measured bf16 burst",
             "launches": reps}
 
@@ -592,6 +592,8 @@ def main():
     gemv_ms = max_over_ranks(pg, gemv_ms)
     achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
     prefill = None if (args.no_prefill or world > 1) else time_prefill(fb, torch, dev)
+    if prefill is not None:
+        prefill["hd64"] = time_prefill(fb, torch, dev, hd=64)
     serve = None if (args.no_serve or world > 1) else run_serve(fb, torch, local)
     model_prefill = None if (args.no_prefill or world > 1) else time_model_prefill(fb, torch, local)
     if rank != 0:
