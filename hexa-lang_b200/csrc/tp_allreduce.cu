@@ -56,11 +56,18 @@ __global__ void __launch_bounds__(kThreads) k_tp_allreduce(float* x, int n, cons
     const int sl = blockIdx.x;
     const int per = ((n + kSlices - 1) / kSlices + 3) & ~3;  // whole float4s per slice
     const int s0 = sl * per, s1 = min(n, s0 + per);
+    // Under programmatic dependent launch the next kernel (the next GEMV)
+    // may start now and stream its weights while this exchange runs; this
+    // kernel itself waits for the one that wrote x. The epoch counters are
+    // this kernel's own (the previous all-reduce took its value at its start,
+    // and uses the other buffer generation).
+    pdl_trigger();
     if (threadIdx.x == 0) {
         s_ep = d.epoch[sl] + 1;
         d.epoch[sl] = s_ep;
         s_ok = 1;
     }
+    pdl_wait();
     __syncthreads();
     const uint32_t ep = s_ep;
     const int gen = ep & 1;
@@ -215,7 +222,17 @@ int forge_tp_ar_capacity(const ForgeTpAr* ar) { return ar ? ar->dev.cap : 0; }
 
 int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStream_t stream) {
     if (!ar || n <= 0 || n > ar->dev.cap) return forge_fail(-1, "tp all-reduce: %d floats above capacity", n);
-    k_tp_allreduce<<<kSlices, kThreads, 0, stream>>>(x, n, ar->dev, err);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kSlices);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, k_tp_allreduce, x, n, (const ArDev)ar->dev, err) != cudaSuccess)
+        return forge_fail(-1, "tp all-reduce launch: %s", cudaGetErrorString(cudaGetLastError()));
     return forge_check_launch("tp all-reduce");
 }
 
