@@ -84,6 +84,10 @@ struct ForgeGemvArgs {
     // sums, [K][2 batch] int8 hi/lo in the shared-memory layout of the
     // staging — and is copied instead of staged.
     const uint8_t* pq_in;
+    // With an RMSNorm prologue: pq_in holds the codes of gain * x and pq_ssq
+    // [batch][K/128] the sums of squares of x per group; the GEMV forms the
+    // RMSNorm factor from them and folds it into the group scales.
+    const float* pq_ssq;
 };
 
 // Bytes of a handoff block for K inputs and `batch` sequences.
@@ -226,7 +230,17 @@ const ForgeTpFusedDev* forge_tp_fused_dev(const ForgeTpAr* ar);
 int forge_tp_ar_init(void* comm, int rank, int T, int cap, cudaStream_t stream, ForgeTpAr** out);
 void forge_tp_ar_destroy(ForgeTpAr* ar);
 int forge_tp_ar_capacity(const ForgeTpAr* ar);
-int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStream_t stream);
+// Handoff from the one-shot all-reduce to the next GEMV (batch <= 4, int4):
+// the summed x staged as that GEMV's input block (codes of gain * x, see
+// ForgeGemvArgs::pq_in) plus per (sequence, 128-group) sums of squares of x.
+struct ForgeArHandoff {
+    uint8_t* pq;          // null: no handoff
+    float* ssq;           // [batch][d / 128]
+    const float* gain;    // RMSNorm gain of the next GEMV [d]
+    int batch, d;
+};
+int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStream_t stream,
+                        const ForgeArHandoff* handoff = nullptr);
 
 // Per-device error word of the per-op entries (created on first use).
 uint32_t* forge_ops_err_word();

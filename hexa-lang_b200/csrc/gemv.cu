@@ -232,14 +232,32 @@ __global__ void __maxnreg__(FORGE_GEMV_MAXNREG) k_gemv(const ForgeGemvArgs a) {
     // ---------------------------------------------------------- consumers
     pdl_wait();
     if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4 + 1] = globaltimer_ns();
-    if (WK == FORGE_W_Q4 && PRO == FORGE_PRO_PLAIN && a.pq_in) {
+    if (WK == FORGE_W_Q4 && (PRO == FORGE_PRO_PLAIN || (PRO == FORGE_PRO_RMSNORM && a.pq_ssq)) && a.pq_in) {
         // the previous kernel staged the activations: one copy of its block
         if (threadIdx.x == 0) {
             const uint32_t bytes = (uint32_t)forge_pq_bytes(a.K, a.batch);
             mbar_arrive_expect_tx(pq_bar, bytes);
             bulk_g2s(sxf, a.pq_in, bytes, pq_bar);
         }
-        mbar_wait(pq_bar, 0, a.err);
+        if (PRO == FORGE_PRO_RMSNORM) {
+            // RMSNorm factor of sequence b (warp b) from the groups' sums of
+            // squares, in the same order in every CTA, folded into the
+            // group scales
+            float* invs = red + kRedFloats - 8;
+            const int G = a.K >> 7;
+            if (warp < a.batch) {
+                float tot = 0.f;
+                for (int g = lane; g < G; g += 32) tot += __ldcg(a.pq_ssq + warp * G + g);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+                if (lane == 0) invs[warp] = 1.0f / sqrtf(tot / (float)a.K + a.eps);
+            }
+            mbar_wait(pq_bar, 0, a.err);
+            named_bar_sync(1, 256);
+            for (int i = threadIdx.x; i < G * a.batch; i += 256) sxf[(i / a.batch) * 4 + i % a.batch] *= invs[i % a.batch];
+        } else {
+            mbar_wait(pq_bar, 0, a.err);
+        }
     } else if (WK == FORGE_W_Q4) {
         stage_x_q8<PRO, 256>(a, xq, sxf, ssum, red);
     } else {
@@ -503,6 +521,8 @@ int forge_gemv_launch(const ForgeGemvArgs& a0, cudaStream_t stream, bool pdl) {
     if (max_cols > 8) max_cols = 8;
     const int per_launch = max_cols / cols_per_seq;
     if (per_launch < 1) return forge_fail(-1, "gemv: K=%d too large for the staged activation", a0.K);
+    if (a0.pq_in && (!q4 || a0.batch > 4 || a0.batch > per_launch || (a0.pro == FORGE_PRO_RMSNORM && !a0.pq_ssq)))
+        return forge_fail(-1, "gemv: a staged input block takes int4 weights and 1..4 sequences in one launch");
     const bool batched_ok = q4 ? (a0.epi != FORGE_EPI_LOGITS) : !a0.split;
     // above 4 sequences (int4: more than one launch's worth; bf16: bf16
     // activations, where one CTA per sequence stages in parallel)

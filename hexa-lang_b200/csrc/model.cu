@@ -153,6 +153,11 @@ struct ForgeB200 {
     // block instead of staging (FORGE_PREQUANT=0 turns it off)
     bool prequant = false;
     uint8_t* pq_ctx = nullptr;
+    // The same under tensor parallelism for the GEMVs after each peer-memory
+    // all-reduce (QKV after down, gate/up after O): the all-reduce stages
+    // gain * x and the groups' sums of squares [4][d / 128] for them
+    uint8_t* pq_ar = nullptr;
+    float* pq_ssq = nullptr;
     uint32_t* err = nullptr;
     uint16_t *stA = nullptr, *stB = nullptr;
     uint8_t* codes = nullptr;
@@ -356,9 +361,20 @@ int resid_epi(const ForgeB200* h) { return h->tp_rank == 0 ? FORGE_EPI_RESID : F
 bool tp_oneshot(const ForgeB200* h, int B) {
     return h->ar && B * h->d <= 32768 && B * h->d <= forge_tp_ar_capacity(h->ar);
 }
-int tp_sum(ForgeB200* h, float* x, int B) {
+bool tp_fused(const ForgeB200* h, int B);
+// Whether the peer-memory all-reduce at batch B stages the next GEMV's input.
+bool pq_ar_on(const ForgeB200* h, int B) {
+    return h->prequant && h->comm && B <= 4 && tp_oneshot(h, B) && !tp_fused(h, B);
+}
+// next_gain: the RMSNorm gain of the GEMV that reads x next, when the
+// all-reduce hands it x staged (the decode step's own chain only)
+int tp_sum(ForgeB200* h, float* x, int B, const float* next_gain = nullptr) {
     if (!h->comm) return 0;
-    if (tp_oneshot(h, B)) return forge_tp_ar_sum_f32(h->ar, x, B * h->d, h->err, h->stream);
+    if (tp_oneshot(h, B)) {
+        ForgeArHandoff ho{};
+        if (next_gain && pq_ar_on(h, B)) ho = ForgeArHandoff{h->pq_ar, h->pq_ssq, next_gain, B, h->d};
+        return forge_tp_ar_sum_f32(h->ar, x, B * h->d, h->err, h->stream, &ho);
+    }
     return forge_tp_allreduce_sum_f32(h->comm, x, (size_t)B * h->d, h->stream);
 }
 
@@ -374,14 +390,21 @@ bool tp_fused(const ForgeB200* h, int B) {
     }
     return on && h->ar && B <= 4 && B * h->d <= forge_tp_ar_capacity(h->ar);
 }
-int resid_gemv(ForgeB200* h, ForgeGemvArgs& g, float* x, int B, bool pdl) {
+int resid_gemv(ForgeB200* h, ForgeGemvArgs& g, float* x, int B, bool pdl, const float* next_gain = nullptr) {
     if (tp_fused(h, B)) {
         g.epi = FORGE_EPI_RESID_TP;
         g.tpf = forge_tp_fused_dev(h->ar);
         return forge_gemv_launch(g, h->stream, pdl);
     }
     if (forge_gemv_launch(g, h->stream, pdl)) return -1;
-    return tp_sum(h, x, B);
+    return tp_sum(h, x, B, next_gain);
+}
+// An RMSNorm GEMV reads x as the all-reduce before it staged it.
+void take_ar_handoff(const ForgeB200* h, ForgeGemvArgs& g, int B) {
+    if (pq_ar_on(h, B)) {
+        g.pq_in = h->pq_ar;
+        g.pq_ssq = h->pq_ssq;
+    }
 }
 
 // Next node's slot of the multi-kernel step timeline (or null).
@@ -403,7 +426,10 @@ struct RowMap {
 };
 
 // RMSNorm + QKV + RoPE, K/V appended at each sequence's position.
-int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl, const RowMap* rm = nullptr) {
+// handoff: the decode step's own chain, where the previous layer's down
+// all-reduce staged x.
+int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl, const RowMap* rm = nullptr,
+                bool handoff = false) {
     const LayerDev& Ld = h->layers[l];
     ForgeGemvArgs g = gemv_base(h, B);
     if (rm && rm->exact) g.split = 1;
@@ -417,6 +443,7 @@ int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl, 
         g.pos = rm->pos;
         g.seq_of = rm->seq;
     }
+    if (handoff && !rm && l > 0) take_ar_handoff(h, g, B);
     return forge_gemv_launch(g, h->stream, pdl);
 }
 
@@ -461,11 +488,14 @@ int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool p
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
     g.trace = trace_slot(h);
     if (handoff && !rm && pq_ctx_on(h, B)) g.pq_in = h->pq_ctx;
-    return resid_gemv(h, g, x, B, pdl);
+    return resid_gemv(h, g, x, B, pdl, handoff && !rm ? Ld.g2 : nullptr);
 }
 
 // x += Wd (silu(Wg n) * (Wu n)), n = RMSNorm(x) * g2
-int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl, const RowMap* rm = nullptr, float* s = nullptr) {
+// handoff: the decode step's own chain (gate/up reads x as the O
+// all-reduce staged it; the down all-reduce stages it for the next QKV).
+int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl, const RowMap* rm = nullptr, float* s = nullptr,
+                bool handoff = false) {
     const LayerDev& Ld = h->layers[l];
     const bool exact = rm && rm->exact;
     if (!s) s = h->s;
@@ -475,13 +505,14 @@ int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl, const RowMap* rm
     g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g2; g.eps = h->desc.rms_eps;
     g.epi = FORGE_EPI_SWIGLU; g.s_out = s; g.F = h->F;
     g.trace = trace_slot(h);
+    if (handoff && !rm) take_ar_handoff(h, g, B);
     if (forge_gemv_launch(g, h->stream, pdl)) return -1;
     g = gemv_base(h, B);
     if (exact) g.split = 1;
     g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = s; g.x_stride = h->F;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
     g.trace = trace_slot(h);
-    return resid_gemv(h, g, x, B, pdl);
+    return resid_gemv(h, g, x, B, pdl, handoff && !rm && l + 1 < h->L ? h->layers[l + 1].g1 : nullptr);
 }
 
 // final RMSNorm + LM head into the handle's logits, argmax keys updated
@@ -501,8 +532,10 @@ int enqueue_step(ForgeB200* h, int B) {
     cudaStream_t st = h->stream;
     if (forge_embed_launch(h->emb, h->d, h->Vfull, h->tok, B, h->x, h->err, st, false)) return -1;
     for (int l = 0; l < h->L; ++l) {
-        if (enqueue_qkv(h, l, B, h->x, h->q, true) || enqueue_attn(h, l, B, h->q, h->ctx, true, nullptr, true) ||
-            enqueue_oproj(h, l, B, h->ctx, h->x, true, nullptr, true) || enqueue_mlp(h, l, B, h->x, true))
+        if (enqueue_qkv(h, l, B, h->x, h->q, true, nullptr, true) ||
+            enqueue_attn(h, l, B, h->q, h->ctx, true, nullptr, true) ||
+            enqueue_oproj(h, l, B, h->ctx, h->x, true, nullptr, true) ||
+            enqueue_mlp(h, l, B, h->x, true, nullptr, nullptr, true))
             return -1;
     }
     if (enqueue_head(h, B, h->x, true)) return -1;
@@ -820,7 +853,9 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
         h->prequant = h->q4 && !(e && strcmp(e, "0") == 0);
         if (h->prequant) {
             h->pq_ctx = (uint8_t*)h->alloc((size_t)forge_pq_bytes(h->qd, 4));
-            if (!h->pq_ctx) h->prequant = false;
+            h->pq_ar = (uint8_t*)h->alloc((size_t)forge_pq_bytes(h->d, 4));
+            h->pq_ssq = (float*)h->alloc(sizeof(float) * 4 * (h->d / 128));
+            if (!h->pq_ctx || !h->pq_ar || !h->pq_ssq) h->prequant = false;
         }
     }
     h->bar = (unsigned long long*)h->alloc(16);

@@ -18,6 +18,7 @@
 #include <vector>
 #include "common.cuh"
 #include "forge_internal.h"
+#include "gemv_core.cuh"
 #include "../../include/forge_b200.h"
 
 namespace {
@@ -50,12 +51,21 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
-__global__ void __launch_bounds__(kThreads) k_tp_allreduce(float* x, int n, const ArDev d, uint32_t* err) {
+__global__ void __launch_bounds__(kThreads) k_tp_allreduce(float* x, int n, const ArDev d, uint32_t* err,
+                                                           const ForgeArHandoff ho) {
     __shared__ uint32_t s_ep;
     __shared__ int s_ok;
     const int sl = blockIdx.x;
-    const int per = ((n + kSlices - 1) / kSlices + 3) & ~3;  // whole float4s per slice
-    const int s0 = sl * per, s1 = min(n, s0 + per);
+    int s0, s1;
+    if (ho.pq) {  // slices of whole 128-groups (the handoff quantises groups)
+        const int gps = ((n >> 7) + kSlices - 1) / kSlices;
+        s0 = min(n, sl * gps * 128);
+        s1 = min(n, (sl + 1) * gps * 128);
+    } else {
+        const int per = ((n + kSlices - 1) / kSlices + 3) & ~3;  // whole float4s per slice
+        s0 = sl * per;
+        s1 = min(n, s0 + per);
+    }
     // Under programmatic dependent launch the next kernel (the next GEMV)
     // may start now and stream its weights while this exchange runs; this
     // kernel itself waits for the one that wrote x. The epoch counters are
@@ -107,10 +117,35 @@ __global__ void __launch_bounds__(kThreads) k_tp_allreduce(float* x, int n, cons
     if (!s_ok) return;
     // 4. sum the slots in rank order (the same bits on every rank)
     const float* base = d.peer_buf[d.rank] + (size_t)gen * d.T * d.cap;
-    for (int i = s0 + (int)threadIdx.x; i < s1; i += kThreads) {
-        float acc = base[i];
-        for (int r = 1; r < d.T; ++r) acc += __ldcv(base + (size_t)r * d.cap + i);
-        x[i] = acc;
+    if (!ho.pq) {
+        for (int i = s0 + (int)threadIdx.x; i < s1; i += kThreads) {
+            float acc = base[i];
+            for (int r = 1; r < d.T; ++r) acc += __ldcv(base + (size_t)r * d.cap + i);
+            x[i] = acc;
+        }
+        return;
+    }
+    // 5. with the handoff, one warp per 128-group: the sum, then the next
+    // GEMV's input staged from it — the codes of gain * x (int8 hi/lo,
+    // scale, column sums) and the group's sum of squares of x, from which
+    // that GEMV forms its RMSNorm factor
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = ho.d >> 7;
+    for (int gs = s0 + 128 * warp; gs < s1; gs += 128 * (kThreads / 32)) {
+        const int i = gs + 4 * lane;
+        float4 acc = *reinterpret_cast<const float4*>(base + i);
+        for (int r = 1; r < d.T; ++r) {
+            const float4 v = __ldcv(reinterpret_cast<const float4*>(base + (size_t)r * d.cap + i));
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        *reinterpret_cast<float4*>(x + i) = acc;
+        const int b = gs / ho.d, kk = gs - b * ho.d;
+        const float4 gv = __ldg(reinterpret_cast<const float4*>(ho.gain + kk + 4 * lane));
+        float ss = acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) ho.ssq[b * G + (kk >> 7)] = ss;
+        pq_group_warp(make_float4(gv.x * acc.x, gv.y * acc.y, gv.z * acc.z, gv.w * acc.w), kk >> 7, b,
+                      2 * ho.batch, G, ho.pq);
     }
 }
 }  // namespace
@@ -220,8 +255,14 @@ void forge_tp_ar_destroy(ForgeTpAr* ar) {
 
 int forge_tp_ar_capacity(const ForgeTpAr* ar) { return ar ? ar->dev.cap : 0; }
 
-int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStream_t stream) {
+int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStream_t stream, const ForgeArHandoff* handoff) {
     if (!ar || n <= 0 || n > ar->dev.cap) return forge_fail(-1, "tp all-reduce: %d floats above capacity", n);
+    ForgeArHandoff ho{};
+    if (handoff && handoff->pq) {
+        if (handoff->d % 128 || n != handoff->batch * handoff->d || handoff->batch > 4 || !handoff->ssq || !handoff->gain)
+            return forge_fail(-1, "tp all-reduce: bad handoff shape");
+        ho = *handoff;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kSlices);
     cfg.blockDim = dim3(kThreads);
@@ -231,7 +272,7 @@ int forge_tp_ar_sum_f32(ForgeTpAr* ar, float* x, int n, uint32_t* err, cudaStrea
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, k_tp_allreduce, x, n, (const ArDev)ar->dev, err) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, k_tp_allreduce, x, n, (const ArDev)ar->dev, err, (const ForgeArHandoff)ho) != cudaSuccess)
         return forge_fail(-1, "tp all-reduce launch: %s", cudaGetErrorString(cudaGetLastError()));
     return forge_check_launch("tp all-reduce");
 }
@@ -271,7 +312,7 @@ extern "C" FORGE_API int forge_tp_selftest_absent_peer(int T, int n, unsigned lo
         d.cap = cap;
         d.wait_ns = wait_ns;
         cudaEventRecord(e0);
-        k_tp_allreduce<<<kSlices, kThreads>>>(x, n, d, err);
+        k_tp_allreduce<<<kSlices, kThreads>>>(x, n, d, err, ForgeArHandoff{});
         cudaEventRecord(e1);
         if (cudaEventSynchronize(e1) != cudaSuccess) {
             rc = forge_fail(-1, "forge_tp_selftest_absent_peer: %s", cudaGetErrorString(cudaGetLastError()));
@@ -283,7 +324,7 @@ extern "C" FORGE_API int forge_tp_selftest_absent_peer(int T, int n, unsigned lo
             // the context still runs work: one rank alone needs no flags
             d.T = 1;
             cudaMemset(err, 0, 4);
-            k_tp_allreduce<<<kSlices, kThreads>>>(x, n, d, err);
+            k_tp_allreduce<<<kSlices, kThreads>>>(x, n, d, err, ForgeArHandoff{});
             uint32_t e2 = 0;
             if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&e2, err, 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
                 e2 != 0)
