@@ -30,6 +30,7 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTile = 64;    // keys per shared-memory tile
 constexpr int kStages = 2;   // K+V tiles in flight per CTA
+constexpr int kFastMerge = 16;  // splits merged with all loads in one round trip
 
 template <int HD>
 constexpr int stage_bytes() { return 2 * kTile * HD * 2; }  // K tile + V tile, bf16
@@ -276,54 +277,90 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
     if (!is_last) return;
     __threadfence();
 
-    // ---- merge all splits (log-sum-exp), write the fp32 context. Every
-    // split's (m, l) is loaded at once into shared memory (one L2 round trip
-    // instead of one per split), one thread per head forms the weights and
-    // the normaliser, then every output element sums its splits with all of
-    // its loads issued together. Same operations in the same order as one
-    // thread per element walking the splits.
+    // ---- merge all splits (log-sum-exp), write the fp32 context: per head,
+    // mg = max m_s, w_s = exp(m_s - mg), o = sum_s w_s O_s / sum_s w_s l_s,
+    // both sums in split order.
     float* mw = reinterpret_cast<float*>(smem);  // [G][nsplit] m, then the weight
     float* lw = mw + G * nsplit;                 // [G][nsplit] l
     float* ls = lw + G * nsplit;                 // [G] normaliser
     float* vals = mw + ((2 * G * nsplit + G + 3) & ~3);  // [G][HD] merged context (handoff), 16-byte aligned
-    for (int idx = tid; idx < G * nsplit; idx += kThreads) {
-        const int g = idx / nsplit, s2 = idx % nsplit;
-        const float* pm = a.partial + (((size_t)b * a.H + kvh * G + g) * nsplit + s2) * stride + HD;
-        mw[idx] = __ldcg(pm);
-        lw[idx] = __ldcg(pm + 1);
-    }
-    __syncthreads();
-    if (tid < G) {
-        float mg = -INFINITY;
-        for (int s2 = 0; s2 < nsplit; ++s2) mg = fmaxf(mg, mw[tid * nsplit + s2]);
-        float lsum = 0.f;
-        for (int s2 = 0; s2 < nsplit; ++s2) {
-            const float ms = mw[tid * nsplit + s2];
-            const float w = ms == -INFINITY ? 0.f : expf(ms - mg);
-            mw[tid * nsplit + s2] = w;
-            lsum = fmaf(w, lw[tid * nsplit + s2], lsum);
-        }
-        ls[tid] = lsum;
-    }
-    __syncthreads();
-    for (int idx = tid; idx < G * HD; idx += kThreads) {
-        const int g = idx / HD, e = idx % HD;
-        const int h = kvh * G + g;
-        const float* pb = a.partial + ((size_t)b * a.H + h) * nsplit * stride + e;
-        const float* wg = mw + g * nsplit;
-        float o = 0.f;
-        int s2 = 0;
-        for (; s2 + 8 <= nsplit; s2 += 8) {
-            float v[8];
+    if (nsplit <= kFastMerge) {
+        // every thread loads all splits' (m, l) and partials of its elements
+        // at once (one L2 round trip) and forms its head's weights itself
+        for (int idx = tid; idx < G * HD; idx += kThreads) {
+            const int g = idx / HD, e = idx % HD;
+            const int h = kvh * G + g;
+            const float* pb = a.partial + ((size_t)b * a.H + h) * nsplit * stride;
+            float2 ml[kFastMerge];
+            float v[kFastMerge];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __ldcg(pb + (size_t)(s2 + j) * stride);
+            for (int s2 = 0; s2 < kFastMerge; ++s2) {
+                if (s2 < nsplit) {
+                    ml[s2].x = __ldcg(pb + (size_t)s2 * stride + HD);
+                    ml[s2].y = __ldcg(pb + (size_t)s2 * stride + HD + 1);
+                    v[s2] = __ldcg(pb + (size_t)s2 * stride + e);
+                }
+            }
+            float mg = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) o = fmaf(wg[s2 + j], v[j], o);
+            for (int s2 = 0; s2 < kFastMerge; ++s2)
+                if (s2 < nsplit) mg = fmaxf(mg, ml[s2].x);
+            float lsum = 0.f, o = 0.f;
+#pragma unroll
+            for (int s2 = 0; s2 < kFastMerge; ++s2) {
+                if (s2 < nsplit) {
+                    const float w = ml[s2].x == -INFINITY ? 0.f : expf(ml[s2].x - mg);
+                    lsum = fmaf(w, ml[s2].y, lsum);
+                    o = fmaf(w, v[s2], o);
+                }
+            }
+            const float val = o / lsum;
+            a.out[(size_t)b * a.H * HD + (size_t)h * HD + e] = val;
+            if (HD == 128 && a.pq_out) vals[idx] = val;
         }
-        for (; s2 < nsplit; ++s2) o = fmaf(wg[s2], __ldcg(pb + (size_t)s2 * stride), o);
-        const float val = o / ls[g];
-        a.out[(size_t)b * a.H * HD + (size_t)h * HD + e] = val;
-        if (HD == 128 && a.pq_out) vals[idx] = val;
+    } else {
+        // many splits: every split's (m, l) once into shared memory, one
+        // thread per head forms the weights and the normaliser, then every
+        // output element sums its splits with its loads issued in batches
+        for (int idx = tid; idx < G * nsplit; idx += kThreads) {
+            const int g = idx / nsplit, s2 = idx % nsplit;
+            const float* pm = a.partial + (((size_t)b * a.H + kvh * G + g) * nsplit + s2) * stride + HD;
+            mw[idx] = __ldcg(pm);
+            lw[idx] = __ldcg(pm + 1);
+        }
+        __syncthreads();
+        if (tid < G) {
+            float mg = -INFINITY;
+            for (int s2 = 0; s2 < nsplit; ++s2) mg = fmaxf(mg, mw[tid * nsplit + s2]);
+            float lsum = 0.f;
+            for (int s2 = 0; s2 < nsplit; ++s2) {
+                const float ms = mw[tid * nsplit + s2];
+                const float w = ms == -INFINITY ? 0.f : expf(ms - mg);
+                mw[tid * nsplit + s2] = w;
+                lsum = fmaf(w, lw[tid * nsplit + s2], lsum);
+            }
+            ls[tid] = lsum;
+        }
+        __syncthreads();
+        for (int idx = tid; idx < G * HD; idx += kThreads) {
+            const int g = idx / HD, e = idx % HD;
+            const int h = kvh * G + g;
+            const float* pb = a.partial + ((size_t)b * a.H + h) * nsplit * stride + e;
+            const float* wg = mw + g * nsplit;
+            float o = 0.f;
+            int s2 = 0;
+            for (; s2 + 8 <= nsplit; s2 += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = __ldcg(pb + (size_t)(s2 + j) * stride);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o = fmaf(wg[s2 + j], v[j], o);
+            }
+            for (; s2 < nsplit; ++s2) o = fmaf(wg[s2], __ldcg(pb + (size_t)s2 * stride), o);
+            const float val = o / ls[g];
+            a.out[(size_t)b * a.H * HD + (size_t)h * HD + e] = val;
+            if (HD == 128 && a.pq_out) vals[idx] = val;
+        }
     }
     if (HD == 128 && a.pq_out) {
         // each head's context is one 128-group of the O projection's input:
