@@ -100,6 +100,12 @@ __host__ __device__ inline int64_t forge_pq_bytes(int K, int batch) {
 int forge_gemv_launch(const ForgeGemvArgs& a, cudaStream_t stream, bool pdl);
 int forge_gemv_configure();
 int forge_gemv_launch_count(int K, int batch, bool split, bool q4, bool batched);
+// x [B][x_stride] (K % 128 == 0, B <= 4) staged into an int4 GEMV's input
+// block (layout of ForgeGemvArgs::pq_in), one warp per 128-group; with a
+// gain, the block of an RMSNorm GEMV (codes of gain * x, and the groups'
+// sums of squares of x in ssq [B][K / 128], see ForgeGemvArgs::pq_ssq).
+int forge_stage_groups_launch(const float* x, int x_stride, int K, int B, uint8_t* blk, const float* gain, float* ssq,
+                              cudaStream_t stream, bool pdl);
 // Batched int4 path (gemv_batched.cu): up to forge_gemv_b_max_seq()
 // sequences per weight stream.
 int forge_gemv_b_max_seq();

@@ -488,6 +488,49 @@ int forge_gemv_configure() {
     return rc ? -1 : 0;
 }
 
+namespace {
+// One warp per (128-group, sequence) of x: the group staged in an int4
+// GEMV's input block (ForgeGemvArgs::pq_in), the bytes of stage_x_q8. With
+// a gain (the next GEMV's RMSNorm): the codes of gain * x, and the group's
+// sum of squares of x in ssq [B][K / 128].
+__global__ void __launch_bounds__(128) k_stage_groups(const float* x, int x_stride, int K, int B, uint8_t* blk,
+                                                      const float* gain, float* ssq) {
+    pdl_trigger();
+    pdl_wait();
+    const int G = K >> 7, lane = threadIdx.x & 31;
+    const int item = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (item >= G * B) return;
+    const int g = item % G, b = item / G;
+    float4 v = __ldcg(reinterpret_cast<const float4*>(x + (size_t)b * x_stride + g * 128) + lane);
+    if (gain) {
+        float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) ssq[b * G + g] = ss;
+        const float4 gv = __ldg(reinterpret_cast<const float4*>(gain + g * 128) + lane);
+        v = make_float4(gv.x * v.x, gv.y * v.y, gv.z * v.z, gv.w * v.w);
+    }
+    pq_group_warp(v, g, b, 2 * B, G, blk);
+}
+}  // namespace
+
+int forge_stage_groups_launch(const float* x, int x_stride, int K, int B, uint8_t* blk, const float* gain, float* ssq,
+                              cudaStream_t stream, bool pdl) {
+    if (!x || !blk || K <= 0 || (K % 128) || (x_stride % 4) || B <= 0 || B > 4 || (gain && !ssq))
+        return forge_fail(-1, "stage groups: bad shape K=%d B=%d", K, B);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((K / 128 * B + 3) / 4));
+    cfg.blockDim = dim3(128);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_stage_groups, x, x_stride, K, B, blk, gain, ssq);
+    return e == cudaSuccess ? 0 : forge_fail(-1, "stage groups launch: %s", cudaGetErrorString(e));
+}
+
 // Number of launches forge_gemv_launch issues for one call (int4 with a
 // batched scratch: two per forge_gemv_b_max_seq() sequences).
 int forge_gemv_launch_count(int K, int batch, bool split, bool q4, bool batched) {

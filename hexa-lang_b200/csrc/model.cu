@@ -147,16 +147,26 @@ struct ForgeB200 {
     uint32_t* counters = nullptr;
     int nsplit = 1;
     bool flat_attn = false;  // small batches on attn_flat.cu (FORGE_ATTN=flat)
-    // Staged-context handoff for batch <= 4 (int4 weights, head dim 128; a
-    // rank's own heads under tensor parallelism): the flash-decode merge
-    // stages each head's context for the O projection, which copies the
-    // block instead of staging (FORGE_PREQUANT=0 turns it off)
+    // Staged-input handoffs of the decode step for batch <= 4 (int4
+    // weights; FORGE_PREQUANT=0 turns them all off): the GEMV copies its
+    // input block (int8 hi/lo groups, scales, column sums) instead of
+    // staging it.
+    // - context: the flash-decode merge stages each head's context for the O
+    //   projection (head dim 128; a rank's own heads under tensor parallelism)
     bool prequant = false;
     uint8_t* pq_ctx = nullptr;
-    // The same under tensor parallelism for the GEMVs after each peer-memory
-    // all-reduce (QKV after down, gate/up after O): the all-reduce stages
-    // gain * x and the groups' sums of squares [4][d / 128] for them
-    uint8_t* pq_ar = nullptr;
+    // - s: a small kernel stages the SwiGLU output for the down projection
+    //   (FORGE_PREQUANT_S=0 turns it off); same bytes as the staging
+    bool pq_s_on = false;
+    uint8_t* pq_s = nullptr;
+    // - x: the residual stream for the next RMSNorm GEMV (QKV after down,
+    //   gate/up after O) as codes of gain * x plus the groups' sums of squares
+    //   [4][d / 128], from which the GEMV forms its RMSNorm factor; written by
+    //   the peer-memory all-reduce under tensor parallelism, else by the small
+    //   kernel (FORGE_PREQUANT_NORM=0 turns it off; logits within the last
+    //   bits of the staging's)
+    bool pq_norm = false;
+    uint8_t* pq_x = nullptr;
     float* pq_ssq = nullptr;
     uint32_t* err = nullptr;
     uint16_t *stA = nullptr, *stB = nullptr;
@@ -363,16 +373,18 @@ bool tp_oneshot(const ForgeB200* h, int B) {
 }
 bool tp_fused(const ForgeB200* h, int B);
 // Whether the peer-memory all-reduce at batch B stages the next GEMV's input.
-bool pq_ar_on(const ForgeB200* h, int B) {
-    return h->prequant && h->comm && B <= 4 && tp_oneshot(h, B) && !tp_fused(h, B);
+bool pq_x_on(const ForgeB200* h, int B) {
+    return h->pq_norm && B <= 4 && forge_gemv_launch_count(h->d, B, h->split_for(B), true, false) == 1;
 }
+// whether the peer-memory all-reduce writes the x block
+bool pq_by_ar(const ForgeB200* h, int B) { return h->comm && tp_oneshot(h, B) && !tp_fused(h, B); }
 // next_gain: the RMSNorm gain of the GEMV that reads x next, when the
 // all-reduce hands it x staged (the decode step's own chain only)
 int tp_sum(ForgeB200* h, float* x, int B, const float* next_gain = nullptr) {
     if (!h->comm) return 0;
     if (tp_oneshot(h, B)) {
         ForgeArHandoff ho{};
-        if (next_gain && pq_ar_on(h, B)) ho = ForgeArHandoff{h->pq_ar, h->pq_ssq, next_gain, B, h->d};
+        if (next_gain && pq_x_on(h, B)) ho = ForgeArHandoff{h->pq_x, h->pq_ssq, next_gain, B, h->d};
         return forge_tp_ar_sum_f32(h->ar, x, B * h->d, h->err, h->stream, &ho);
     }
     return forge_tp_allreduce_sum_f32(h->comm, x, (size_t)B * h->d, h->stream);
@@ -394,15 +406,18 @@ int resid_gemv(ForgeB200* h, ForgeGemvArgs& g, float* x, int B, bool pdl, const 
     if (tp_fused(h, B)) {
         g.epi = FORGE_EPI_RESID_TP;
         g.tpf = forge_tp_fused_dev(h->ar);
-        return forge_gemv_launch(g, h->stream, pdl);
+        if (forge_gemv_launch(g, h->stream, pdl)) return -1;
+    } else {
+        if (forge_gemv_launch(g, h->stream, pdl) || tp_sum(h, x, B, next_gain)) return -1;
     }
-    if (forge_gemv_launch(g, h->stream, pdl)) return -1;
-    return tp_sum(h, x, B, next_gain);
+    if (next_gain && pq_x_on(h, B) && !pq_by_ar(h, B))
+        return forge_stage_groups_launch(x, h->d, h->d, B, h->pq_x, next_gain, h->pq_ssq, h->stream, pdl);
+    return 0;
 }
-// An RMSNorm GEMV reads x as the all-reduce before it staged it.
-void take_ar_handoff(const ForgeB200* h, ForgeGemvArgs& g, int B) {
-    if (pq_ar_on(h, B)) {
-        g.pq_in = h->pq_ar;
+// An RMSNorm GEMV reads x as staged after the kernel that wrote it.
+void take_x_handoff(const ForgeB200* h, ForgeGemvArgs& g, int B) {
+    if (pq_x_on(h, B)) {
+        g.pq_in = h->pq_x;
         g.pq_ssq = h->pq_ssq;
     }
 }
@@ -443,7 +458,7 @@ int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl, 
         g.pos = rm->pos;
         g.seq_of = rm->seq;
     }
-    if (handoff && !rm && l > 0) take_ar_handoff(h, g, B);
+    if (handoff && !rm && l > 0) take_x_handoff(h, g, B);
     return forge_gemv_launch(g, h->stream, pdl);
 }
 
@@ -505,12 +520,16 @@ int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl, const RowMap* rm
     g.pro = FORGE_PRO_RMSNORM; g.gain = Ld.g2; g.eps = h->desc.rms_eps;
     g.epi = FORGE_EPI_SWIGLU; g.s_out = s; g.F = h->F;
     g.trace = trace_slot(h);
-    if (handoff && !rm) take_ar_handoff(h, g, B);
+    if (handoff && !rm) take_x_handoff(h, g, B);
     if (forge_gemv_launch(g, h->stream, pdl)) return -1;
     g = gemv_base(h, B);
     if (exact) g.split = 1;
     g.w = Ld.dn_w; g.s = Ld.dn_s; g.N = h->d; g.K = h->F; g.x = s; g.x_stride = h->F;
     g.pro = FORGE_PRO_PLAIN; g.epi = resid_epi(h); g.y = x; g.y_stride = h->d;
+    if (handoff && !rm && h->pq_s_on && B <= 4 && forge_gemv_launch_count(h->F, B, g.split, true, false) == 1) {
+        if (forge_stage_groups_launch(s, h->F, h->F, B, h->pq_s, nullptr, nullptr, h->stream, pdl)) return -1;
+        g.pq_in = h->pq_s;
+    }
     g.trace = trace_slot(h);
     return resid_gemv(h, g, x, B, pdl, handoff && !rm && l + 1 < h->L ? h->layers[l + 1].g1 : nullptr);
 }
@@ -853,9 +872,18 @@ int create_impl(const ForgeModelDesc* desc, int device, const void* nccl_id, For
         h->prequant = h->q4 && !(e && strcmp(e, "0") == 0);
         if (h->prequant) {
             h->pq_ctx = (uint8_t*)h->alloc((size_t)forge_pq_bytes(h->qd, 4));
-            h->pq_ar = (uint8_t*)h->alloc((size_t)forge_pq_bytes(h->d, 4));
-            h->pq_ssq = (float*)h->alloc(sizeof(float) * 4 * (h->d / 128));
-            if (!h->pq_ctx || !h->pq_ar || !h->pq_ssq) h->prequant = false;
+            if (!h->pq_ctx) h->prequant = false;
+            const char* es = getenv("FORGE_PREQUANT_S");
+            if (h->prequant && !(es && strcmp(es, "0") == 0) && h->F % 128 == 0) {
+                h->pq_s = (uint8_t*)h->alloc((size_t)forge_pq_bytes(h->F, 4));
+                h->pq_s_on = h->pq_s != nullptr;
+            }
+            const char* en = getenv("FORGE_PREQUANT_NORM");
+            if (h->prequant && !(en && strcmp(en, "0") == 0)) {
+                h->pq_x = (uint8_t*)h->alloc((size_t)forge_pq_bytes(h->d, 4));
+                h->pq_ssq = (float*)h->alloc(sizeof(float) * 4 * (h->d / 128));
+                h->pq_norm = h->pq_x && h->pq_ssq;
+            }
         }
     }
     h->bar = (unsigned long long*)h->alloc(16);
@@ -1521,7 +1549,11 @@ FORGE_API int forge_b200_launches_per_step(ForgeB200* h, int batch) {
     auto launches = [&](int K) { return forge_gemv_launch_count(K, batch, split, h->q4, h->bscratch != nullptr); };
     int per_layer = launches(h->d) * 2 + launches(h->qd) + launches(h->F) + 1;
     if (h->comm && !tp_fused(h, batch) && tp_oneshot(h, batch)) per_layer += 2;  // the peer-memory all-reduces
-    return 1 + h->L * per_layer + forge_gemv_launch_count(h->d, batch, split, false, h->bscratch != nullptr) + 1;
+    if (h->pq_s_on && batch <= 4 && forge_gemv_launch_count(h->F, batch, split, true, false) == 1)
+        per_layer += 1;  // the staging of s
+    const int norm_stages = pq_x_on(h, batch) && !pq_by_ar(h, batch) ? 2 * h->L - 1 : 0;  // x staged after O / down
+    return 1 + h->L * per_layer + norm_stages + forge_gemv_launch_count(h->d, batch, split, false, h->bscratch != nullptr) +
+           1;
 }
 int64_t forge_b200_width(const ForgeB200* h, int which) {
     if (!h) return 0;

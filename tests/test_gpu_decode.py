@@ -141,26 +141,51 @@ def test_fused_and_graph_paths_agree(forge, oracle, cuda, name, monkeypatch):
     assert np.abs(outs[0] - outs[1]).max() < 2e-3
 
 
-@pytest.mark.parametrize("batch", [1, 2, 4])
-def test_context_handoff_bit_identical(forge, oracle, cuda, batch, monkeypatch):
-    """int4, head dim 128, up to 4 sequences: the flash-decode merge hands
-    each head's context to the O projection already staged (int8 hi/lo
-    groups, scales, column sums), which copies it instead of staging. The
-    bytes equal the staging's, so logits and tokens are bit-identical with
-    the handoff off (FORGE_PREQUANT=0, read at handle creation)."""
+def _handoff_runs(oracle, forge, batch, monkeypatch, settings):
     cfg = CONFIGS["mha_q4"]
     monkeypatch.setenv("FORGE_DECODE_PATH", "graph")
     runs = []
-    for pq in ("1", "0"):
-        monkeypatch.setenv("FORGE_PREQUANT", pq)
+    for env in settings:
+        for k, v in env.items():
+            monkeypatch.setenv(k, v)
         _, fm = _models(oracle, forge, cfg, batch, 64)
         fm.init_synthetic(1234, 0.02)
         fm.fill_kv_synthetic(5, 20, 0.5)
         toks = np.arange(batch, dtype=np.int32) * 37 + 3
-        lgs = []
+        lgs, tks = [], []
         for _ in range(6):
             toks, lg = fm.step(toks, want_logits=True)
             lgs.append(lg)
+            tks.append(toks.copy())
         fm.close()
-        runs.append(np.stack(lgs))
-    assert np.array_equal(runs[0], runs[1])
+        runs.append((np.stack(lgs), np.stack(tks)))
+    return runs
+
+
+@pytest.mark.parametrize("batch", [1, 2, 4])
+def test_context_handoff_bit_identical(forge, oracle, cuda, batch, monkeypatch):
+    """int4, head dim 128, up to 4 sequences: the flash-decode merge hands
+    each head's context to the O projection already staged (int8 hi/lo
+    groups, scales, column sums), and a small kernel stages the SwiGLU output
+    for the down projection; both GEMVs copy the block instead of staging.
+    The bytes equal the staging's, so logits and tokens are bit-identical
+    with the handoffs off (FORGE_PREQUANT=0, read at handle creation). The
+    residual-stream handoff, which is not bit-identical, is off in both."""
+    runs = _handoff_runs(oracle, forge, batch, monkeypatch,
+                         [dict(FORGE_PREQUANT="1", FORGE_PREQUANT_NORM="0"), dict(FORGE_PREQUANT="0")])
+    assert np.array_equal(runs[0][0], runs[1][0])
+
+
+@pytest.mark.parametrize("batch", [1, 2, 4])
+def test_residual_handoff_close_to_staging(forge, oracle, cuda, batch, monkeypatch):
+    """The residual stream staged for the next RMSNorm GEMV (QKV after down,
+    gate/up after O) as codes of gain * x plus per-group sums of squares, the
+    GEMV folding its RMSNorm factor into the group scales: same tokens as
+    the GEMVs staging x themselves, logits within 2e-3 of the logit scale
+    (the reordered RMSNorm sum moves QKV outputs in the last bits, which can
+    round a cached K/V value one bf16 step apart)."""
+    on, off = _handoff_runs(oracle, forge, batch, monkeypatch,
+                            [dict(FORGE_PREQUANT="1", FORGE_PREQUANT_NORM="1"), dict(FORGE_PREQUANT="0")])
+    assert np.array_equal(on[1], off[1])
+    scale = np.abs(off[0]).max()
+    assert np.abs(on[0] - off[0]).max() <= 2e-3 * scale, np.abs(on[0] - off[0]).max() / scale
