@@ -57,6 +57,9 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
     const int sp = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int nsplit = gridDim.x;
+    const int lin = sp + nsplit * (kvh + gridDim.y * b);
+    unsigned long long* trace = (a.trace && lin < a.trace_ctas) ? a.trace + (size_t)lin * 4 : nullptr;
+    if (trace && tid == 0) trace[0] = globaltimer_ns();
 
     // Positions only change between steps, so the split range and every
     // cached row below P can be fetched before the dependency wait; row P
@@ -123,6 +126,7 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
         for (int i = 0; i < kStages && i < ntiles; ++i) issue(i);
     pdl_trigger();
     pdl_wait();
+    if (trace && tid == 0) trace[1] = globaltimer_ns();
     if (bad) {  // no copies were issued
         if (tid == 0) atomicOr(a.err, FORGE_DEVERR_BAD_INDEX);
         return;
@@ -268,6 +272,7 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
     }
     __threadfence();
     __syncthreads();
+    if (trace && tid == 0) trace[2] = globaltimer_ns();
     __shared__ int is_last;
     if (tid == 0) {
         const uint32_t old = atomicAdd(a.counters + (size_t)b * a.Hkv + kvh, 1u);
@@ -372,6 +377,7 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
         }
     }
     if (tid == 0) a.counters[(size_t)b * a.Hkv + kvh] = 0u;
+    if (trace && tid == 0) trace[3] = globaltimer_ns();
 }
 
 template <int HD, int G>

@@ -145,9 +145,12 @@ struct ForgeAttnArgs {
     // Flat kernel (attn_flat.cu): partial slots per (b, kv head); partial is
     // [B][Hkv][flat_slots][H/Hkv][hd + 2].
     int32_t flat_slots;
-    // Optional timeline [grid][4] (start, dependency released, first query
-    // loaded, done), flat kernel only, FORGE_GRAPH_TRACE only.
+    // Optional timeline (FORGE_GRAPH_TRACE only), [CTA][4] %globaltimer
+    // stamps. Flat kernel: start, dependency released, first query loaded,
+    // done. Split kernel, for the first trace_ctas CTAs (x fastest): start,
+    // dependency released, partial written, merge done (merging CTA only).
     unsigned long long* trace;
+    int32_t trace_ctas;
     // Prompt prefill (split kernel, contiguous cache): query row b attends
     // to rows 0..pos[b] of cache sequence seq_of[b] (null: sequence b).
     const int32_t* seq_of;

@@ -477,6 +477,7 @@ int enqueue_attn(ForgeB200* h, int l, int B, const float* q, float* ctx, bool pd
     at.B = B; at.H = h->H; at.Hkv = h->Hkv; at.hd = h->hd; at.lmax = h->lmax;
     at.partial = h->partial; at.counters = h->counters; at.out = ctx; at.err = h->err;
     at.trace = trace_slot(h);
+    at.trace_ctas = forge_sm_count();
     if (rm) {
         // every cached row of a prompt row was written by this pass's QKV
         // kernel: no copies before the dependency, so no programmatic launch
