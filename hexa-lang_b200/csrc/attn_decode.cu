@@ -270,17 +270,20 @@ __global__ void __launch_bounds__(kThreads) k_flash_decode(const ForgeAttnArgs a
         pm[0] = n > 0 ? st_m[tid] : -INFINITY;
         pm[1] = n > 0 ? st_l[tid] : 0.f;
     }
-    __threadfence();
+    // ticket: the block barrier orders every thread's partial stores before
+    // thread 0's release; the last CTA's acquire orders its loads after all
+    // the other CTAs' stores (the barrier hands the acquire to every thread)
     __syncthreads();
     if (trace && tid == 0) trace[2] = globaltimer_ns();
     __shared__ int is_last;
     if (tid == 0) {
-        const uint32_t old = atomicAdd(a.counters + (size_t)b * a.Hkv + kvh, 1u);
+        uint32_t old;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
+                     : "=r"(old) : "l"(a.counters + (size_t)b * a.Hkv + kvh) : "memory");
         is_last = (old == (uint32_t)(nsplit - 1));
     }
     __syncthreads();
     if (!is_last) return;
-    __threadfence();
 
     // ---- merge all splits (log-sum-exp), write the fp32 context: per head,
     // mg = max m_s, w_s = exp(m_s - mg), o = sum_s w_s O_s / sum_s w_s l_s,
