@@ -419,20 +419,25 @@ __global__ void __maxnreg__(128) k_gemv_tc(const __grid_constant__ CUtensorMap t
                     } else if (lane == 0) {
                         s_fail = 1;
                     }
-                    __threadfence();
+                    // ticket: the barrier orders the epilogue threads' partial
+                    // stores before one acquire-release atomic; the last
+                    // arrival's acquire reaches every epilogue thread through
+                    // the second barrier
                     named_bar_sync(1, kEpiThreads);
                     if (threadIdx.x == kWarpEpi * 32) {
                         int last = 0;
                         if (!s_fail) {
                             const int n = g - piece_g0 + 1;
-                            last = (atomicAdd(t.ticket + tl, n) + n == G2) ? 1 : 0;
+                            uint32_t old;
+                            asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;"
+                                         : "=r"(old) : "l"(t.ticket + tl), "r"((uint32_t)n) : "memory");
+                            last = ((int)old + n == G2) ? 1 : 0;
                         }
                         s_last = last;
                     }
                     named_bar_sync(1, kEpiThreads);
                     fin = s_last != 0;
                     if (fin) {
-                        __threadfence();
                         // the tile's pieces in CTA order
                         const int c0 = unit_owner((int64_t)tl * G2, U, P);
                         const int c1 = unit_owner((int64_t)tl * G2 + G2 - 1, U, P);
