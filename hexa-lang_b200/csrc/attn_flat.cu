@@ -93,7 +93,8 @@ __global__ void __maxnreg__(72) k_attn_flat(const ForgeAttnArgs a) {
     int* spos = tcount + kMaxB;                                     // [B] position P
     uint64_t* full = reinterpret_cast<uint64_t*>(spos + kMaxB);
     uint64_t* empty = full + S;
-    volatile int* flags = reinterpret_cast<volatile int*>(empty + S);  // [0] abort, [1] last CTA of a pair
+    // [0] abort, [1] last CTA of a pair, [2] tiles the producer has issued
+    volatile int* flags = reinterpret_cast<volatile int*>(empty + S);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int B = a.B;
@@ -116,6 +117,7 @@ __global__ void __maxnreg__(72) k_attn_flat(const ForgeAttnArgs a) {
         tstart[B] = acc;
         flags[0] = 0;
         flags[1] = 0;
+        flags[2] = 0;
         if (bad && blockIdx.x == 0) atomicOr(a.err, FORGE_DEVERR_BAD_INDEX);
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -144,6 +146,8 @@ __global__ void __maxnreg__(72) k_attn_flat(const ForgeAttnArgs a) {
                 const int r0 = j * TK;
                 const int rows = min(r0 + TK, spos[b]) - r0;  // row P is read after the dependency wait
                 uint8_t* dst = ring + (size_t)s * kTileBytes;
+                __threadfence_block();
+                flags[2] = (int)(it + 1);  // slot s's previous tile has been released
                 if (rows > 0) {
                     const uint32_t bytes = (uint32_t)rows * HD * 2;
                     const size_t base = (((size_t)b * a.Hkv + kvh) * a.lmax + r0) * HD;
@@ -196,6 +200,22 @@ __global__ void __maxnreg__(72) k_attn_flat(const ForgeAttnArgs a) {
         for (long long u = t; u < seg_end; ++u, ++it) {
             if ((int)(it % kCW) != warp) continue;
             const int s = it % S;
+            // With fewer ring slots than warps (S = 6), a warp can reach tile
+            // `it` before the producer has refilled slot s for tile it - S;
+            // the slot's phase parity would then read as already complete.
+            // Wait (bounded) until tile `it` has been issued: from then on
+            // the slot's phase is that of tile it or the one after.
+            if (S != kCW && !flags[0] && flags[2] <= (int)it) {
+                const uint64_t t0 = globaltimer_ns();
+                uint32_t spins = 0;
+                while (flags[2] <= (int)it && !flags[0]) {
+                    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > FORGE_WAIT_NS) {
+                        if (lane == 0) atomicOr(a.err, FORGE_DEVERR_MBAR_TIMEOUT);
+                        flags[0] = 1;
+                    }
+                }
+                __threadfence_block();
+            }
             if (!flags[0] && !mbar_wait(&full[s], (it / S) & 1u, a.err)) flags[0] = 1;
             if (!flags[0]) {
                 const int r0 = (j0 + (int)(u - t)) * TK;

@@ -19,6 +19,11 @@ CASES = [
     (4, 8, 2, 128, 2048, [100, 31, 32, 1999]),             # GQA 4:1, hd 128, tile edges
     (8, 32, 32, 128, 600, [0, 1, 31, 32, 63, 64, 511, 599]),
     (2, 16, 2, 64, 700, [63, 64]),                         # GQA 8:1
+    # several tiles per CTA with a 6-slot ring (4 or more query heads per KV
+    # head): warps run ahead of the ring's refills
+    (8, 32, 8, 64, 1500, [1400, 1450, 1499, 1300, 1472, 1024, 1408, 1399]),  # 1B bs8
+    (8, 16, 2, 64, 4200, [4100, 4000, 4199, 3000, 4150, 4096, 2047, 4111]),  # GQA 8:1
+    (4, 8, 2, 128, 4100, [4000, 4095, 3333, 4096]),       # GQA 4:1, hd 128
 ]
 
 
