@@ -372,7 +372,8 @@ bool tp_oneshot(const ForgeB200* h, int B) {
     return h->ar && B * h->d <= 32768 && B * h->d <= forge_tp_ar_capacity(h->ar);
 }
 bool tp_fused(const ForgeB200* h, int B);
-// Whether the peer-memory all-reduce at batch B stages the next GEMV's input.
+// Whether the decode step at batch B hands the residual stream x staged to
+// the next RMSNorm GEMV (written by the all-reduce or the staging kernel).
 bool pq_x_on(const ForgeB200* h, int B) {
     return h->pq_norm && B <= 4 && forge_gemv_launch_count(h->d, B, h->split_for(B), true, false) == 1;
 }
@@ -441,8 +442,8 @@ struct RowMap {
 };
 
 // RMSNorm + QKV + RoPE, K/V appended at each sequence's position.
-// handoff: the decode step's own chain, where the previous layer's down
-// all-reduce staged x.
+// handoff: the decode step's own chain, where x was staged after the
+// previous layer's down projection.
 int enqueue_qkv(ForgeB200* h, int l, int B, const float* x, float* q, bool pdl, const RowMap* rm = nullptr,
                 bool handoff = false) {
     const LayerDev& Ld = h->layers[l];
@@ -508,8 +509,9 @@ int enqueue_oproj(ForgeB200* h, int l, int B, const float* ctx, float* x, bool p
 }
 
 // x += Wd (silu(Wg n) * (Wu n)), n = RMSNorm(x) * g2
-// handoff: the decode step's own chain (gate/up reads x as the O
-// all-reduce staged it; the down all-reduce stages it for the next QKV).
+// handoff: the decode step's own chain (gate/up reads x as staged after the
+// O projection; s is staged for the down projection; x is staged after it
+// for the next layer's QKV).
 int enqueue_mlp(ForgeB200* h, int l, int B, float* x, bool pdl, const RowMap* rm = nullptr, float* s = nullptr,
                 bool handoff = false) {
     const LayerDev& Ld = h->layers[l];
