@@ -19,10 +19,14 @@
 //                      drains.
 //   warps 0-7          stage the activations once per CTA (RMSNorm in the same
 //                      pass; int4: int8 hi/lo pairs per 128-group, bf16: hi/lo
-//                      bf16), then for every piece take A fragments straight
-//                      from the packed weights (int4: two LOP3 per register
-//                      into mma.sync.m16n8k32 u8 x s8; bf16: mma.sync.m16n8k16)
-//                      with the activations as B operand.
+//                      bf16) — or, for int4 when the kernel before has staged
+//                      them into a block (ForgeGemvArgs::pq_in), copy that
+//                      block with one bulk copy, folding the RMSNorm factor
+//                      into the group scales — then for every piece take A
+//                      fragments straight from the packed weights (int4: two
+//                      LOP3 per register into mma.sync.m16n8k32 u8 x s8;
+//                      bf16: mma.sync.m16n8k16) with the activations as B
+//                      operand.
 //   The eight warps split each piece along K (two 128-groups per warp for
 //   int4); a shared-memory reduction and the fused epilogue finish each unit.
 // Why mma.sync: at batch 1-4 the GEMV has 1-8 columns; a tcgen05 MMA needs

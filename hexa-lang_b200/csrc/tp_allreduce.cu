@@ -9,7 +9,11 @@
 // (source rank, slice) on every peer, waits for the peers' flags in its own
 // memory, then sums the slots in rank order, so every rank ends with the same
 // bits. Two buffer generations alternate, so a rank that runs ahead writes
-// into the generation its peers finished reading.
+// into the generation its peers finished reading. With a handoff
+// (ForgeArHandoff, int4, up to 4 sequences) the slices are whole 128-groups
+// and each summed group is also staged for the RMSNorm GEMV that reads x
+// next: the codes of gain * x in that GEMV's input-block layout, and the
+// group's sum of squares of x.
 //
 // Every wait is bounded (%globaltimer; 2 s, or FORGE_WAIT_NS at set-up): on
 // expiry the kernel sets the handle's error word and returns.
